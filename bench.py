@@ -1,0 +1,345 @@
+"""Benchmark of the quantized mat-vec hot path (Q4_K x Q8_K at FFN shapes).
+
+One step = the two FFN projections of one decode token (M=1): x[1,4096] . W_up^T (W 14336x4096)
+and h[1,14336] . W_down^T (W 4096x14336), each the full mul_mat op (activation quantized to Q8_K
+on the fly, then the Q4_K GEMV).  Weights come from an 8-slot ring of distinct seeded copies
+(528 MB >> 126 MB L2) so every step streams its weights from HBM.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  value = weight GB/s of the whole job; e2e = the same metric
+through the host-pointer C ABI (dcg_ctx_mul_mat: H2D of x, both kernels, D2H of y, per call).
+--impl reference times the CPU implementation of the same op (the oracle restatement of ggml's
+vec_dot / quantize_row_q8_K, all host threads) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "quant mat-vec weight GB/s (Q4_K x Q8_K FFN GEMV, M=1)"
+UNIT = "GB/s"
+SHAPES = ((14336, 4096), (4096, 14336))  # (n, k) of W_up and W_down
+RING = 8
+Q4_K, Q8_K = 12, 15
+
+
+def q4k_bytes(n, k):
+    return n * (k // 256) * 144
+
+
+WEIGHT_BYTES = sum(q4k_bytes(n, k) for n, k in SHAPES)
+# algorithmic bytes of one GEMV launch: weights + Q8_K activation (qs + d + bsums) + f32 output
+ALG_BYTES = sum(q4k_bytes(n, k) + k + (k // 256) * 4 + (k // 16) * 2 + n * 4 for n, k in SHAPES)
+
+
+def read_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def read_traffic():
+    """dram bytes per GEMV launch pair from the committed ncu summary, if present."""
+    p = os.path.join(ROOT, "profiles", "gemv_q4_K_ffn_m1.txt")
+    try:
+        for line in open(p):
+            if line.startswith("traffic_bytes_per_step:"):
+                return int(float(line.split(":", 1)[1]))
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, fl in rows for i, v in enumerate(fl) if v == "Active"})
+        top = max(r[0] for r in rows)
+        loaded = [r[0] for r in rows if r[0] >= 0.5 * top] or [r[0] for r in rows]
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": rows[0][1], "reasons": reasons,
+                "samples": len(rows)}
+
+
+def cpu_reference(budget_s: float):
+    """The oracle's row-sliced mul_mat (ggml vec_dot_q4_K_q8_K restated) plus quantize_row_q8_K
+    on all host threads, on the same shapes; repeats whole steps until ~budget_s elapsed."""
+    import numpy as np
+
+    from oracle import oracle as O
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(1)
+    mats = []
+    for n, k in SHAPES:
+        w = (rng.standard_normal((n, k), dtype=np.float32) * 0.02).astype(np.float32)
+        mats.append((O.quantize(w, O.Q4_K), k, rng.standard_normal((1, k)).astype(np.float32)))
+    steps = 0
+    t0 = time.perf_counter()
+    while True:
+        for wq, k, x in mats:
+            xq = O.quantize(x, O.Q8_K)
+            O.mul_mat(O.Q4_K, wq, k, xq, 1, nthreads=threads)
+        steps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return {"value": WEIGHT_BYTES * steps / el / 1e9, "unit": UNIT, "cores": threads,
+            "kind": "port", "steps": steps, "seconds": el,
+            "sample": f"{steps} full steps (both FFN matmuls, M=1) of config 2 on {threads} "
+                      f"host threads, oracle restatement of ggml vec_dot_q4_K_q8_K"}
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from densecore_b200 import ops
+
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    # ---- resident data: RING slots x (W_up, W_down), GPU-encoded from seeded N(0, 0.02) ----
+    gen = torch.Generator(device=dev)
+    ring = []
+    for s in range(RING):
+        pair = []
+        for n, k in SHAPES:
+            gen.manual_seed(1 + 1000 * s + n)
+            w = torch.randn((n, k), generator=gen, device=dev) * 0.02
+            pair.append(ops.QuantWeight.from_float(w, Q4_K))
+            del w
+        ring.append(pair)
+    xs = [torch.randn((1, k), generator=gen, device=dev) for _, k in SHAPES]
+    ys = [torch.empty((1, n), device=dev) for n, _ in SHAPES]
+    scr = [torch.empty(ops.mul_mat_scratch_size(Q4_K, 1, k), dtype=torch.uint8, device=dev)
+           for _, k in SHAPES]
+    acts = [ops.quantize_act(x, Q8_K) for x in xs]
+    torch.cuda.synchronize()
+
+    def ring_pass():          # RING steps, each = 2 x (quantize + GEMV)
+        for s in range(RING):
+            for j in range(2):
+                ops.mul_mat(ring[s][j], xs[j], out=ys[j], scratch=scr[j])
+
+    def gemv_pass():          # the GEMV kernels alone, same weights
+        for s in range(RING):
+            for j in range(2):
+                ops.mul_mat_q(ring[s][j], acts[j], 1, out=ys[j])
+
+    # CUDA graphs: one ring pass per replay (launch overhead off the timed path)
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        ring_pass()
+        gemv_pass()
+    torch.cuda.current_stream().wait_stream(side)
+    g_step, g_gemv = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_step):
+        ring_pass()
+    with torch.cuda.graph(g_gemv):
+        gemv_pass()
+
+    reps = max(1, (args.steps + RING - 1) // RING)
+    steps = reps * RING
+    for _ in range(max(1, (args.warmup + RING - 1) // RING)):
+        g_step.replay()
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            g_step.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if ws > 1:
+        dist.barrier()
+
+    # kernel-only timing of the GEMV (the dominant kernel)
+    for _ in range(3):
+        g_gemv.replay()
+    torch.cuda.synchronize()
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k0.record()
+    for _ in range(reps):
+        g_gemv.replay()
+    k1.record()
+    torch.cuda.synchronize()
+    gemv_ms_per_step = k0.elapsed_time(k1) / steps
+
+    # e2e through the host-pointer ABI (weights registered once; x / y cross PCIe every call)
+    ctx = ops.HostContext(local)
+    hw = [[ctx.register(ring[s][j].to_ggml().cpu().numpy(), Q4_K, SHAPES[j][1]) for j in range(2)]
+          for s in range(RING)]
+    hx = [x.cpu().numpy() for x in xs]
+    e2e_steps = min(steps, 2048)
+    for s in range(RING):
+        for j in range(2):
+            ctx.mul_mat(hw[s][j], hx[j])
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        s = i % RING
+        for j in range(2):
+            ctx.mul_mat(hw[s][j], hx[j])
+    e2e_s = time.perf_counter() - t0
+    ctx.close()
+
+    # max over ranks
+    vals = torch.tensor([ms, gemv_ms_per_step, e2e_s], device=dev, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms, gemv_ms_per_step, e2e_s = vals.tolist()
+
+    if rank == 0:
+        peak, peak_kind = read_peak()
+        achieved = ALG_BYTES / (gemv_ms_per_step * 1e-3) / 1e9
+        traffic = read_traffic()
+        out = {
+            "metric": METRIC, "value": round(ws * WEIGHT_BYTES * steps / (ms * 1e-3) / 1e9, 2),
+            "unit": UNIT, "n_gpus": ws, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / steps, 6), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded N(0,0.02) weights)",
+            "config": {"workload": "config 2: Q4_K x Q8_K mul_mat, W_up 14336x4096 + W_down "
+                                   "4096x14336, M=1, activation quantized per call",
+                       "weight_bytes_per_step": WEIGHT_BYTES,
+                       "l2": f"{RING}-slot weight ring, {RING * WEIGHT_BYTES / 1e6:.0f} MB > L2",
+                       "parallelism": f"replicas x{ws}", "cuda_graph": True},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_source": f"{peak_kind} hbm_gbs",
+                         "traffic": traffic, "kernel": "gemv_kernel<Q4_K,1,4>",
+                         "alg_bytes_per_step": ALG_BYTES,
+                         "kernel_us_per_step": round(gemv_ms_per_step * 1e3, 3)},
+            "e2e": {"value": round(ws * WEIGHT_BYTES * e2e_steps / e2e_s / 1e9, 2), "unit": UNIT,
+                    "h2d_bytes_per_step": sum(4 * k for _, k in SHAPES),
+                    "d2h_bytes_per_step": sum(4 * n for n, _ in SHAPES),
+                    "steps": e2e_steps, "api": "dcg_ctx_mul_mat (host pointers)"},
+            "gpu_launches": 4 * steps,
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_reference(args.cpu_seconds)
+        print(json.dumps(out), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    del np
+
+
+def run_reference(args):
+    ws, rank, _ = _dist()
+    if rank != 0:
+        return
+    per_step = []
+    total = 0.0
+    for _ in range(args.warmup):
+        cpu_reference(0.0)
+    for _ in range(args.steps):
+        r = cpu_reference(args.ref_step_seconds)
+        per_step.append(r)
+        total += r["seconds"]
+    n_steps = sum(r["steps"] for r in per_step)
+    value = WEIGHT_BYTES * n_steps / total / 1e9
+    cb = dict(per_step[-1])
+    cb["value"] = round(value, 4)
+    cb["sample"] = (f"{args.steps} timed samples of >= {args.ref_step_seconds}s, {n_steps} full steps "
+                    f"of config 2 (both FFN matmuls, M=1) on {cb['cores']} host threads; ggml is "
+                    "absent, so this is the oracle restatement of vec_dot_q4_K_q8_K")
+    out = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
+           "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": round(total / n_steps * 1e3, 3), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+           "config": {"workload": "config 2: Q4_K x Q8_K mul_mat, W_up 14336x4096 + W_down "
+                                  "4096x14336, M=1", "weight_bytes_per_step": WEIGHT_BYTES},
+           "cpu_baseline": cb,
+           "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-step-seconds", type=float, default=2.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        # bounded: each timed step is a ~2 s sample of the CPU workload
+        args.steps = min(args.steps, 20)
+        args.warmup = min(args.warmup, 1)
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

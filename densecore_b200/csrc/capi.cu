@@ -1,0 +1,197 @@
+// capi.cu -- the extern "C" boundary of libdcgpu.so (declarations and citations: include/dcgpu.h).
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <cstdio>
+#include <cstring>
+
+#include "../../include/dcgpu.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+int cuda_fail(cudaError_t e, const char* where) {
+    g_last_error = std::string(where) + ": " + cudaGetErrorString(e);
+    return DCG_ECUDA;
+}
+#define DCG_CUDA(call, where)                              \
+    do {                                                   \
+        cudaError_t _e = (call);                           \
+        if (_e != cudaSuccess) return cuda_fail(_e, where); \
+    } while (0)
+
+bool weight_type_ok(int t) {
+    return t == DCG_TYPE_Q8_0 || t == DCG_TYPE_Q4_K || t == DCG_TYPE_Q6_K;
+}
+int check_shape(int type, int64_t n, int64_t k) {
+    if (!weight_type_ok(type)) return fail(DCG_EINVAL, "unsupported weight type " + std::to_string(type));
+    if (n < 0 || k <= 0) return fail(DCG_EINVAL, "bad shape");
+    const int64_t blk = type == DCG_TYPE_Q8_0 ? QK8_0 : QK_K;
+    if (k % blk) return fail(DCG_EINVAL, "k=" + std::to_string(k) + " is not a multiple of the block size " + std::to_string(blk));
+    return DCG_OK;
+}
+int act_type_of(int wtype) { return wtype == DCG_TYPE_Q8_0 ? DCG_TYPE_Q8_0 : DCG_TYPE_Q8_K; }
+bool aligned(const void* p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+}  // namespace
+
+namespace dcg_internal {
+void set_error(const std::string& m) { g_last_error = m; }
+}  // namespace dcg_internal
+
+// ------------------------------------------------------------------------------------------
+// internal: enqueue quantize + GEMV chunks (no checks beyond shapes; scratch already sized)
+// ------------------------------------------------------------------------------------------
+static int enqueue_mul_mat(int type, const void* w, int64_t n, int64_t k, const float* x,
+                           int64_t m, float* y, void* scratch, cudaStream_t st) {
+    DCG_CUDA(dcg::launch_quantize_act(act_type_of(type), x, scratch, m, k, true, st), "quantize");
+    for (int64_t m0 = 0; m0 < m; m0 += 8) {
+        const int64_t mc = (m - m0) < 8 ? (m - m0) : 8;
+        DCG_CUDA(dcg::launch_gemv(type, w, n, k, scratch, m, m0, mc, y, st), "gemv");
+    }
+    return DCG_OK;
+}
+
+extern "C" {
+
+int dcg_version(void) { return 100; }
+
+const char* dcg_strerror(int code) {
+    switch (code) {
+        case DCG_OK: return "ok";
+        case DCG_EINVAL: return "invalid argument";
+        case DCG_ECUDA: return "CUDA error";
+        case DCG_ENOMEM: return "out of device memory";
+        case DCG_ESCRATCH: return "scratch buffer too small";
+        case DCG_ENOTFOUND: return "not registered";
+    }
+    return "unknown error";
+}
+
+const char* dcg_last_error(void) { return g_last_error.c_str(); }
+
+size_t dcg_row_size(int type, int64_t k) {
+    switch (type) {
+        case DCG_TYPE_Q8_0: return (size_t)(k / QK8_0) * Q8_0_BYTES;
+        case DCG_TYPE_Q4_K: return (size_t)(k / QK_K) * Q4_K_BYTES;
+        case DCG_TYPE_Q6_K: return (size_t)(k / QK_K) * Q6_K_BYTES;
+        case DCG_TYPE_Q8_K: return (size_t)(k / QK_K) * Q8_K_BYTES;
+        case DCG_TYPE_F16: return (size_t)k * 2;
+        case DCG_TYPE_F32: return (size_t)k * 4;
+    }
+    return 0;
+}
+
+size_t dcg_packed_weight_size(int type, int64_t n, int64_t k) {
+    if (!weight_type_ok(type)) return 0;
+    return dcg::packed_weight_bytes(type, n, k);
+}
+
+size_t dcg_mul_mat_scratch_size(int type, int64_t m, int64_t k) {
+    if (!weight_type_ok(type)) return 0;
+    return dcg::act_bytes(act_type_of(type), m, k);
+}
+
+static int quantize_rows(int act_type, const float* x, void* y, int64_t m, int64_t k, void* stream) {
+    const int64_t blk = act_type == DCG_TYPE_Q8_0 ? QK8_0 : QK_K;
+    if (!x || !y) return fail(DCG_EINVAL, "null pointer");
+    if (m < 0 || k <= 0 || k % blk) return fail(DCG_EINVAL, "k must be a positive multiple of the block size");
+    if (!aligned(x, 16)) return fail(DCG_EINVAL, "x must be 16-byte aligned");
+    if (act_type == DCG_TYPE_Q8_K && !aligned(y, 4)) return fail(DCG_EINVAL, "y must be 4-byte aligned");
+    if (act_type == DCG_TYPE_Q8_0 && !aligned(y, 2)) return fail(DCG_EINVAL, "y must be 2-byte aligned");
+    DCG_CUDA(dcg::launch_quantize_act(act_type, x, y, m, k, false, (cudaStream_t)stream), "quantize");
+    return DCG_OK;
+}
+
+int dcg_quantize_row_q8_0(const float* x, void* y, int64_t m, int64_t k, void* stream) {
+    return quantize_rows(DCG_TYPE_Q8_0, x, y, m, k, stream);
+}
+int dcg_quantize_row_q8_K(const float* x, void* y, int64_t m, int64_t k, void* stream) {
+    return quantize_rows(DCG_TYPE_Q8_K, x, y, m, k, stream);
+}
+
+int dcg_quantize_weights(int type, const float* x, void* rows, int64_t n, int64_t k, void* stream) {
+    int rc = check_shape(type, n, k);
+    if (rc) return rc;
+    if (!x || !rows) return fail(DCG_EINVAL, "null pointer");
+    if (!aligned(x, 16) || !aligned(rows, 4)) return fail(DCG_EINVAL, "misaligned buffer");
+    DCG_CUDA(dcg::launch_encode_weights(type, x, rows, n, k, (cudaStream_t)stream), "encode");
+    return DCG_OK;
+}
+
+int dcg_weight_pack(int type, const void* rows, size_t row_stride, int64_t n, int64_t k,
+                    void* packed, void* stream) {
+    int rc = check_shape(type, n, k);
+    if (rc) return rc;
+    if (!rows || !packed) return fail(DCG_EINVAL, "null pointer");
+    if (row_stride < dcg_row_size(type, k)) return fail(DCG_EINVAL, "row_stride smaller than a row");
+    if (!aligned(packed, 256)) return fail(DCG_EINVAL, "packed buffer must be 256-byte aligned");
+    DCG_CUDA(dcg::launch_pack(type, rows, row_stride, packed, n, k, false, (cudaStream_t)stream), "pack");
+    return DCG_OK;
+}
+
+int dcg_weight_unpack(int type, const void* packed, int64_t n, int64_t k, void* rows,
+                      size_t row_stride, void* stream) {
+    int rc = check_shape(type, n, k);
+    if (rc) return rc;
+    if (!rows || !packed) return fail(DCG_EINVAL, "null pointer");
+    if (row_stride < dcg_row_size(type, k)) return fail(DCG_EINVAL, "row_stride smaller than a row");
+    DCG_CUDA(dcg::launch_pack(type, rows, row_stride, const_cast<void*>(packed), n, k, true,
+                              (cudaStream_t)stream), "unpack");
+    return DCG_OK;
+}
+
+int dcg_mul_mat(int type, const void* w, int64_t n, int64_t k, const float* x, int64_t m, float* y,
+                void* scratch, size_t scratch_bytes, void* stream) {
+    int rc = check_shape(type, n, k);
+    if (rc) return rc;
+    if (m < 0) return fail(DCG_EINVAL, "m < 0");
+    if (m == 0 || n == 0) return DCG_OK;
+    if (!w || !x || !y || !scratch) return fail(DCG_EINVAL, "null pointer");
+    if (!aligned(w, 256) || !aligned(scratch, 256)) return fail(DCG_EINVAL, "w and scratch must be 256-byte aligned");
+    if (!aligned(x, 16) || !aligned(y, 4)) return fail(DCG_EINVAL, "x must be 16-byte aligned, y 4-byte aligned");
+    const size_t need = dcg_mul_mat_scratch_size(type, m, k);
+    if (scratch_bytes < need)
+        return fail(DCG_ESCRATCH, "scratch needs " + std::to_string(need) + " bytes, got " + std::to_string(scratch_bytes));
+    return enqueue_mul_mat(type, w, n, k, x, m, y, scratch, (cudaStream_t)stream);
+}
+
+size_t dcg_act_size(int act_type, int64_t m, int64_t k) {
+    if (act_type != DCG_TYPE_Q8_0 && act_type != DCG_TYPE_Q8_K) return 0;
+    return dcg::act_bytes(act_type, m, k);
+}
+
+int dcg_quantize_act(int act_type, const float* x, void* act, int64_t m, int64_t k, void* stream) {
+    if (act_type != DCG_TYPE_Q8_0 && act_type != DCG_TYPE_Q8_K)
+        return fail(DCG_EINVAL, "act_type must be Q8_0 or Q8_K");
+    const int64_t blk = act_type == DCG_TYPE_Q8_0 ? QK8_0 : QK_K;
+    if (!x || !act) return fail(DCG_EINVAL, "null pointer");
+    if (m < 0 || k <= 0 || k % blk) return fail(DCG_EINVAL, "k must be a positive multiple of the block size");
+    if (!aligned(x, 16) || !aligned(act, 256)) return fail(DCG_EINVAL, "x must be 16-byte and act 256-byte aligned");
+    DCG_CUDA(dcg::launch_quantize_act(act_type, x, act, m, k, true, (cudaStream_t)stream), "quantize");
+    return DCG_OK;
+}
+
+int dcg_mul_mat_q(int type, const void* w, int64_t n, int64_t k, const void* act, int64_t m,
+                  float* y, void* stream) {
+    int rc = check_shape(type, n, k);
+    if (rc) return rc;
+    if (m < 0) return fail(DCG_EINVAL, "m < 0");
+    if (m == 0 || n == 0) return DCG_OK;
+    if (!w || !act || !y) return fail(DCG_EINVAL, "null pointer");
+    if (!aligned(w, 256) || !aligned(act, 256) || !aligned(y, 4)) return fail(DCG_EINVAL, "misaligned buffer");
+    for (int64_t m0 = 0; m0 < m; m0 += 8) {
+        const int64_t mc = (m - m0) < 8 ? (m - m0) : 8;
+        DCG_CUDA(dcg::launch_gemv(type, w, n, k, act, m, m0, mc, y, (cudaStream_t)stream), "gemv");
+    }
+    return DCG_OK;
+}
+
+}  // extern "C"

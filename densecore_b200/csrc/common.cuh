@@ -1,0 +1,128 @@
+// common.cuh -- shared definitions for the dcgpu sm_100a kernels.
+//
+// Block formats are ggml's (GGUF): Q8_0 (32 x int8 + fp16 d, 34 B), Q4_K (256: fp16 d, fp16 dmin,
+// 12 B packed 6-bit scales/mins, 128 B nibbles; 144 B), Q6_K (256: 128 B low nibbles, 64 B high
+// 2-bit planes, 16 int8 scales, fp16 d; 210 B), Q8_K (256: f32 d, 256 int8, 16 int16 bsums; 292 B).
+//
+// Device ("packed") weight layout, written once at upload by dcg_weight_pack:
+//   Q4_K : unchanged ggml rows (a 144-B block is nine 16-B vectors).
+//   Q8_0 : payload [n][k] int8 (row = k bytes), then fp16 d [n][k/32].
+//   Q6_K : payload [n][k/256][208 B = ql|qh|scales], then fp16 d [n][k/256].
+// Device activation layout (written by the quantize kernels for mul_mat):
+//   Q8_0 act : qs [m][k] int8, then fp16 d [m][k/32].
+//   Q8_K act : qs [m][k] int8, then f32 d [m][k/256], then int16 bsums [m][k/16].
+// Every region starts on a 256-B boundary so every payload load is an aligned 16-B vector.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define DCG_TYPE_F32 0
+#define DCG_TYPE_F16 1
+#define DCG_TYPE_Q8_0 8
+#define DCG_TYPE_Q4_K 12
+#define DCG_TYPE_Q6_K 14
+#define DCG_TYPE_Q8_K 15
+
+#define QK8_0 32
+#define QK_K 256
+#define Q8_0_BYTES 34
+#define Q4_K_BYTES 144
+#define Q6_K_BYTES 210
+#define Q6_K_PAYLOAD 208
+#define Q8_K_BYTES 292
+
+namespace dcg {
+
+__host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// ---- packed weight layout ----
+struct PackedW {
+    const uint8_t* payload;  // row-major payload
+    const __half* d;         // per-block fp16 scales (Q8_0, Q6_K); null for Q4_K
+    size_t row_bytes;        // payload bytes per row
+    int nb;                  // blocks per row (32-blocks for Q8_0, 256-blocks for K-quants)
+};
+
+__host__ __device__ inline size_t packed_payload_row_bytes(int type, int64_t k) {
+    switch (type) {
+        case DCG_TYPE_Q8_0: return (size_t)k;
+        case DCG_TYPE_Q4_K: return (size_t)(k / QK_K) * Q4_K_BYTES;
+        case DCG_TYPE_Q6_K: return (size_t)(k / QK_K) * Q6_K_PAYLOAD;
+    }
+    return 0;
+}
+__host__ __device__ inline int blocks_per_row(int type, int64_t k) {
+    return type == DCG_TYPE_Q8_0 ? (int)(k / QK8_0) : (int)(k / QK_K);
+}
+__host__ __device__ inline size_t packed_weight_bytes(int type, int64_t n, int64_t k) {
+    size_t p = align256(packed_payload_row_bytes(type, k) * (size_t)n);
+    if (type == DCG_TYPE_Q4_K) return p;
+    return p + align256((size_t)n * blocks_per_row(type, k) * 2);
+}
+__host__ __device__ inline PackedW packed_view(int type, const void* base, int64_t n, int64_t k) {
+    PackedW w;
+    w.payload = (const uint8_t*)base;
+    w.row_bytes = packed_payload_row_bytes(type, k);
+    w.nb = blocks_per_row(type, k);
+    w.d = type == DCG_TYPE_Q4_K ? nullptr
+                                : (const __half*)(w.payload + align256(w.row_bytes * (size_t)n));
+    return w;
+}
+
+// ---- activation layout ----
+struct ActQ {
+    int8_t* qs;      // [m][k]
+    void* d;         // fp16 [m][k/32] (Q8_0) or f32 [m][k/256] (Q8_K)
+    int16_t* bsums;  // [m][k/16] (Q8_K only)
+};
+__host__ __device__ inline size_t act_bytes(int act_type, int64_t m, int64_t k) {
+    size_t q = align256((size_t)m * k);
+    if (act_type == DCG_TYPE_Q8_0) return q + align256((size_t)m * (k / QK8_0) * 2);
+    return q + align256((size_t)m * (k / QK_K) * 4) + align256((size_t)m * (k / 16) * 2);
+}
+__host__ __device__ inline ActQ act_view(int act_type, void* base, int64_t m, int64_t k) {
+    ActQ a;
+    uint8_t* p = (uint8_t*)base;
+    a.qs = (int8_t*)p;
+    p += align256((size_t)m * k);
+    a.d = p;
+    if (act_type == DCG_TYPE_Q8_0) {
+        a.bsums = nullptr;
+    } else {
+        p += align256((size_t)m * (k / QK_K) * 4);
+        a.bsums = (int16_t*)p;
+    }
+    return a;
+}
+
+// ---- loads ----
+// Streaming 16-B weight load: read-only path, no L1 allocation, 256-B L2 prefetch.
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
+    uint4 r;
+    asm("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+// Activation load: cached in L1 (every warp of the SM reads the same activation rows).
+__device__ __forceinline__ uint4 ld_act_v4(const void* p) { return __ldg((const uint4*)p); }
+
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+// 6-bit scale/min j (0..7) from the 12-byte Q4_K scale field given as three u32 words
+// (bytes 0-3, 4-7, 8-11); ggml's get_scale_min_k4 bit layout.
+__device__ __forceinline__ void q4k_scale_min(uint32_t s0, uint32_t s1, uint32_t s2, int j, int& sc,
+                                              int& m) {
+    if (j < 4) {
+        sc = (s0 >> (8 * j)) & 63;
+        m = (s1 >> (8 * j)) & 63;
+    } else {
+        const int jj = j - 4;
+        const uint32_t b8 = (s2 >> (8 * jj)) & 0xFF;
+        sc = (b8 & 0xF) | (((s0 >> (8 * jj + 6)) & 3) << 4);
+        m = (b8 >> 4) | (((s1 >> (8 * jj + 6)) & 3) << 4);
+    }
+}
+
+}  // namespace dcg

@@ -1,0 +1,236 @@
+// gemv.cu -- memory-bound quantized mat-vec (M <= 8 activation rows per launch).
+//
+// Replaces the row loop of DenseCore's cb_gemv_custom (core/src/inference.cpp:916-924), which calls
+// ggml vec_dot_{q8_0_q8_0,q4_K_q8_K,q6_K_q8_K} once per output row.  Here every lane streams
+// 16-byte vectors of weight payload (ld.global.nc, no L1 allocation), unpacks them to int8 lanes in
+// registers, takes dp4a int32 dot products per sub-block, applies the integer sub-block scales,
+// and converts to fp32 once per (lane, super-block) with the fp16/f32 block scales.
+//
+// Work mapping (one CTA = 8 warps):
+//   * a "unit" is the span of one row that one warp covers with one 16-B load per lane:
+//       Q8_0: 16 blocks of 32 (512 weights; lane = (block, half-block));
+//       Q4_K / Q6_K: 4 super-blocks of 256 (1024 weights; 8 lanes per super-block).
+//   * warp w owns R consecutive rows and the K-slice ks = w % S (units ks, ks+S, ...);
+//     the S partial sums of a row are combined through shared memory at the end.
+// The activation rows (SoA Q8_0 / Q8_K, common.cuh) are read through L1: every warp of the SM
+// reads the same few KB.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dcg {
+
+template <int TYPE>
+struct UnitInfo;
+template <>
+struct UnitInfo<DCG_TYPE_Q8_0> { static constexpr int BLOCKS = 16; };
+template <>
+struct UnitInfo<DCG_TYPE_Q4_K> { static constexpr int BLOCKS = 4; };
+template <>
+struct UnitInfo<DCG_TYPE_Q6_K> { static constexpr int BLOCKS = 4; };
+
+// weight registers of one (unit, row) for one lane
+struct WReg {
+    uint4 a;  // Q8_0: 16 qs | Q4_K: 16 nibble bytes | Q6_K: ql
+    uint4 b;  // Q4_K: block header (d, dmin, scales) | Q6_K: qh
+    uint4 c;  // Q6_K: scales
+    float d;  // Q8_0 / Q6_K: block scale (fp16 -> f32); Q4_K: d
+    float dmin;
+};
+
+template <int TYPE>
+__device__ __forceinline__ void load_w(const PackedW& w, int64_t row, int blk, int lane, WReg& r) {
+    if (TYPE == DCG_TYPE_Q8_0) {
+        const uint8_t* p = w.payload + row * w.row_bytes + (size_t)blk * QK8_0 + (lane & 1) * 16;
+        r.a = ld_stream_v4(p);
+        r.d = __half2float(w.d[row * w.nb + blk]);
+    } else if (TYPE == DCG_TYPE_Q4_K) {
+        const uint8_t* p = w.payload + row * w.row_bytes + (size_t)blk * Q4_K_BYTES;
+        r.b = ld_stream_v4(p);
+        r.a = ld_stream_v4(p + 16 + (lane & 7) * 16);
+    } else {
+        const int i = lane & 7, h = i >> 2, c = (i >> 1) & 1, half = i & 1;
+        const uint8_t* p = w.payload + row * w.row_bytes + (size_t)blk * Q6_K_PAYLOAD;
+        r.a = ld_stream_v4(p + h * 64 + c * 32 + half * 16);
+        r.b = ld_stream_v4(p + 128 + h * 32 + half * 16);
+        r.c = ld_stream_v4(p + 192);
+        r.d = __half2float(w.d[row * w.nb + blk]);
+    }
+}
+
+__device__ __forceinline__ uint32_t u4(const uint4& v, int t) {
+    return t == 0 ? v.x : (t == 1 ? v.y : (t == 2 ? v.z : v.w));
+}
+
+// one lane's contribution of one (unit, row) against activation row m
+template <int TYPE>
+__device__ __forceinline__ float lane_dot(const WReg& r, const ActQ& a, int64_t k, int nb, int m,
+                                          int blk, int lane) {
+    if (TYPE == DCG_TYPE_Q8_0) {
+        const size_t e0 = (size_t)m * k + (size_t)blk * QK8_0 + (lane & 1) * 16;
+        const uint4 xv = ld_act_v4(a.qs + e0);
+        int s = 0;
+        s = dp4a((int)r.a.x, (int)xv.x, s);
+        s = dp4a((int)r.a.y, (int)xv.y, s);
+        s = dp4a((int)r.a.z, (int)xv.z, s);
+        s = dp4a((int)r.a.w, (int)xv.w, s);
+        const float dx = __half2float(((const __half*)a.d)[(size_t)m * nb + blk]);
+        return __fmul_rn(r.d, dx) * (float)s;
+    } else if (TYPE == DCG_TYPE_Q4_K) {
+        const int i = lane & 7, g = i >> 1, half = i & 1;
+        const int j0 = 2 * g, j1 = 2 * g + 1;
+        const int8_t* xq = a.qs + (size_t)m * k + (size_t)blk * QK_K + j0 * 32 + half * 16;
+        const uint4 xl = ld_act_v4(xq);
+        const uint4 xh = ld_act_v4(xq + 32);
+        int d0 = 0, d1 = 0;
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+            const uint32_t q = u4(r.a, t);
+            d0 = dp4a((int)(q & 0x0F0F0F0Fu), (int)u4(xl, t), d0);
+            d1 = dp4a((int)((q >> 4) & 0x0F0F0F0Fu), (int)u4(xh, t), d1);
+        }
+        int sc0, m0, sc1, m1;
+        q4k_scale_min(r.b.y, r.b.z, r.b.w, j0, sc0, m0);
+        q4k_scale_min(r.b.y, r.b.z, r.b.w, j1, sc1, m1);
+        const int isum = sc0 * d0 + sc1 * d1;
+        const int16_t* bs = a.bsums + (size_t)m * (k / 16) + (size_t)blk * 16;
+        const int msum = m0 * (int)bs[2 * j0 + half] + m1 * (int)bs[2 * j1 + half];
+        const float dx = ((const float*)a.d)[(size_t)m * nb + blk];
+        const __half2 dd = *reinterpret_cast<const __half2*>(&r.b.x);
+        const float dw = __low2float(dd), dmin = __high2float(dd);
+        return dx * (dw * (float)isum - dmin * (float)msum);
+    } else {
+        const int i = lane & 7, h = i >> 2, c = (i >> 1) & 1, half = i & 1;
+        const int s_lo = h * 8 + c * 2 + half, s_hi = s_lo + 4;
+        const int8_t* xq = a.qs + (size_t)m * k + (size_t)blk * QK_K + h * 128 + c * 32 + half * 16;
+        const uint4 xl = ld_act_v4(xq);
+        const uint4 xh = ld_act_v4(xq + 64);
+        int d0 = 0, d1 = 0;
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+            const uint32_t ql = u4(r.a, t), qh = u4(r.b, t);
+            const uint32_t lo = (ql & 0x0F0F0F0Fu) | (((qh >> (2 * c)) & 0x03030303u) << 4);
+            const uint32_t hi = ((ql >> 4) & 0x0F0F0F0Fu) | (((qh >> (2 * c + 4)) & 0x03030303u) << 4);
+            d0 = dp4a((int)__vsub4(lo, 0x20202020u), (int)u4(xl, t), d0);
+            d1 = dp4a((int)__vsub4(hi, 0x20202020u), (int)u4(xh, t), d1);
+        }
+        const int sc_lo = (int)(int8_t)((u4(r.c, s_lo >> 2) >> (8 * (s_lo & 3))) & 0xFF);
+        const int sc_hi = (int)(int8_t)((u4(r.c, s_hi >> 2) >> (8 * (s_hi & 3))) & 0xFF);
+        const int isum = sc_lo * d0 + sc_hi * d1;
+        const float dx = ((const float*)a.d)[(size_t)m * nb + blk];
+        return __fmul_rn(r.d, dx) * (float)isum;
+    }
+}
+
+template <int TYPE, int M, int R>
+__global__ void __launch_bounds__(256) gemv_kernel(PackedW w, int64_t n, int64_t k, ActQ a,
+                                                   int m0, float* __restrict__ y, int S) {
+    constexpr int PER = UnitInfo<TYPE>::BLOCKS;
+    constexpr int U = 2;  // units in flight per warp
+    __shared__ float red[8][R * M];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int rg = wid / S, ks = wid % S;
+    const int rows_per_cta = (8 / S) * R;
+    const int64_t row0 = (int64_t)blockIdx.x * rows_per_cta + (int64_t)rg * R;
+    const int nb = w.nb;
+    const int n_units = (nb + PER - 1) / PER;
+    const int lane_blk = (TYPE == DCG_TYPE_Q8_0) ? (lane >> 1) : (lane >> 3);
+
+    float acc[R][M];
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+        for (int mm = 0; mm < M; mm++) acc[r][mm] = 0.0f;
+
+    for (int u0 = ks; u0 < n_units; u0 += S * U) {
+        WReg wr[U][R];
+        bool ok[U][R];
+#pragma unroll
+        for (int uu = 0; uu < U; uu++) {
+            const int u = u0 + uu * S;
+            const int blk = u * PER + lane_blk;
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                ok[uu][r] = (u < n_units) && (blk < nb) && (row0 + r < n);
+                if (ok[uu][r]) load_w<TYPE>(w, row0 + r, blk, lane, wr[uu][r]);
+            }
+        }
+#pragma unroll
+        for (int uu = 0; uu < U; uu++) {
+            const int blk = (u0 + uu * S) * PER + lane_blk;
+#pragma unroll
+            for (int mm = 0; mm < M; mm++)
+#pragma unroll
+                for (int r = 0; r < R; r++)
+                    if (ok[uu][r]) acc[r][mm] += lane_dot<TYPE>(wr[uu][r], a, k, nb, m0 + mm, blk, lane);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+        for (int mm = 0; mm < M; mm++) {
+            float v = acc[r][mm];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) red[wid][r * M + mm] = v;
+        }
+    __syncthreads();
+    for (int t = threadIdx.x; t < (8 / S) * R * M; t += blockDim.x) {
+        const int g = t / (R * M), rm = t % (R * M);
+        const int r = rm / M, mm = rm % M;
+        const int64_t row = (int64_t)blockIdx.x * rows_per_cta + (int64_t)g * R + r;
+        if (row >= n) continue;
+        float s = 0.0f;
+        for (int q = 0; q < S; q++) s += red[g * S + q][rm];
+        y[(size_t)(m0 + mm) * n + row] = s;
+    }
+}
+
+template <int TYPE, int M>
+static cudaError_t launch_gemv_t(const PackedW& w, int64_t n, int64_t k, const ActQ& a, int m0,
+                                 float* y, cudaStream_t st) {
+    constexpr int R = (M <= 2) ? 4 : 2;
+    constexpr int PER = UnitInfo<TYPE>::BLOCKS;
+    const int n_units = (w.nb + PER - 1) / PER;
+    // smallest K-split that still gives >= 4 CTAs per SM, keeping >= 2 units per warp
+    int S = 1;
+    while (S < 8) {
+        const int64_t ctas = (n + (8 / S) * R - 1) / ((8 / S) * R);
+        if (ctas >= 4 * 148 || n_units < 4 * S) break;
+        S *= 2;
+    }
+    const int64_t ctas = (n + (8 / S) * R - 1) / ((8 / S) * R);
+    gemv_kernel<TYPE, M, R><<<(unsigned)ctas, 256, 0, st>>>(w, n, k, a, m0, y, S);
+    return cudaGetLastError();
+}
+
+template <int TYPE>
+static cudaError_t dispatch_m(const PackedW& w, int64_t n, int64_t k, const ActQ& a, int m0, int m,
+                              float* y, cudaStream_t st) {
+    switch (m) {
+        case 1: return launch_gemv_t<TYPE, 1>(w, n, k, a, m0, y, st);
+        case 2: return launch_gemv_t<TYPE, 2>(w, n, k, a, m0, y, st);
+        case 3: return launch_gemv_t<TYPE, 3>(w, n, k, a, m0, y, st);
+        case 4: return launch_gemv_t<TYPE, 4>(w, n, k, a, m0, y, st);
+        case 5: return launch_gemv_t<TYPE, 5>(w, n, k, a, m0, y, st);
+        case 6: return launch_gemv_t<TYPE, 6>(w, n, k, a, m0, y, st);
+        case 7: return launch_gemv_t<TYPE, 7>(w, n, k, a, m0, y, st);
+        case 8: return launch_gemv_t<TYPE, 8>(w, n, k, a, m0, y, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gemv(int type, const void* packed_w, int64_t n, int64_t k, const void* act,
+                        int64_t act_m, int64_t m0, int64_t m, float* y, cudaStream_t st) {
+    if (m < 1 || m > 8) return cudaErrorInvalidValue;
+    const PackedW w = packed_view(type, packed_w, n, k);
+    const int act_type = type == DCG_TYPE_Q8_0 ? DCG_TYPE_Q8_0 : DCG_TYPE_Q8_K;
+    const ActQ a = act_view(act_type, const_cast<void*>(act), act_m, k);
+    switch (type) {
+        case DCG_TYPE_Q8_0: return dispatch_m<DCG_TYPE_Q8_0>(w, n, k, a, (int)m0, (int)m, y, st);
+        case DCG_TYPE_Q4_K: return dispatch_m<DCG_TYPE_Q4_K>(w, n, k, a, (int)m0, (int)m, y, st);
+        case DCG_TYPE_Q6_K: return dispatch_m<DCG_TYPE_Q6_K>(w, n, k, a, (int)m0, (int)m, y, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace dcg

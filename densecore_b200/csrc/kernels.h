@@ -1,0 +1,20 @@
+// kernels.h -- internal launchers shared between the .cu files and the C-ABI layer.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dcg {
+
+cudaError_t launch_quantize_act(int act_type, const float* x, void* y, int64_t m, int64_t k,
+                                bool soa, cudaStream_t st);
+cudaError_t launch_encode_weights(int type, const float* x, void* y, int64_t n, int64_t k,
+                                  cudaStream_t st);
+cudaError_t launch_pack(int type, const void* src, size_t src_stride, void* dst, int64_t n,
+                        int64_t k, bool unpack, cudaStream_t st);
+
+// y[m][n] = W[n] . act[m]; act in the SoA activation layout; m <= 8 per launch.
+cudaError_t launch_gemv(int type, const void* packed_w, int64_t n, int64_t k, const void* act,
+                        int64_t act_m, int64_t m0, int64_t m, float* y, cudaStream_t st);
+
+
+}  // namespace dcg

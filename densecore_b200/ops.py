@@ -1,0 +1,189 @@
+"""Torch-facing operators over libdcgpu.so.  torch only provides device memory and the current
+stream; all arithmetic runs in the sm_100a kernels.  Names follow the reference operator surface:
+
+  quantize_row_q8_0 / quantize_row_q8_K  ggml from_float (core/src/inference.cpp:887-894)
+  mul_mat                                 smart_mul_mat / cb_gemv_custom / ggml_mul_mat on a
+                                          quantized weight (inference.cpp:1043-1064, :840-948)
+  QuantWeight                             a weight tensor resident on the device (the
+                                          weight_tensor->data of cb_gemv_custom, uploaded once)
+  HostContext                             the synchronous host-pointer boundary (dcg_ctx_*)
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _lib
+from .ggml_types import Q4_K, Q6_K, Q8_0, Q8_K, VEC_DOT_TYPE, block_size, row_size
+
+
+def _stream(stream=None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _ptr(t: torch.Tensor) -> int:
+    return t.data_ptr()
+
+
+def _check_cuda(t: torch.Tensor, name: str, dtype=None):
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if dtype is not None and t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+
+
+def _quantize_rows(fn: str, qtype: int, x: torch.Tensor, out: torch.Tensor | None):
+    _check_cuda(x, "x", torch.float32)
+    k = x.shape[-1]
+    m = x.numel() // k
+    if out is None:
+        out = torch.empty((m, row_size(qtype, k)), dtype=torch.uint8, device=x.device)
+    _lib.check(getattr(_lib.load(), fn)(_ptr(x), _ptr(out), m, k, _stream()), fn)
+    return out
+
+
+def quantize_row_q8_0(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """f32 [..., k] -> ggml Q8_0 rows (uint8 [m, k/32*34])."""
+    return _quantize_rows("dcg_quantize_row_q8_0", Q8_0, x, out)
+
+
+def quantize_row_q8_K(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """f32 [..., k] -> ggml Q8_K rows (uint8 [m, k/256*292])."""
+    return _quantize_rows("dcg_quantize_row_q8_K", Q8_K, x, out)
+
+
+def quantize_weights(x: torch.Tensor, qtype: int) -> torch.Tensor:
+    """Encode an f32 [n, k] weight as ggml Q8_0 / Q4_K / Q6_K rows on the device."""
+    _check_cuda(x, "x", torch.float32)
+    n, k = x.shape
+    out = torch.empty((n, row_size(qtype, k)), dtype=torch.uint8, device=x.device)
+    _lib.check(_lib.load().dcg_quantize_weights(qtype, _ptr(x), _ptr(out), n, k, _stream()),
+               "dcg_quantize_weights")
+    return out
+
+
+class QuantWeight:
+    """An n x k quantized weight in the device layout the matmul streams (dcg_weight_pack)."""
+
+    def __init__(self, qtype: int, n: int, k: int, packed: torch.Tensor):
+        self.qtype, self.n, self.k, self.packed = qtype, n, k, packed
+
+    @classmethod
+    def from_ggml(cls, rows: torch.Tensor, qtype: int, k: int) -> "QuantWeight":
+        """rows: uint8 [n, >=row_size] ggml rows on the device (tensor nb[1] = rows.stride(0))."""
+        _check_cuda(rows, "rows", torch.uint8)
+        n = rows.shape[0]
+        L = _lib.load()
+        nbytes = L.dcg_packed_weight_size(qtype, n, k)
+        if nbytes == 0:
+            raise ValueError(f"unsupported weight type {qtype}")
+        packed = torch.empty(nbytes, dtype=torch.uint8, device=rows.device)
+        _lib.check(L.dcg_weight_pack(qtype, _ptr(rows), rows.stride(0), n, k, _ptr(packed),
+                                     _stream()), "dcg_weight_pack")
+        return cls(qtype, n, k, packed)
+
+    @classmethod
+    def from_float(cls, w: torch.Tensor, qtype: int) -> "QuantWeight":
+        return cls.from_ggml(quantize_weights(w, qtype), qtype, w.shape[1])
+
+    def to_ggml(self) -> torch.Tensor:
+        rows = torch.empty((self.n, row_size(self.qtype, self.k)), dtype=torch.uint8,
+                           device=self.packed.device)
+        _lib.check(_lib.load().dcg_weight_unpack(self.qtype, _ptr(self.packed), self.n, self.k,
+                                                 _ptr(rows), rows.stride(0), _stream()),
+                   "dcg_weight_unpack")
+        return rows
+
+    @property
+    def nbytes(self) -> int:
+        """Algorithmic bytes (ggml block bytes) of the weight."""
+        return self.n * row_size(self.qtype, self.k)
+
+
+def mul_mat_scratch_size(qtype: int, m: int, k: int) -> int:
+    return int(_lib.load().dcg_mul_mat_scratch_size(qtype, m, k))
+
+
+def mul_mat(w: QuantWeight, x: torch.Tensor, out: torch.Tensor | None = None,
+            scratch: torch.Tensor | None = None) -> torch.Tensor:
+    """y[m, n] = x[m, k] . W[n, k]^T with x quantized on the fly to W's vec_dot_type."""
+    _check_cuda(x, "x", torch.float32)
+    if x.shape[-1] != w.k:
+        raise ValueError(f"x has k={x.shape[-1]}, weight has k={w.k}")
+    m = x.numel() // w.k
+    if out is None:
+        out = torch.empty((m, w.n), dtype=torch.float32, device=x.device)
+    need = mul_mat_scratch_size(w.qtype, m, w.k)
+    if scratch is None:
+        scratch = torch.empty(need, dtype=torch.uint8, device=x.device)
+    _lib.check(_lib.load().dcg_mul_mat(w.qtype, _ptr(w.packed), w.n, w.k, _ptr(x), m, _ptr(out),
+                                       _ptr(scratch), scratch.numel(), _stream()), "dcg_mul_mat")
+    return out
+
+
+def quantize_act(x: torch.Tensor, act_type: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """f32 [m, k] -> device-layout activation (dcg_quantize_act) for mul_mat_q."""
+    _check_cuda(x, "x", torch.float32)
+    k = x.shape[-1]
+    m = x.numel() // k
+    L = _lib.load()
+    if out is None:
+        out = torch.empty(L.dcg_act_size(act_type, m, k), dtype=torch.uint8, device=x.device)
+    _lib.check(L.dcg_quantize_act(act_type, _ptr(x), _ptr(out), m, k, _stream()), "dcg_quantize_act")
+    return out
+
+
+def mul_mat_q(w: QuantWeight, act: torch.Tensor, m: int, out: torch.Tensor | None = None,
+              stream=None) -> torch.Tensor:
+    """y[m, n] = W . act with act from quantize_act(x, VEC_DOT_TYPE[w.qtype])."""
+    if out is None:
+        out = torch.empty((m, w.n), dtype=torch.float32, device=act.device)
+    _lib.check(_lib.load().dcg_mul_mat_q(w.qtype, _ptr(w.packed), w.n, w.k, _ptr(act), m,
+                                         _ptr(out), _stream(stream)), "dcg_mul_mat_q")
+    return out
+
+
+class HostContext:
+    """The synchronous host boundary: weights registered once by host pointer, per-call host
+    activations in and host results out (dcg_ctx_*)."""
+
+    def __init__(self, device: int = 0):
+        self._L = _lib.load()
+        h = ctypes.c_void_p()
+        _lib.check(self._L.dcg_ctx_create(device, ctypes.byref(h)), "dcg_ctx_create")
+        self.h = h
+        self._keep = {}
+
+    def register(self, rows: np.ndarray, qtype: int, k: int):
+        rows = np.ascontiguousarray(rows, dtype=np.uint8)
+        n = rows.shape[0]
+        w = ctypes.c_void_p()
+        _lib.check(self._L.dcg_ctx_weight_register(self.h, qtype, rows.ctypes.data, rows.strides[0],
+                                                   n, k, ctypes.byref(w)),
+                   "dcg_ctx_weight_register")
+        self._keep[w.value] = (rows, n, k)
+        return w
+
+    def mul_mat(self, w, x: np.ndarray) -> np.ndarray:
+        rows, n, k = self._keep[w.value]
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, k)
+        y = np.empty((x.shape[0], n), dtype=np.float32)
+        _lib.check(self._L.dcg_ctx_mul_mat(self.h, w, x.ctypes.data, x.shape[0], y.ctypes.data),
+                   "dcg_ctx_mul_mat")
+        return y
+
+    def close(self):
+        if self.h:
+            self._L.dcg_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,126 @@
+/*
+ * dcgpu.h -- C ABI of libdcgpu.so, the B200 (sm_100a) implementation of DenseCore's quantized
+ * weight matmul and paged decode attention.
+ *
+ * Plain C: pointers, sizes, ints.  Every entry point returns DCG_OK (0) or a negative DCG_E* code
+ * (DenseCore's C API convention, core/include/densecore.h:244); no C++ exception crosses it.
+ * dcg_last_error() gives the message of the calling thread's last failure.
+ *
+ * Two families:
+ *  (1) device entry points (suffix-free): all buffers are device pointers, work is enqueued on the
+ *      given cudaStream_t (passed as void*, NULL = legacy default stream) and nothing synchronizes.
+ *      These are what an engine with device-resident weights and KV cache calls per step.
+ *  (2) host entry points (dcg_ctx_*): the drop-in for the CPU call sites.  Weights are uploaded
+ *      once (dcg_ctx_weight_register) and stay resident; each call copies its host activations in
+ *      and its host results out and returns when they are ready.
+ *
+ * Type ids are ggml's enum ggml_type values.
+ */
+#ifndef DCGPU_H
+#define DCGPU_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DCG_OK 0
+#define DCG_EINVAL (-1)       /* bad argument: null pointer, unsupported type, bad shape */
+#define DCG_ECUDA (-2)        /* CUDA runtime error (message in dcg_last_error) */
+#define DCG_ENOMEM (-3)       /* device allocation failed */
+#define DCG_ESCRATCH (-4)     /* caller-provided scratch too small */
+#define DCG_ENOTFOUND (-5)    /* weight handle / host pointer not registered */
+
+#define DCG_TYPE_F32 0
+#define DCG_TYPE_F16 1
+#define DCG_TYPE_Q8_0 8
+#define DCG_TYPE_Q4_K 12
+#define DCG_TYPE_Q6_K 14
+#define DCG_TYPE_Q8_K 15
+
+#define DCG_KV_BLOCK_SIZE 16 /* tokens per KV block (core/include/kv_cache.h:17) */
+
+int dcg_version(void);
+const char* dcg_strerror(int code);
+const char* dcg_last_error(void);
+
+/* ---------------------------------------------------------------------------------------------
+ * Sizes
+ * ------------------------------------------------------------------------------------------- */
+/* ggml row bytes of k elements of `type` (ggml_row_size; inference.cpp:983, kv_cache.cpp:341). */
+size_t dcg_row_size(int type, int64_t k);
+/* bytes of an n x k weight in the device layout (see dcg_weight_pack). */
+size_t dcg_packed_weight_size(int type, int64_t n, int64_t k);
+/* scratch bytes dcg_mul_mat needs for m activation rows of length k. */
+size_t dcg_mul_mat_scratch_size(int type, int64_t m, int64_t k);
+
+/* ---------------------------------------------------------------------------------------------
+ * Activation quantization -- ggml type-trait from_float for the vec_dot_type of the weight
+ * (replaces from_float(x, q, N) at core/src/inference.cpp:889-892).  Output: ggml block bytes,
+ * m rows of dcg_row_size(type, k).  Byte-identical to ggml's reference quantizers.
+ * ------------------------------------------------------------------------------------------- */
+int dcg_quantize_row_q8_0(const float* x, void* y, int64_t m, int64_t k, void* stream);
+int dcg_quantize_row_q8_K(const float* x, void* y, int64_t m, int64_t k, void* stream);
+
+/* Weight encoder f32 -> ggml Q8_0 / Q4_K / Q6_K rows (offline-quantizer role of
+ * core/src/quantize.cpp; used to build seeded synthetic checkpoints on the device). */
+int dcg_quantize_weights(int type, const float* x, void* rows, int64_t n, int64_t k, void* stream);
+
+/* Upload-time repack of n ggml rows (row_stride bytes apart; ggml tensor nb[1]) into the device
+ * layout the matmul streams: Q4_K unchanged; Q8_0 and Q6_K with the fp16 block scales moved to a
+ * separate array so every payload row is 16-byte aligned.  dcg_weight_unpack inverts it. */
+int dcg_weight_pack(int type, const void* rows, size_t row_stride, int64_t n, int64_t k,
+                    void* packed, void* stream);
+int dcg_weight_unpack(int type, const void* packed, int64_t n, int64_t k, void* rows,
+                      size_t row_stride, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Quantized matmul -- the mul_mat op on a quantized weight (smart_mul_mat / ggml_mul_mat_gemv /
+ * cb_gemv_custom, core/src/inference.cpp:1043-1064, :958-1033, :840-948; ggml_mul_mat at
+ * :1063, :1794-1797, :1817).
+ *   y[m][n] = sum_k W[n][k] * x[m][k], x quantized on the fly to Q8_0 (Q8_0 weights) or Q8_K
+ *   (Q4_K / Q6_K weights), integer block dots, fp32 scaling and accumulation.
+ * w: device layout (dcg_weight_pack) of an n x k weight; k % 256 == 0 (k % 32 for Q8_0).
+ * scratch: >= dcg_mul_mat_scratch_size(type, m, k) bytes of device memory, 256-B aligned.
+ * ------------------------------------------------------------------------------------------- */
+int dcg_mul_mat(int type, const void* w, int64_t n, int64_t k, const float* x, int64_t m, float* y,
+                void* scratch, size_t scratch_bytes, void* stream);
+
+/* The two stages of dcg_mul_mat, for callers that quantize one activation once and multiply it by
+ * several weights (the Q/K/V projections share one input, inference.cpp:1128-1130).
+ * dcg_quantize_act writes the activation in the device layout (int8 payload rows, then block
+ * scales, then Q8_K block sums) that dcg_mul_mat_q reads; act_type is the vec_dot_type
+ * (DCG_TYPE_Q8_0 or DCG_TYPE_Q8_K); act must hold dcg_act_size(act_type, m, k) bytes, 256-B
+ * aligned.  dcg_mul_mat_q is ComputeDotProductBatch's job (core/src/simd_ops.cpp:140-197) for all
+ * rows and all m activation rows at once. */
+size_t dcg_act_size(int act_type, int64_t m, int64_t k);
+int dcg_quantize_act(int act_type, const float* x, void* act, int64_t m, int64_t k, void* stream);
+int dcg_mul_mat_q(int type, const void* w, int64_t n, int64_t k, const void* act, int64_t m,
+                  float* y, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Host boundary (drop-in for the CPU call sites; synchronous).
+ * ------------------------------------------------------------------------------------------- */
+typedef struct dcg_ctx dcg_ctx;
+typedef struct dcg_weight dcg_weight;
+
+/* One context per device (InitEngine-time, engine.cpp:122-278).  Thread-safe: calls serialize on
+ * an internal mutex. */
+int dcg_ctx_create(int device, dcg_ctx** out);
+int dcg_ctx_destroy(dcg_ctx* ctx);
+
+/* Upload one ggml weight tensor (n rows of k, ggml row stride) and keep it resident.  The host
+ * pointer is the key dcg_ctx_find_weight looks up (the weight_tensor->data of cb_gemv_custom). */
+int dcg_ctx_weight_register(dcg_ctx* ctx, int type, const void* host_rows, size_t row_stride,
+                            int64_t n, int64_t k, dcg_weight** out);
+int dcg_ctx_weight_release(dcg_ctx* ctx, dcg_weight* w);
+int dcg_ctx_find_weight(dcg_ctx* ctx, const void* host_rows, dcg_weight** out);
+
+/* cb_gemv_custom / ggml_mul_mat replacement: y_host[m][n] = W . x_host[m] (x f32, k per row). */
+int dcg_ctx_mul_mat(dcg_ctx* ctx, dcg_weight* w, const float* x_host, int64_t m, float* y_host);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DCGPU_H */

@@ -1,0 +1,161 @@
+"""GPU parity of the quantize / mul_mat kernels against the CPU oracle, through the C ABI.
+
+Bars: quantized activation bytes, weight bytes and repacks are bit-exact; fp32 mul_mat rows agree
+with the oracle to 1e-5 of sum_k |w_k x_k| (the rounding of a different summation order)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-5
+
+
+@pytest.fixture(scope="module")
+def ops():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from densecore_b200 import ops as _ops
+    return _ops
+
+
+def _dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _assert_rows_close(y, wq, wt, k, xq, xt, y_ref):
+    wd = O.dequantize(wq, wt, k).astype(np.float64)
+    xd = O.dequantize(xq, xt, k).astype(np.float64)
+    bound = np.abs(xd) @ np.abs(wd).T
+    err = np.abs(y.astype(np.float64) - y_ref.astype(np.float64))
+    worst = float((err / (bound + 1e-30)).max())
+    assert np.all(err <= RTOL * bound + 1e-30), f"max err/bound = {worst:.3e}"
+
+
+@pytest.mark.parametrize("m,k", [(1, 4096), (8, 4096), (3, 1024), (5, 14336)])
+def test_quantize_row_q8_0_bit_exact(ops, m, k):
+    rng = np.random.default_rng(m * 7 + k)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    x[0, :32] = 0.0
+    x[-1, 64:96] *= 1e5
+    got = ops.quantize_row_q8_0(_dev(x)).cpu().numpy()
+    assert np.array_equal(got, O.quantize(x, O.Q8_0))
+
+
+def test_quantize_row_q8_0_matches_gguf_golden(ops):
+    import os
+    G = np.load(os.path.join(os.path.dirname(__file__), "golden", "golden.npz"))
+    got = ops.quantize_row_q8_0(_dev(G["q8_0_x"])).cpu().numpy()
+    assert np.array_equal(got, G["q8_0_bytes"])
+
+
+@pytest.mark.parametrize("m,k", [(1, 4096), (16, 4096), (2, 14336), (4, 2560)])
+def test_quantize_row_q8_K_bit_exact(ops, m, k):
+    rng = np.random.default_rng(m * 11 + k)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    x[0, :256] = 0.0                              # all-zero block
+    x[-1, 300] = 50.0
+    x[-1, 301] = -50.0                            # magnitude tie: first index wins (sign +)
+    got = ops.quantize_row_q8_K(_dev(x)).cpu().numpy()
+    assert np.array_equal(got, O.quantize(x, O.Q8_K))
+
+
+@pytest.mark.parametrize("wt", [O.Q8_0, O.Q4_K, O.Q6_K])
+def test_weight_encoder_and_repack_bit_exact(ops, wt):
+    rng = np.random.default_rng(wt)
+    n, k = 64, 2560 if wt != O.Q8_0 else 1024
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    w[3, :256] = 0.0
+    rows = ops.quantize_weights(_dev(w), wt)
+    assert np.array_equal(rows.cpu().numpy(), O.quantize(w, wt))
+    qw = ops.QuantWeight.from_ggml(rows, wt, k)
+    assert np.array_equal(qw.to_ggml().cpu().numpy(), rows.cpu().numpy())
+
+
+MATMUL_CASES = [
+    # (weight type, n, k, m)
+    (O.Q8_0, 4096, 4096, 1),      # config 1
+    (O.Q8_0, 4096, 4096, 8),      # config 1
+    (O.Q8_0, 100, 1024, 3),       # ragged n
+    (O.Q8_0, 64, 4128, 2),        # k not a multiple of 512
+    (O.Q4_K, 2048, 4096, 1),
+    (O.Q4_K, 512, 14336, 1),
+    (O.Q4_K, 300, 2560, 5),       # ragged super-block count (10)
+    (O.Q4_K, 256, 9728, 12),      # 38 super-blocks, m > 8
+    (O.Q4_K, 128, 4096, 16),
+    (O.Q6_K, 1024, 4096, 1),
+    (O.Q6_K, 200, 9728, 7),
+    (O.Q6_K, 64, 2560, 16),
+]
+
+
+@pytest.mark.parametrize("wt,n,k,m", MATMUL_CASES)
+def test_mul_mat_matches_oracle(ops, wt, n, k, m):
+    rng = np.random.default_rng(n + k + m)
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    wq = O.quantize(w, wt)
+    xt = O.VEC_DOT_TYPE[wt]
+    xq = O.quantize(x, xt)
+    y_ref = O.mul_mat(wt, wq, k, xq, m, nthreads=8)
+    qw = ops.QuantWeight.from_ggml(_dev(wq), wt, k)
+    y = ops.mul_mat(qw, _dev(x)).cpu().numpy()
+    _assert_rows_close(y, wq, wt, k, xq, xt, y_ref)
+
+
+def test_mul_mat_config2_full_size(ops):
+    """Config 2 shapes (Q4_K 4096x14336 and 14336x4096, seed 1) at M=1: GPU-encoded weights equal
+    the oracle's bytes and the product matches the oracle row by row."""
+    rng = np.random.default_rng(1)
+    for n, k in ((14336, 4096), (4096, 14336)):
+        w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+        x = rng.standard_normal((1, k)).astype(np.float32)
+        wq = O.quantize(w, O.Q4_K)
+        rows = ops.quantize_weights(_dev(w), O.Q4_K)
+        assert np.array_equal(rows.cpu().numpy(), wq)
+        xq = O.quantize(x, O.Q8_K)
+        y_ref = O.mul_mat(O.Q4_K, wq, k, xq, 1, nthreads=8)
+        y = ops.mul_mat(ops.QuantWeight.from_ggml(rows, O.Q4_K, k), _dev(x)).cpu().numpy()
+        _assert_rows_close(y, wq, O.Q4_K, k, xq, O.Q8_K, y_ref)
+
+
+def test_mul_mat_linearity_in_x(ops):
+    """Size-independent property at config-2 size: W.(2^j x) == 2^j W.x exactly (power-of-two
+    scaling commutes with Q8_K quantization and with every fp32 rounding)."""
+    rng = np.random.default_rng(21)
+    n, k = 14336, 4096
+    w = torch.randn(n, k, device="cuda") * 0.02
+    qw = ops.QuantWeight.from_float(w, O.Q4_K)
+    x = torch.randn(1, k, device="cuda")
+    y1 = ops.mul_mat(qw, x)
+    y8 = ops.mul_mat(qw, x * 8.0)
+    assert torch.equal(y8, y1 * 8.0)
+    del rng
+
+
+def test_host_context_roundtrip(ops):
+    rng = np.random.default_rng(5)
+    n, k = 512, 4096
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    wq = O.quantize(w, O.Q4_K)
+    ctx = ops.HostContext(0)
+    h = ctx.register(wq, O.Q4_K, k)
+    for m in (1, 4):
+        x = rng.standard_normal((m, k)).astype(np.float32)
+        y = ctx.mul_mat(h, x)
+        xq = O.quantize(x, O.Q8_K)
+        _assert_rows_close(y, wq, O.Q4_K, k, xq, O.Q8_K, O.mul_mat(O.Q4_K, wq, k, xq, m, 8))
+    ctx.close()
+
+
+def test_errors_are_reported_not_raised_in_c(ops):
+    from densecore_b200._lib import DcgError
+    x = torch.zeros(1, 100, device="cuda")
+    with pytest.raises(DcgError):
+        ops.quantize_row_q8_0(x)          # k not a multiple of 32
+    w = ops.QuantWeight.from_float(torch.zeros(8, 256, device="cuda"), O.Q4_K)
+    with pytest.raises(DcgError):
+        ops.mul_mat(w, torch.zeros(1, 256, device="cuda"), scratch=torch.empty(16, dtype=torch.uint8,
+                                                                               device="cuda"))
