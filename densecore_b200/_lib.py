@@ -23,6 +23,7 @@ SIGNATURES = {
     "dcg_version": (i32, []),
     "dcg_strerror": (ctypes.c_char_p, [i32]),
     "dcg_last_error": (ctypes.c_char_p, []),
+    "dcg_device_error": (i32, [ctypes.POINTER(i32), i32]),
     "dcg_row_size": (sz, [i32, i64]),
     "dcg_packed_weight_size": (sz, [i32, i64, i64]),
     "dcg_mul_mat_scratch_size": (sz, [i32, i64, i64]),

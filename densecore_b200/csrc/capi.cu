@@ -163,6 +163,12 @@ int dcg_mul_mat(int type, const void* w, int64_t n, int64_t k, const float* x, i
     return enqueue_mul_mat(type, w, n, k, x, m, y, scratch, (cudaStream_t)stream);
 }
 
+int dcg_device_error(int* code, int clear) {
+    if (!code) return fail(DCG_EINVAL, "null pointer");
+    DCG_CUDA(dcg::gemv_device_error(code, clear != 0), "read device error flag");
+    return DCG_OK;
+}
+
 size_t dcg_act_size(int act_type, int64_t m, int64_t k) {
     if (act_type != DCG_TYPE_Q8_0 && act_type != DCG_TYPE_Q8_K) return 0;
     return dcg::act_bytes(act_type, m, k);

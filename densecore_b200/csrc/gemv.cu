@@ -16,6 +16,9 @@
 // reads the same few KB.
 #include "common.cuh"
 #include "kernels.h"
+#include "tma.cuh"
+
+#include <algorithm>
 
 namespace dcg {
 
@@ -37,24 +40,38 @@ struct WReg {
     float dmin;
 };
 
-template <int TYPE>
-__device__ __forceinline__ void load_w(const PackedW& w, int64_t row, int blk, int lane, WReg& r) {
+template <bool SMEM>
+__device__ __forceinline__ uint4 ldw(const uint8_t* p) {
+    if (SMEM) return *(const uint4*)p;
+    return ld_stream_v4(p);
+}
+
+// lane's weight registers of block `blk` of one row; rowp = start of the row's payload (global
+// or shared), drow = the row's fp16 block scales (Q8_0 / Q6_K; global)
+template <int TYPE, bool SMEM>
+__device__ __forceinline__ void load_w_row(const uint8_t* rowp, const __half* drow, int blk, int lane,
+                                           WReg& r) {
     if (TYPE == DCG_TYPE_Q8_0) {
-        const uint8_t* p = w.payload + row * w.row_bytes + (size_t)blk * QK8_0 + (lane & 1) * 16;
-        r.a = ld_stream_v4(p);
-        r.d = __half2float(w.d[row * w.nb + blk]);
+        r.a = ldw<SMEM>(rowp + (size_t)blk * QK8_0 + (lane & 1) * 16);
+        r.d = __half2float(drow[blk]);
     } else if (TYPE == DCG_TYPE_Q4_K) {
-        const uint8_t* p = w.payload + row * w.row_bytes + (size_t)blk * Q4_K_BYTES;
-        r.b = ld_stream_v4(p);
-        r.a = ld_stream_v4(p + 16 + (lane & 7) * 16);
+        const uint8_t* p = rowp + (size_t)blk * Q4_K_BYTES;
+        r.b = ldw<SMEM>(p);
+        r.a = ldw<SMEM>(p + 16 + (lane & 7) * 16);
     } else {
         const int i = lane & 7, h = i >> 2, c = (i >> 1) & 1, half = i & 1;
-        const uint8_t* p = w.payload + row * w.row_bytes + (size_t)blk * Q6_K_PAYLOAD;
-        r.a = ld_stream_v4(p + h * 64 + c * 32 + half * 16);
-        r.b = ld_stream_v4(p + 128 + h * 32 + half * 16);
-        r.c = ld_stream_v4(p + 192);
-        r.d = __half2float(w.d[row * w.nb + blk]);
+        const uint8_t* p = rowp + (size_t)blk * Q6_K_PAYLOAD;
+        r.a = ldw<SMEM>(p + h * 64 + c * 32 + half * 16);
+        r.b = ldw<SMEM>(p + 128 + h * 32 + half * 16);
+        r.c = ldw<SMEM>(p + 192);
+        r.d = __half2float(drow[blk]);
     }
+}
+
+template <int TYPE>
+__device__ __forceinline__ void load_w(const PackedW& w, int64_t row, int blk, int lane, WReg& r) {
+    load_w_row<TYPE, false>(w.payload + row * w.row_bytes, w.d ? w.d + row * w.nb : nullptr, blk,
+                            lane, r);
 }
 
 __device__ __forceinline__ uint32_t u4(const uint4& v, int t) {
@@ -185,6 +202,139 @@ __global__ void __launch_bounds__(256) gemv_kernel(PackedW w, int64_t n, int64_t
     }
 }
 
+// ------------------------------------------------------------------------------------------
+// TMA-streamed GEMV.  Tiles of TR consecutive whole rows (contiguous bytes of the row-major
+// payload) are copied global -> shared by the bulk-copy engine through a STAGES-deep ring of
+// buffers completing on mbarriers; the 8 warps decode from shared memory.  Thread 0 keeps
+// STAGES-1 tiles in flight; a __syncthreads at the end of each tile frees its buffer.
+//   TR >= 8: warp w reduces rows w, w+8, ... of the tile on its own;
+//   TR <  8: 8/TR warps split one row's units and combine partials in a fixed order.
+// ------------------------------------------------------------------------------------------
+// error flag of the bounded waits in this file (read back by dcg_device_error)
+__device__ int g_gemv_error = 0;
+
+cudaError_t gemv_device_error(int* out, bool clear) {
+    cudaError_t e = cudaMemcpyFromSymbol(out, g_gemv_error, sizeof(int));
+    if (e == cudaSuccess && clear && *out) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(g_gemv_error, &zero, sizeof(int));
+    }
+    return e;
+}
+
+constexpr int TMA_STAGES = 4;
+constexpr int TMA_TILE = 24 * 1024;  // bytes per stage; 2 CTAs (2 x ~97 KB) fit one SM
+
+template <int TYPE, int M>
+__global__ void __launch_bounds__(256, 2) gemv_tma_kernel(PackedW w, int64_t n, int64_t k, ActQ a,
+                                                          int m0, float* __restrict__ y, int TR) {
+    constexpr int PER = UnitInfo<TYPE>::BLOCKS;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = (uint64_t*)smem;                                    // [STAGES]
+    float* red = (float*)(smem + 64);                                    // [2][8][M]
+    uint8_t* buf = smem + 64 + ((2 * 8 * M * 4 + 127) & ~127);           // [STAGES][TILE]
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int nb = w.nb;
+    const int upr = (nb + PER - 1) / PER;  // units per row
+    const int lane_blk = (TYPE == DCG_TYPE_Q8_0) ? (lane >> 1) : (lane >> 3);
+    const int64_t n_tiles = (n + TR - 1) / TR;
+    const int my_tiles = (int)((n_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < TMA_STAGES; s++) mbar_init(&full[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    auto issue = [&](int i) {  // tile i of this CTA into stage i % STAGES
+        const int64_t t = blockIdx.x + (int64_t)i * gridDim.x;
+        const int64_t r0 = t * TR;
+        const int rows = (int)((n - r0) < TR ? (n - r0) : TR);
+        const uint32_t bytes = (uint32_t)(rows * w.row_bytes);
+        uint64_t* bar = &full[i % TMA_STAGES];
+        mbar_arrive_expect_tx(bar, bytes);
+        bulk_g2s(buf + (size_t)(i % TMA_STAGES) * TMA_TILE, w.payload + r0 * w.row_bytes, bytes, bar);
+    };
+    if (threadIdx.x == 0)
+        for (int i = 0; i < TMA_STAGES - 1 && i < my_tiles; i++) issue(i);
+
+    const int wpr = TR >= 8 ? 1 : 8 / TR;  // warps per row
+    for (int i = 0; i < my_tiles; i++) {
+        if (threadIdx.x == 0 && i + TMA_STAGES - 1 < my_tiles) {
+            fence_proxy_async_smem();
+            issue(i + TMA_STAGES - 1);
+        }
+        const int64_t r0 = (blockIdx.x + (int64_t)i * gridDim.x) * TR;
+        const int rows = (int)((n - r0) < TR ? (n - r0) : TR);
+        bool ok = mbar_wait(&full[i % TMA_STAGES], (uint32_t)((i / TMA_STAGES) & 1), &g_gemv_error);
+        const uint8_t* tile = buf + (size_t)(i % TMA_STAGES) * TMA_TILE;
+        float* redb = red + (i & 1) * 8 * M;
+        for (int rr = wid / wpr; rr < rows; rr += 8 / wpr) {
+            const int64_t row = r0 + rr;
+            const uint8_t* rowp = tile + (size_t)rr * w.row_bytes;
+            const __half* drow = w.d ? w.d + row * nb : nullptr;
+            float acc[M];
+#pragma unroll
+            for (int mm = 0; mm < M; mm++) acc[mm] = 0.0f;
+            for (int u = wid % wpr; u < upr; u += wpr) {
+                const int blk = u * PER + lane_blk;
+                if (blk < nb) {
+                    WReg r;
+                    load_w_row<TYPE, true>(rowp, drow, blk, lane, r);
+#pragma unroll
+                    for (int mm = 0; mm < M; mm++) acc[mm] += lane_dot<TYPE>(r, a, k, nb, m0 + mm, blk, lane);
+                }
+            }
+#pragma unroll
+            for (int mm = 0; mm < M; mm++) {
+                float v = acc[mm];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                acc[mm] = v;
+            }
+            if (lane == 0) {
+                if (wpr == 1) {
+#pragma unroll
+                    for (int mm = 0; mm < M; mm++) y[(size_t)(m0 + mm) * n + row] = acc[mm];
+                } else {
+#pragma unroll
+                    for (int mm = 0; mm < M; mm++) redb[wid * M + mm] = acc[mm];
+                }
+            }
+        }
+        ok = __syncthreads_and(ok);  // frees this stage for the next issue; uniform exit on error
+        if (!ok) return;
+        if (wpr > 1 && threadIdx.x < rows * M) {
+            const int rr = threadIdx.x / M, mm = threadIdx.x % M;
+            float s = 0.0f;
+            for (int q = 0; q < wpr; q++) s += redb[(rr * wpr + q) * M + mm];
+            y[(size_t)(m0 + mm) * n + r0 + rr] = s;
+        }
+    }
+}
+
+template <int TYPE, int M>
+static cudaError_t launch_gemv_tma_t(const PackedW& w, int64_t n, int64_t k, const ActQ& a, int m0,
+                                     float* y, cudaStream_t st) {
+    static int num_sms = 0;
+    static bool attr_set = false;
+    const size_t smem = 64 + ((2 * 8 * M * 4 + 127) & ~127) + (size_t)TMA_STAGES * TMA_TILE;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(gemv_tma_kernel<TYPE, M>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+        attr_set = true;
+    }
+    int TR = 1;
+    while (TR * 2 * (int64_t)w.row_bytes <= TMA_TILE && TR < 64) TR *= 2;
+    const int64_t n_tiles = (n + TR - 1) / TR;
+    const int64_t grid = std::min<int64_t>(n_tiles, (int64_t)num_sms * 2);
+    gemv_tma_kernel<TYPE, M><<<(unsigned)grid, 256, smem, st>>>(w, n, k, a, m0, y, TR);
+    return cudaGetLastError();
+}
+
 template <int TYPE, int M>
 static cudaError_t launch_gemv_t(const PackedW& w, int64_t n, int64_t k, const ActQ& a, int m0,
                                  float* y, cudaStream_t st) {
@@ -206,6 +356,18 @@ static cudaError_t launch_gemv_t(const PackedW& w, int64_t n, int64_t k, const A
 template <int TYPE>
 static cudaError_t dispatch_m(const PackedW& w, int64_t n, int64_t k, const ActQ& a, int m0, int m,
                               float* y, cudaStream_t st) {
+    if (w.row_bytes <= (size_t)TMA_TILE && w.row_bytes % 16 == 0) {
+        switch (m) {
+            case 1: return launch_gemv_tma_t<TYPE, 1>(w, n, k, a, m0, y, st);
+            case 2: return launch_gemv_tma_t<TYPE, 2>(w, n, k, a, m0, y, st);
+            case 3: return launch_gemv_tma_t<TYPE, 3>(w, n, k, a, m0, y, st);
+            case 4: return launch_gemv_tma_t<TYPE, 4>(w, n, k, a, m0, y, st);
+            case 5: return launch_gemv_tma_t<TYPE, 5>(w, n, k, a, m0, y, st);
+            case 6: return launch_gemv_tma_t<TYPE, 6>(w, n, k, a, m0, y, st);
+            case 7: return launch_gemv_tma_t<TYPE, 7>(w, n, k, a, m0, y, st);
+            case 8: return launch_gemv_tma_t<TYPE, 8>(w, n, k, a, m0, y, st);
+        }
+    }
     switch (m) {
         case 1: return launch_gemv_t<TYPE, 1>(w, n, k, a, m0, y, st);
         case 2: return launch_gemv_t<TYPE, 2>(w, n, k, a, m0, y, st);

@@ -16,5 +16,7 @@ cudaError_t launch_pack(int type, const void* src, size_t src_stride, void* dst,
 cudaError_t launch_gemv(int type, const void* packed_w, int64_t n, int64_t k, const void* act,
                         int64_t act_m, int64_t m0, int64_t m, float* y, cudaStream_t st);
 
+// error flag of the bounded waits of the GEMV kernels (0 = none); optionally cleared
+cudaError_t gemv_device_error(int* out, bool clear);
 
 }  // namespace dcg

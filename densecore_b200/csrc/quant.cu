@@ -93,8 +93,10 @@ __global__ void __launch_bounds__(256) quantize_q8_K_kernel(const float* __restr
         w1 |= (uint32_t)(uint8_t)q[i + 4] << (8 * i);
     }
     if (!out_soa) {
-        uint8_t* blk = y + b * Q8_K_BYTES;  // 292*b is 4-B aligned
-        *(uint2*)(blk + 4 + lane * 8) = make_uint2(w0, w1);
+        uint8_t* blk = y + b * Q8_K_BYTES;  // 292*b is only 4-B aligned: two 4-B stores
+        uint32_t* qw = (uint32_t*)(blk + 4 + lane * 8);
+        qw[0] = w0;
+        qw[1] = w1;
         if ((lane & 1) == 0) *(int16_t*)(blk + 260 + lane) = (int16_t)s;
         if (lane == 0) *(float*)blk = d;
     } else {

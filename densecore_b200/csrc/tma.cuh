@@ -1,0 +1,64 @@
+// tma.cuh -- 1-D bulk async copy (cp.async.bulk, TMA engine) and mbarrier helpers, sm_90+/sm_100a.
+// No cluster multicast anywhere: each CTA copies global memory of this GPU into its own shared
+// memory.  Every wait is bounded; on timeout the kernel records an error code
+// (a per-file __device__ flag passed in by the caller) and the host reads it back through
+// dcg_device_error instead of hanging the GPU.
+#pragma once
+#include <stdint.h>
+
+namespace dcg {
+
+constexpr int ERR_MBAR_TIMEOUT = 1;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// arm the barrier for `bytes` of transaction and arrive once
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+// global -> shared bulk copy completing on `bar`; src/dst 16-B aligned, bytes % 16 == 0
+__device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst_smem)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// wait for phase `parity` of `bar`; returns false after ~max_iter polls
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
+                                          uint32_t max_iter = 1u << 22) {
+    const uint32_t a = smem_u32(bar);
+    for (uint32_t it = 0; it < max_iter; ++it) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    atomicExch(err, ERR_MBAR_TIMEOUT);
+    return false;
+}
+
+}  // namespace dcg

@@ -45,6 +45,12 @@ int dcg_version(void);
 const char* dcg_strerror(int code);
 const char* dcg_last_error(void);
 
+/* Status of the kernels' bounded waits: *code = 0, or DCG_DEVERR_TIMEOUT when a kernel gave up
+ * waiting for a bulk copy and returned early (its outputs are then invalid).  clear != 0 resets
+ * it.  The flag is read with a blocking copy, so call it between steps. */
+#define DCG_DEVERR_TIMEOUT 1
+int dcg_device_error(int* code, int clear);
+
 /* ---------------------------------------------------------------------------------------------
  * Sizes
  * ------------------------------------------------------------------------------------------- */

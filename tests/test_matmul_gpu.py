@@ -159,3 +159,13 @@ def test_errors_are_reported_not_raised_in_c(ops):
     with pytest.raises(DcgError):
         ops.mul_mat(w, torch.zeros(1, 256, device="cuda"), scratch=torch.empty(16, dtype=torch.uint8,
                                                                                device="cuda"))
+
+
+def test_no_bounded_wait_expired(ops):
+    """After every kernel above, the bounded-wait error flag is still clear."""
+    import ctypes
+    from densecore_b200 import _lib
+    torch.cuda.synchronize()
+    code = ctypes.c_int(-1)
+    _lib.check(_lib.load().dcg_device_error(ctypes.byref(code), 0), "dcg_device_error")
+    assert code.value == 0
