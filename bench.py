@@ -322,6 +322,25 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+def profile_case(args):
+    """Small eager run for ncu: one weight (a few hundred MB at most), a few launches."""
+    import torch
+
+    from densecore_b200 import ops
+    torch.cuda.set_device(0)
+    qtype = {"q4k": Q4_K, "q8_0": 8, "q6k": 14}[args.profile_type]
+    n, k = {"up": SHAPES[0], "down": SHAPES[1], "sq": (4096, 4096)}[args.profile_shape]
+    m = args.profile_m
+    w = ops.QuantWeight.from_float(torch.randn((n, k), device="cuda") * 0.02, qtype)
+    x = torch.randn((m, k), device="cuda")
+    act = ops.quantize_act(x, Q8_K if qtype != 8 else 8)
+    y = torch.empty((m, n), device="cuda")
+    for _ in range(args.profile_iters):
+        ops.mul_mat_q(w, act, m, out=y)
+    torch.cuda.synchronize()
+    print("profile case done", qtype, n, k, m)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -331,7 +350,15 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-step-seconds", type=float, default=2.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-type", default=None, choices=["q4k", "q8_0", "q6k"],
+                    help="run only a small eager GEMV case (for ncu) and exit")
+    ap.add_argument("--profile-shape", default="up", choices=["up", "down", "sq"])
+    ap.add_argument("--profile-m", type=int, default=1)
+    ap.add_argument("--profile-iters", type=int, default=6)
     args = ap.parse_args()
+    if args.profile_type:
+        profile_case(args)
+        return
     if args.impl == "reference":
         # bounded: each timed step is a ~2 s sample of the CPU workload
         args.steps = min(args.steps, 20)

@@ -312,6 +312,258 @@ __global__ void __launch_bounds__(256, 2) gemv_tma_kernel(PackedW w, int64_t n, 
     }
 }
 
+// ------------------------------------------------------------------------------------------
+// Register-resident-activation variant (M <= 2).  A lane always decodes the same K positions of
+// every row it touches (its slot inside a super-block / block and the units u = sub + j*wpr of
+// its warp), so its slice of the quantized activation -- payload bytes, block scale and (Q4_K)
+// the two Q8_K block sums it needs -- is loaded into registers once per kernel.  The loop body is
+// then shared-memory weight loads, nibble unpacking, dp4a and a few fp32 ops.
+// ------------------------------------------------------------------------------------------
+struct XReg {
+    uint4 lo, hi;  // Q8_0: lo only; Q4_K: sub-blocks j0 / j1; Q6_K: low / high nibble elements
+    float d;       // activation block scale
+    int b0, b1;    // Q4_K: Q8_K bsums of this lane's 16-element halves of sub-blocks j0 / j1
+};
+
+template <int TYPE>
+__device__ __forceinline__ void load_x(const ActQ& a, int64_t k, int nb, int m, int blk, int lane,
+                                       XReg& x) {
+    if (TYPE == DCG_TYPE_Q8_0) {
+        x.lo = ld_act_v4(a.qs + (size_t)m * k + (size_t)blk * QK8_0 + (lane & 1) * 16);
+        x.d = __half2float(((const __half*)a.d)[(size_t)m * nb + blk]);
+    } else if (TYPE == DCG_TYPE_Q4_K) {
+        const int i = lane & 7, g = i >> 1, half = i & 1;
+        const int8_t* xq = a.qs + (size_t)m * k + (size_t)blk * QK_K + 64 * g + half * 16;
+        x.lo = ld_act_v4(xq);
+        x.hi = ld_act_v4(xq + 32);
+        x.d = ((const float*)a.d)[(size_t)m * nb + blk];
+        const int16_t* bs = a.bsums + (size_t)m * (k / 16) + (size_t)blk * 16;
+        x.b0 = bs[4 * g + half];
+        x.b1 = bs[4 * g + 2 + half];
+    } else {
+        const int i = lane & 7, h = i >> 2, c = (i >> 1) & 1, half = i & 1;
+        const int8_t* xq = a.qs + (size_t)m * k + (size_t)blk * QK_K + h * 128 + c * 32 + half * 16;
+        x.lo = ld_act_v4(xq);
+        x.hi = ld_act_v4(xq + 64);
+        x.d = ((const float*)a.d)[(size_t)m * nb + blk];
+    }
+}
+
+// Q4_K: the (scale, min) pairs of sub-blocks j0 = 2g and j1 = 2g+1, branch-free; returns
+// sc0 | sc1 << 8 in *sc and m0 | m1 << 8 in *mn (ggml get_scale_min_k4 layout)
+__device__ __forceinline__ void q4k_pair(const uint4& hdr, int g, uint32_t& sc, uint32_t& mn) {
+    const int sh = 16 * (g & 1);  // bytes (2g)&3 and (2g+1)&3 of each scale word
+    const uint32_t a0 = (hdr.y >> sh) & 0xFFFFu, a1 = (hdr.z >> sh) & 0xFFFFu, a2 = (hdr.w >> sh) & 0xFFFFu;
+    const uint32_t sc_lo = a0 & 0x3F3Fu, mn_lo = a1 & 0x3F3Fu;
+    const uint32_t sc_hi = (a2 & 0x0F0Fu) | ((a0 >> 2) & 0x3030u);
+    const uint32_t mn_hi = ((a2 >> 4) & 0x0F0Fu) | ((a1 >> 2) & 0x3030u);
+    sc = g >= 2 ? sc_hi : sc_lo;
+    mn = g >= 2 ? mn_hi : mn_lo;
+}
+
+template <int TYPE>
+__device__ __forceinline__ float xr_dot(const uint4& wa, const uint4& wb, const uint4& wc, float wd,
+                                        const XReg& x, int lane) {
+    if (TYPE == DCG_TYPE_Q8_0) {
+        int s = dp4a((int)wa.x, (int)x.lo.x, 0);
+        s = dp4a((int)wa.y, (int)x.lo.y, s);
+        s = dp4a((int)wa.z, (int)x.lo.z, s);
+        s = dp4a((int)wa.w, (int)x.lo.w, s);
+        return (wd * x.d) * (float)s;
+    } else if (TYPE == DCG_TYPE_Q4_K) {
+        int d0 = 0, d1 = 0;
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+            const uint32_t q = u4(wa, t);
+            d0 = dp4a((int)(q & 0x0F0F0F0Fu), (int)u4(x.lo, t), d0);
+            d1 = dp4a((int)((q >> 4) & 0x0F0F0F0Fu), (int)u4(x.hi, t), d1);
+        }
+        uint32_t sc, mn;
+        q4k_pair(wb, (lane & 7) >> 1, sc, mn);
+        const int isum = (int)(sc & 0xFF) * d0 + (int)(sc >> 8) * d1;
+        const int msum = (int)(mn & 0xFF) * x.b0 + (int)(mn >> 8) * x.b1;
+        const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&wb.x));
+        return x.d * (dd.x * (float)isum - dd.y * (float)msum);
+    } else {
+        const int i = lane & 7, h = i >> 2, c = (i >> 1) & 1, half = i & 1;
+        int d0 = 0, d1 = 0;
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+            const uint32_t ql = u4(wa, t), qh = u4(wb, t);
+            const uint32_t lo = (ql & 0x0F0F0F0Fu) | (((qh >> (2 * c)) & 0x03030303u) << 4);
+            const uint32_t hi = ((ql >> 4) & 0x0F0F0F0Fu) | (((qh >> (2 * c + 4)) & 0x03030303u) << 4);
+            d0 = dp4a((int)__vsub4(lo, 0x20202020u), (int)u4(x.lo, t), d0);
+            d1 = dp4a((int)__vsub4(hi, 0x20202020u), (int)u4(x.hi, t), d1);
+        }
+        const int s_lo = h * 8 + c * 2 + half;  // scales s_lo (word s_lo/4) and s_lo + 4 (next word)
+        const int sc_lo = (int)(int8_t)(u4(wc, s_lo >> 2) >> (8 * (s_lo & 3)));
+        const int sc_hi = (int)(int8_t)(u4(wc, (s_lo >> 2) + 1) >> (8 * (s_lo & 3)));
+        return (wd * x.d) * (float)(sc_lo * d0 + sc_hi * d1);
+    }
+}
+
+template <int TYPE, int M, int UW>
+__global__ void __launch_bounds__(256, 2) gemv_tma_xr_kernel(PackedW w, int64_t n, int64_t k, ActQ a,
+                                                             int m0, float* __restrict__ y, int TR) {
+    constexpr int PER = UnitInfo<TYPE>::BLOCKS;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = (uint64_t*)smem;
+    float* red = (float*)(smem + 64);
+    uint8_t* buf = smem + 64 + ((2 * 8 * M * 4 + 127) & ~127);
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int nb = w.nb;
+    const int upr = (nb + PER - 1) / PER;
+    const int lane_blk = (TYPE == DCG_TYPE_Q8_0) ? (lane >> 1) : (lane >> 3);
+    const int64_t n_tiles = (n + TR - 1) / TR;
+    const int my_tiles = (int)((n_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x);
+    const int wpr = TR >= 8 ? 1 : 8 / TR;
+    const int sub = wid % wpr;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < TMA_STAGES; s++) mbar_init(&full[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    auto issue = [&](int i) {
+        const int64_t t = blockIdx.x + (int64_t)i * gridDim.x;
+        const int64_t r0 = t * TR;
+        const int rows = (int)((n - r0) < TR ? (n - r0) : TR);
+        const uint32_t bytes = (uint32_t)(rows * w.row_bytes);
+        uint64_t* bar = &full[i % TMA_STAGES];
+        mbar_arrive_expect_tx(bar, bytes);
+        bulk_g2s(buf + (size_t)(i % TMA_STAGES) * TMA_TILE, w.payload + r0 * w.row_bytes, bytes, bar);
+    };
+    if (threadIdx.x == 0)
+        for (int i = 0; i < TMA_STAGES - 1 && i < my_tiles; i++) issue(i);
+
+    // this lane's activation slice, once (overlaps the first bulk copies)
+    XReg xr[UW][M];
+    bool uok[UW];
+#pragma unroll
+    for (int j = 0; j < UW; j++) {
+        const int u = sub + j * wpr;
+        const int blk = u * PER + lane_blk;
+        uok[j] = (u < upr) && (blk < nb);
+#pragma unroll
+        for (int mm = 0; mm < M; mm++)
+            if (uok[j]) load_x<TYPE>(a, k, nb, m0 + mm, blk, lane, xr[j][mm]);
+    }
+
+    for (int i = 0; i < my_tiles; i++) {
+        if (threadIdx.x == 0 && i + TMA_STAGES - 1 < my_tiles) {
+            fence_proxy_async_smem();
+            issue(i + TMA_STAGES - 1);
+        }
+        const int64_t r0 = (blockIdx.x + (int64_t)i * gridDim.x) * TR;
+        const int rows = (int)((n - r0) < TR ? (n - r0) : TR);
+        bool ok = mbar_wait(&full[i % TMA_STAGES], (uint32_t)((i / TMA_STAGES) & 1), &g_gemv_error);
+        const uint8_t* tile = buf + (size_t)(i % TMA_STAGES) * TMA_TILE;
+        float* redb = red + (i & 1) * 8 * M;
+        for (int rr = wid / wpr; rr < rows; rr += 8 / wpr) {
+            const int64_t row = r0 + rr;
+            const uint8_t* rowp = tile + (size_t)rr * w.row_bytes;
+            float wdv[UW];
+            if (TYPE != DCG_TYPE_Q4_K) {
+#pragma unroll
+                for (int j = 0; j < UW; j++)
+                    wdv[j] = uok[j] ? __half2float(w.d[row * nb + (sub + j * wpr) * PER + lane_blk]) : 0.0f;
+            }
+            float acc[M];
+#pragma unroll
+            for (int mm = 0; mm < M; mm++) acc[mm] = 0.0f;
+#pragma unroll
+            for (int j = 0; j < UW; j++) {
+                if (!uok[j]) continue;
+                const int blk = (sub + j * wpr) * PER + lane_blk;
+                uint4 wa, wb = make_uint4(0, 0, 0, 0), wc = make_uint4(0, 0, 0, 0);
+                if (TYPE == DCG_TYPE_Q8_0) {
+                    wa = *(const uint4*)(rowp + (size_t)blk * QK8_0 + (lane & 1) * 16);
+                } else if (TYPE == DCG_TYPE_Q4_K) {
+                    const uint8_t* p = rowp + (size_t)blk * Q4_K_BYTES;
+                    wb = *(const uint4*)p;
+                    wa = *(const uint4*)(p + 16 + (lane & 7) * 16);
+                } else {
+                    const int li = lane & 7, h = li >> 2, c = (li >> 1) & 1, half = li & 1;
+                    const uint8_t* p = rowp + (size_t)blk * Q6_K_PAYLOAD;
+                    wa = *(const uint4*)(p + h * 64 + c * 32 + half * 16);
+                    wb = *(const uint4*)(p + 128 + h * 32 + half * 16);
+                    wc = *(const uint4*)(p + 192);
+                }
+#pragma unroll
+                for (int mm = 0; mm < M; mm++)
+                    acc[mm] += xr_dot<TYPE>(wa, wb, wc, TYPE == DCG_TYPE_Q4_K ? 0.0f : wdv[j], xr[j][mm], lane);
+            }
+#pragma unroll
+            for (int mm = 0; mm < M; mm++) {
+                float v = acc[mm];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                acc[mm] = v;
+            }
+            if (lane == 0) {
+                if (wpr == 1) {
+#pragma unroll
+                    for (int mm = 0; mm < M; mm++) y[(size_t)(m0 + mm) * n + row] = acc[mm];
+                } else {
+#pragma unroll
+                    for (int mm = 0; mm < M; mm++) redb[wid * M + mm] = acc[mm];
+                }
+            }
+        }
+        ok = __syncthreads_and(ok);
+        if (!ok) return;
+        if (wpr > 1 && threadIdx.x < rows * M) {
+            const int rr = threadIdx.x / M, mm = threadIdx.x % M;
+            float s = 0.0f;
+            for (int q = 0; q < wpr; q++) s += redb[(rr * wpr + q) * M + mm];
+            y[(size_t)(m0 + mm) * n + r0 + rr] = s;
+        }
+    }
+}
+
+template <int TYPE, int M, int UW>
+static cudaError_t launch_xr(const PackedW& w, int64_t n, int64_t k, const ActQ& a, int m0, float* y,
+                             int TR, int grid, cudaStream_t st) {
+    static bool attr_set = false;
+    const size_t smem = 64 + ((2 * 8 * M * 4 + 127) & ~127) + (size_t)TMA_STAGES * TMA_TILE;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(gemv_tma_xr_kernel<TYPE, M, UW>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    gemv_tma_xr_kernel<TYPE, M, UW><<<(unsigned)grid, 256, smem, st>>>(w, n, k, a, m0, y, TR);
+    return cudaGetLastError();
+}
+
+static int g_num_sms = 0;
+
+// returns cudaErrorNotSupported when the shape needs more than 8 units per warp
+template <int TYPE, int M>
+static cudaError_t launch_gemv_xr_t(const PackedW& w, int64_t n, int64_t k, const ActQ& a, int m0,
+                                    float* y, cudaStream_t st) {
+    if (!g_num_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    constexpr int PER = UnitInfo<TYPE>::BLOCKS;
+    int TR = 1;
+    while (TR * 2 * (int64_t)w.row_bytes <= TMA_TILE && TR < 64) TR *= 2;
+    const int wpr = TR >= 8 ? 1 : 8 / TR;
+    const int upr = (w.nb + PER - 1) / PER;
+    const int uw = (upr + wpr - 1) / wpr;
+    const int64_t n_tiles = (n + TR - 1) / TR;
+    const int grid = (int)std::min<int64_t>(n_tiles, (int64_t)g_num_sms * 2);
+    if (uw <= 1) return launch_xr<TYPE, M, 1>(w, n, k, a, m0, y, TR, grid, st);
+    if (uw <= 2) return launch_xr<TYPE, M, 2>(w, n, k, a, m0, y, TR, grid, st);
+    if (uw <= 4) return launch_xr<TYPE, M, 4>(w, n, k, a, m0, y, TR, grid, st);
+    if constexpr (M == 1) {  // 8 units x 2 activation rows would spill
+        if (uw <= 8) return launch_xr<TYPE, M, 8>(w, n, k, a, m0, y, TR, grid, st);
+    }
+    return cudaErrorNotSupported;
+}
+
 template <int TYPE, int M>
 static cudaError_t launch_gemv_tma_t(const PackedW& w, int64_t n, int64_t k, const ActQ& a, int m0,
                                      float* y, cudaStream_t st) {
@@ -357,6 +609,11 @@ template <int TYPE>
 static cudaError_t dispatch_m(const PackedW& w, int64_t n, int64_t k, const ActQ& a, int m0, int m,
                               float* y, cudaStream_t st) {
     if (w.row_bytes <= (size_t)TMA_TILE && w.row_bytes % 16 == 0) {
+        if (m <= 2) {
+            cudaError_t e = m == 1 ? launch_gemv_xr_t<TYPE, 1>(w, n, k, a, m0, y, st)
+                                   : launch_gemv_xr_t<TYPE, 2>(w, n, k, a, m0, y, st);
+            if (e != cudaErrorNotSupported) return e;
+        }
         switch (m) {
             case 1: return launch_gemv_tma_t<TYPE, 1>(w, n, k, a, m0, y, st);
             case 2: return launch_gemv_tma_t<TYPE, 2>(w, n, k, a, m0, y, st);

@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(256) encode_q4_K_kernel(const float* __restric
         hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
     }
     const float scale = __fdiv_rn(__fsub_rn(hi, lo), 15.0f);
-    const float mn = -lo;
+    const float mn = lo < 0.0f ? -lo : 0.0f;  // +0 (never -0) when the sub-block has no negatives
     float max_scale = scale, max_min = mn;
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {

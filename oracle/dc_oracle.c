@@ -178,7 +178,7 @@ void dco_quantize_row_q4_K(const float* x, void* vy, int64_t k) {
                 if (v > hi) hi = v;
             }
             scale[j] = (hi - lo) / 15.0f;
-            mn[j] = -lo;
+            mn[j] = lo < 0.0f ? -lo : 0.0f; /* +0, never -0 */
             if (scale[j] > max_scale) max_scale = scale[j];
             if (mn[j] > max_min) max_min = mn[j];
         }

@@ -152,9 +152,11 @@ def test_host_context_roundtrip(ops):
 
 def test_errors_are_reported_not_raised_in_c(ops):
     from densecore_b200._lib import DcgError
+    from densecore_b200 import _lib
     x = torch.zeros(1, 100, device="cuda")
-    with pytest.raises(DcgError):
-        ops.quantize_row_q8_0(x)          # k not a multiple of 32
+    y = torch.zeros(1, 200, dtype=torch.uint8, device="cuda")
+    rc = _lib.load().dcg_quantize_row_q8_0(x.data_ptr(), y.data_ptr(), 1, 100, None)
+    assert rc == -1 and b"multiple" in _lib.load().dcg_last_error()   # k not a multiple of 32
     w = ops.QuantWeight.from_float(torch.zeros(8, 256, device="cuda"), O.Q4_K)
     with pytest.raises(DcgError):
         ops.mul_mat(w, torch.zeros(1, 256, device="cuda"), scratch=torch.empty(16, dtype=torch.uint8,
