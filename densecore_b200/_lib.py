@@ -36,6 +36,7 @@ SIGNATURES = {
     "dcg_act_size": (sz, [i32, i64, i64]),
     "dcg_quantize_act": (i32, [i32, vp, vp, i64, i64, vp]),
     "dcg_mul_mat_q": (i32, [i32, vp, i64, i64, vp, i64, vp, vp]),
+    "dcg_mul_mat_noalloc": (i32, [i32, vp, i64, i64, vp, i64, vp, vp]),
     "dcg_ctx_create": (i32, [i32, ctypes.POINTER(vp)]),
     "dcg_ctx_destroy": (i32, [vp]),
     "dcg_ctx_weight_register": (i32, [vp, i32, vp, sz, i64, i64, ctypes.POINTER(vp)]),

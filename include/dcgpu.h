@@ -105,6 +105,17 @@ int dcg_quantize_act(int act_type, const float* x, void* act, int64_t m, int64_t
 int dcg_mul_mat_q(int type, const void* w, int64_t n, int64_t k, const void* act, int64_t m,
                   float* y, void* stream);
 
+/* dcg_mul_mat without scratch: for callers that cannot allocate device memory where they run the
+ * matmul (a ggml custom-op callback inside the compute thread pool, a plugin host that forbids
+ * allocation after start-up, a step that must not synchronize on cudaMalloc).  No counterpart in
+ * the reference.  The quantized activation lives in a fixed 1 MiB device array owned by the
+ * library (held on every GPU that loads it until exit); calls needing more than that
+ * (dcg_act_size of the vec_dot_type) fail with DCG_EINVAL.  All calls share the array: calls that
+ * overlap on the GPU race, so keep them on one stream.  The first call on each device resolves the
+ * array's address; make it before any stream capture.  Allocates nothing. */
+int dcg_mul_mat_noalloc(int type, const void* w, int64_t n, int64_t k, const float* x, int64_t m,
+                        float* y, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Host boundary (drop-in for the CPU call sites; synchronous).
  * ------------------------------------------------------------------------------------------- */
