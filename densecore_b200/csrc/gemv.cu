@@ -402,8 +402,13 @@ __device__ __forceinline__ float xr_dot(const uint4& wa, const uint4& wb, const 
     }
 }
 
+// 3 CTAs of 8 warps per SM: 3 stages of 20 KB each, <= 85 registers per thread
+constexpr int XR_STAGES = 3;
+constexpr int XR_TILE = 20 * 1024;
+constexpr int XR_CTAS = 3;
+
 template <int TYPE, int M, int UW>
-__global__ void __launch_bounds__(256, 2) gemv_tma_xr_kernel(PackedW w, int64_t n, int64_t k, ActQ a,
+__global__ void __launch_bounds__(256, (UW <= 4 ? XR_CTAS : 2)) gemv_tma_xr_kernel(PackedW w, int64_t n, int64_t k, ActQ a,
                                                              int m0, float* __restrict__ y, int TR) {
     constexpr int PER = UnitInfo<TYPE>::BLOCKS;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -420,7 +425,7 @@ __global__ void __launch_bounds__(256, 2) gemv_tma_xr_kernel(PackedW w, int64_t 
     const int sub = wid % wpr;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < TMA_STAGES; s++) mbar_init(&full[s], 1);
+        for (int s = 0; s < XR_STAGES; s++) mbar_init(&full[s], 1);
         fence_mbar_init();
     }
     __syncthreads();
@@ -429,12 +434,12 @@ __global__ void __launch_bounds__(256, 2) gemv_tma_xr_kernel(PackedW w, int64_t 
         const int64_t r0 = t * TR;
         const int rows = (int)((n - r0) < TR ? (n - r0) : TR);
         const uint32_t bytes = (uint32_t)(rows * w.row_bytes);
-        uint64_t* bar = &full[i % TMA_STAGES];
+        uint64_t* bar = &full[i % XR_STAGES];
         mbar_arrive_expect_tx(bar, bytes);
-        bulk_g2s(buf + (size_t)(i % TMA_STAGES) * TMA_TILE, w.payload + r0 * w.row_bytes, bytes, bar);
+        bulk_g2s(buf + (size_t)(i % XR_STAGES) * XR_TILE, w.payload + r0 * w.row_bytes, bytes, bar);
     };
     if (threadIdx.x == 0)
-        for (int i = 0; i < TMA_STAGES - 1 && i < my_tiles; i++) issue(i);
+        for (int i = 0; i < XR_STAGES - 1 && i < my_tiles; i++) issue(i);
 
     // this lane's activation slice, once (overlaps the first bulk copies)
     XReg xr[UW][M];
@@ -450,14 +455,14 @@ __global__ void __launch_bounds__(256, 2) gemv_tma_xr_kernel(PackedW w, int64_t 
     }
 
     for (int i = 0; i < my_tiles; i++) {
-        if (threadIdx.x == 0 && i + TMA_STAGES - 1 < my_tiles) {
+        if (threadIdx.x == 0 && i + XR_STAGES - 1 < my_tiles) {
             fence_proxy_async_smem();
-            issue(i + TMA_STAGES - 1);
+            issue(i + XR_STAGES - 1);
         }
         const int64_t r0 = (blockIdx.x + (int64_t)i * gridDim.x) * TR;
         const int rows = (int)((n - r0) < TR ? (n - r0) : TR);
-        bool ok = mbar_wait(&full[i % TMA_STAGES], (uint32_t)((i / TMA_STAGES) & 1), &g_gemv_error);
-        const uint8_t* tile = buf + (size_t)(i % TMA_STAGES) * TMA_TILE;
+        bool ok = mbar_wait(&full[i % XR_STAGES], (uint32_t)((i / XR_STAGES) & 1), &g_gemv_error);
+        const uint8_t* tile = buf + (size_t)(i % XR_STAGES) * XR_TILE;
         float* redb = red + (i & 1) * 8 * M;
         for (int rr = wid / wpr; rr < rows; rr += 8 / wpr) {
             const int64_t row = r0 + rr;
@@ -525,7 +530,7 @@ template <int TYPE, int M, int UW>
 static cudaError_t launch_xr(const PackedW& w, int64_t n, int64_t k, const ActQ& a, int m0, float* y,
                              int TR, int grid, cudaStream_t st) {
     static bool attr_set = false;
-    const size_t smem = 64 + ((2 * 8 * M * 4 + 127) & ~127) + (size_t)TMA_STAGES * TMA_TILE;
+    const size_t smem = 64 + ((2 * 8 * M * 4 + 127) & ~127) + (size_t)XR_STAGES * XR_TILE;
     if (!attr_set) {
         cudaError_t e = cudaFuncSetAttribute(gemv_tma_xr_kernel<TYPE, M, UW>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -549,12 +554,12 @@ static cudaError_t launch_gemv_xr_t(const PackedW& w, int64_t n, int64_t k, cons
     }
     constexpr int PER = UnitInfo<TYPE>::BLOCKS;
     int TR = 1;
-    while (TR * 2 * (int64_t)w.row_bytes <= TMA_TILE && TR < 64) TR *= 2;
+    while (TR * 2 * (int64_t)w.row_bytes <= XR_TILE && TR < 64) TR *= 2;
     const int wpr = TR >= 8 ? 1 : 8 / TR;
     const int upr = (w.nb + PER - 1) / PER;
     const int uw = (upr + wpr - 1) / wpr;
     const int64_t n_tiles = (n + TR - 1) / TR;
-    const int grid = (int)std::min<int64_t>(n_tiles, (int64_t)g_num_sms * 2);
+    const int grid = (int)std::min<int64_t>(n_tiles, (int64_t)g_num_sms * XR_CTAS);
     if (uw <= 1) return launch_xr<TYPE, M, 1>(w, n, k, a, m0, y, TR, grid, st);
     if (uw <= 2) return launch_xr<TYPE, M, 2>(w, n, k, a, m0, y, TR, grid, st);
     if (uw <= 4) return launch_xr<TYPE, M, 4>(w, n, k, a, m0, y, TR, grid, st);
