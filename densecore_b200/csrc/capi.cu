@@ -169,6 +169,55 @@ int dcg_device_error(int* code, int clear) {
     return DCG_OK;
 }
 
+size_t dcg_paged_attn_scratch_size(int n_seqs, int hq, int hkv, int head_dim, int max_ctx) {
+    if (n_seqs <= 0 || hq <= 0 || hkv <= 0 || head_dim != 128 || max_ctx < 0) return 0;
+    return dcg::attn_scratch_bytes(n_seqs, hq, hkv, max_ctx);
+}
+
+int dcg_paged_attn_decode(const float* q, const void* k_arena, const void* v_arena, int n_layer,
+                          int layer, const int32_t* block_tables, int max_blocks_per_seq,
+                          const int32_t* ctx_lens, int n_seqs, int hq, int hkv, int head_dim,
+                          int max_ctx, float scale, float* out, void* scratch, size_t scratch_bytes,
+                          void* stream) {
+    if (n_seqs < 0) return fail(DCG_EINVAL, "n_seqs < 0");
+    if (n_seqs == 0) return DCG_OK;
+    if (!q || !k_arena || !v_arena || !block_tables || !ctx_lens || !out)
+        return fail(DCG_EINVAL, "null pointer");
+    if (head_dim != 128) return fail(DCG_EINVAL, "head_dim must be 128");
+    if (hkv <= 0 || hq <= 0 || hq % hkv) return fail(DCG_EINVAL, "hq must be a multiple of hkv");
+    const int nrep = hq / hkv;
+    if (nrep != 1 && nrep != 2 && nrep != 4 && nrep != 8) return fail(DCG_EINVAL, "hq/hkv must be 1, 2, 4 or 8");
+    if (n_layer <= 0 || layer < 0 || layer >= n_layer) return fail(DCG_EINVAL, "bad layer");
+    if (max_ctx < 0 || max_ctx > 16 * max_blocks_per_seq) return fail(DCG_EINVAL, "max_ctx exceeds the block table");
+    if (!aligned(k_arena, 16) || !aligned(v_arena, 16) || !aligned(q, 16) || !aligned(out, 16))
+        return fail(DCG_EINVAL, "q, out and the arenas must be 16-byte aligned");
+    const size_t need = dcg::attn_scratch_bytes(n_seqs, hq, hkv, max_ctx);
+    if (scratch_bytes < need || (need && !scratch))
+        return fail(DCG_ESCRATCH, "attention scratch needs " + std::to_string(need) + " bytes");
+    if (need && !aligned(scratch, 256)) return fail(DCG_EINVAL, "scratch must be 256-byte aligned");
+    DCG_CUDA(dcg::launch_paged_attn(q, k_arena, v_arena, n_layer, layer, block_tables,
+                                    max_blocks_per_seq, ctx_lens, n_seqs, hq, hkv, max_ctx, scale, out,
+                                    scratch, (cudaStream_t)stream), "paged_attn_decode");
+    return DCG_OK;
+}
+
+int dcg_kv_append(const float* k, const float* v, void* k_arena, void* v_arena, int n_layer,
+                  int layer, const int32_t* block_tables, int max_blocks_per_seq,
+                  const int32_t* seq_ids, const int32_t* positions, int n_tok, int hkv,
+                  int head_dim, void* stream) {
+    if (n_tok < 0) return fail(DCG_EINVAL, "n_tok < 0");
+    if (n_tok == 0) return DCG_OK;
+    if (!k || !v || !k_arena || !v_arena || !block_tables || !seq_ids || !positions)
+        return fail(DCG_EINVAL, "null pointer");
+    if (hkv <= 0 || head_dim <= 0 || n_layer <= 0 || layer < 0 || layer >= n_layer || max_blocks_per_seq <= 0)
+        return fail(DCG_EINVAL, "bad shape");
+    if (!aligned(k_arena, 2) || !aligned(v_arena, 2)) return fail(DCG_EINVAL, "arenas must be 2-byte aligned");
+    DCG_CUDA(dcg::launch_kv_append(k, v, k_arena, v_arena, n_layer, layer, block_tables,
+                                   max_blocks_per_seq, seq_ids, positions, n_tok, hkv, head_dim,
+                                   (cudaStream_t)stream), "kv_append");
+    return DCG_OK;
+}
+
 size_t dcg_act_size(int act_type, int64_t m, int64_t k) {
     if (act_type != DCG_TYPE_Q8_0 && act_type != DCG_TYPE_Q8_K) return 0;
     return dcg::act_bytes(act_type, m, k);

@@ -16,6 +16,17 @@ cudaError_t launch_pack(int type, const void* src, size_t src_stride, void* dst,
 cudaError_t launch_gemv(int type, const void* packed_w, int64_t n, int64_t k, const void* act,
                         int64_t act_m, int64_t m0, int64_t m, float* y, cudaStream_t st);
 
+// paged decode attention (attn.cu)
+void attn_plan(int n_seqs, int hkv, int max_ctx, int* splits, int* bps);
+size_t attn_scratch_bytes(int n_seqs, int hq, int hkv, int max_ctx);
+cudaError_t launch_paged_attn(const float* q, const void* karena, const void* varena, int n_layer,
+                              int layer, const int* bt, int mbs, const int* ctx, int n_seqs, int hq,
+                              int hkv, int max_ctx, float scale, float* out, void* scratch,
+                              cudaStream_t st);
+cudaError_t launch_kv_append(const float* k, const float* v, void* karena, void* varena, int n_layer,
+                             int layer, const int* bt, int mbs, const int* seq_ids, const int* pos,
+                             int n_tok, int hkv, int hd, cudaStream_t st);
+
 // error flag of the bounded waits of the GEMV kernels (0 = none); optionally cleared
 cudaError_t gemv_device_error(int* out, bool clear);
 

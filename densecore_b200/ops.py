@@ -148,6 +148,51 @@ def mul_mat_q(w: QuantWeight, act: torch.Tensor, m: int, out: torch.Tensor | Non
     return out
 
 
+def paged_attn_scratch_size(n_seqs: int, hq: int, hkv: int, max_ctx: int, head_dim: int = 128) -> int:
+    return int(_lib.load().dcg_paged_attn_scratch_size(n_seqs, hq, hkv, head_dim, max_ctx))
+
+
+def paged_attn_decode(q: torch.Tensor, k_arena: torch.Tensor, v_arena: torch.Tensor, n_layer: int,
+                      layer: int, block_tables: torch.Tensor, ctx_lens: torch.Tensor, hkv: int,
+                      max_ctx: int, scale: float | None = None, out: torch.Tensor | None = None,
+                      scratch: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode attention of one query token per sequence over the paged fp16 KV arena.
+
+    q [n_seqs, hq, 128] f32; k/v_arena fp16 (any shape, layout of dcgpu.h); block_tables
+    [n_seqs, max_blocks] int32; ctx_lens [n_seqs] int32 (<= max_ctx)."""
+    _check_cuda(q, "q", torch.float32)
+    for t, nm in ((k_arena, "k_arena"), (v_arena, "v_arena")):
+        _check_cuda(t, nm, torch.float16)
+    _check_cuda(block_tables, "block_tables", torch.int32)
+    _check_cuda(ctx_lens, "ctx_lens", torch.int32)
+    n_seqs, hq, hd = q.shape
+    if scale is None:
+        scale = 1.0 / float(hd) ** 0.5
+    if out is None:
+        out = torch.empty_like(q)
+    need = paged_attn_scratch_size(n_seqs, hq, hkv, max_ctx, hd)
+    if scratch is None:
+        scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+    _lib.check(_lib.load().dcg_paged_attn_decode(
+        _ptr(q), _ptr(k_arena), _ptr(v_arena), n_layer, layer, _ptr(block_tables),
+        block_tables.shape[1], _ptr(ctx_lens), n_seqs, hq, hkv, hd, max_ctx, scale, _ptr(out),
+        _ptr(scratch), scratch.numel(), _stream()), "dcg_paged_attn_decode")
+    return out
+
+
+def kv_append(k: torch.Tensor, v: torch.Tensor, k_arena: torch.Tensor, v_arena: torch.Tensor,
+              n_layer: int, layer: int, block_tables: torch.Tensor, seq_ids: torch.Tensor,
+              positions: torch.Tensor) -> None:
+    """Write n_tok tokens' K/V ([n_tok, hkv, hd] f32) into their fp16 slots (in place)."""
+    for t, nm in ((k, "k"), (v, "v")):
+        _check_cuda(t, nm, torch.float32)
+    n_tok, hkv, hd = k.shape
+    _lib.check(_lib.load().dcg_kv_append(
+        _ptr(k), _ptr(v), _ptr(k_arena), _ptr(v_arena), n_layer, layer, _ptr(block_tables),
+        block_tables.shape[1], _ptr(seq_ids), _ptr(positions), n_tok, hkv, hd, _stream()),
+        "dcg_kv_append")
+
+
 class HostContext:
     """The synchronous host boundary: weights registered once by host pointer, per-call host
     activations in and host results out (dcg_ctx_*)."""

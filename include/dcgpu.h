@@ -117,6 +117,36 @@ int dcg_mul_mat_noalloc(int type, const void* w, int64_t n, int64_t k, const flo
                         float* y, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
+ * Paged decode attention -- the attention op the runtime selector dispatches for a decode step
+ * (inference.cpp:1506-1573: scale = 1/sqrt(head_dim), softmax(q.K^T * scale).V, GQA with
+ * kv_head = h / (hq/hkv)), reading PagedKVCache's fp16 arena in place instead of cb_kv_manage's
+ * gather (inference.cpp:556-643).  One query token per sequence; sequence s attends to its own
+ * positions 0..ctx_lens[s]-1 (the current token already appended).
+ *   q            [n_seqs][hq][head_dim] f32
+ *   k/v_arena    fp16, element (block, layer, slot, head, dim) at
+ *                ((block*n_layer + layer)*16 + slot)*hkv*head_dim + head*head_dim + dim
+ *                (kv_cache.cpp:353-370, the declared WriteKSlot(block_id, layer, ...) order)
+ *   block_tables [n_seqs][max_blocks_per_seq] int32 physical block ids
+ *   ctx_lens     [n_seqs] int32, each <= max_ctx and <= 16*max_blocks_per_seq
+ *   out          [n_seqs][hq][head_dim] f32
+ * head_dim must be 128 and hq/hkv one of 1, 2, 4, 8.  scratch: dcg_paged_attn_scratch_size bytes
+ * (0 is valid when that size is 0), 256-B aligned.  All pointers are device pointers. */
+size_t dcg_paged_attn_scratch_size(int n_seqs, int hq, int hkv, int head_dim, int max_ctx);
+int dcg_paged_attn_decode(const float* q, const void* k_arena, const void* v_arena, int n_layer,
+                          int layer, const int32_t* block_tables, int max_blocks_per_seq,
+                          const int32_t* ctx_lens, int n_seqs, int hq, int hkv, int head_dim,
+                          int max_ctx, float scale, float* out, void* scratch, size_t scratch_bytes,
+                          void* stream);
+
+/* KV append -- PagedKVCache::WriteKSlot / WriteVSlot (kv_cache.cpp:566-598) for n_tok tokens at
+ * once: token i (k, v: [n_tok][hkv][head_dim] f32) goes to slot positions[i] of sequence
+ * seq_ids[i] through its block table, converted to fp16 (round to nearest even). */
+int dcg_kv_append(const float* k, const float* v, void* k_arena, void* v_arena, int n_layer,
+                  int layer, const int32_t* block_tables, int max_blocks_per_seq,
+                  const int32_t* seq_ids, const int32_t* positions, int n_tok, int hkv,
+                  int head_dim, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
  * Host boundary (drop-in for the CPU call sites; synchronous).
  * ------------------------------------------------------------------------------------------- */
 typedef struct dcg_ctx dcg_ctx;
