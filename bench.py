@@ -173,8 +173,10 @@ def run_ours(args):
         ring.append(pair)
     xs = [torch.randn((1, k), generator=gen, device=dev) for _, k in SHAPES]
     ys = [torch.empty((1, n), device=dev) for n, _ in SHAPES]
-    scr = [torch.empty(ops.mul_mat_scratch_size(Q4_K, 1, k), dtype=torch.uint8, device=dev)
-           for _, k in SHAPES]
+    scr = [torch.empty(ops.mul_mat_scratch_size(Q4_K, n, k, 1), dtype=torch.uint8, device=dev)
+           for n, k in SHAPES]
+    qscr = [torch.zeros(max(1, ops.mul_mat_q_scratch_size(Q4_K, n, k, 1)), dtype=torch.uint8,
+                        device=dev) for n, k in SHAPES]
     acts = [ops.quantize_act(x, Q8_K) for x in xs]
     torch.cuda.synchronize()
 
@@ -186,7 +188,7 @@ def run_ours(args):
     def gemv_pass():          # the GEMV kernels alone, same weights
         for s in range(RING):
             for j in range(2):
-                ops.mul_mat_q(ring[s][j], acts[j], 1, out=ys[j])
+                ops.mul_mat_q(ring[s][j], acts[j], 1, out=ys[j], scratch=qscr[j])
 
     # CUDA graphs: one ring pass per replay (launch overhead off the timed path)
     side = torch.cuda.Stream(device=dev)

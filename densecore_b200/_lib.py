@@ -10,7 +10,7 @@ import re
 
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
-LIB_PATH = os.path.join(PKG, "libdcgpu.so")
+LIB_PATH = os.environ.get("DCG_LIB_PATH") or os.path.join(PKG, "libdcgpu.so")
 HEADER = os.path.join(ROOT, "include", "dcgpu.h")
 
 _lib = None
@@ -26,7 +26,8 @@ SIGNATURES = {
     "dcg_device_error": (i32, [ctypes.POINTER(i32), i32]),
     "dcg_row_size": (sz, [i32, i64]),
     "dcg_packed_weight_size": (sz, [i32, i64, i64]),
-    "dcg_mul_mat_scratch_size": (sz, [i32, i64, i64]),
+    "dcg_mul_mat_scratch_size": (sz, [i32, i64, i64, i64]),
+    "dcg_mul_mat_q_scratch_size": (sz, [i32, i64, i64, i64]),
     "dcg_quantize_row_q8_0": (i32, [vp, vp, i64, i64, vp]),
     "dcg_quantize_row_q8_K": (i32, [vp, vp, i64, i64, vp]),
     "dcg_quantize_weights": (i32, [i32, vp, vp, i64, i64, vp]),
@@ -35,7 +36,7 @@ SIGNATURES = {
     "dcg_mul_mat": (i32, [i32, vp, i64, i64, vp, i64, vp, vp, sz, vp]),
     "dcg_act_size": (sz, [i32, i64, i64]),
     "dcg_quantize_act": (i32, [i32, vp, vp, i64, i64, vp]),
-    "dcg_mul_mat_q": (i32, [i32, vp, i64, i64, vp, i64, vp, vp]),
+    "dcg_mul_mat_q": (i32, [i32, vp, i64, i64, vp, i64, vp, vp, sz, vp]),
     "dcg_mul_mat_noalloc": (i32, [i32, vp, i64, i64, vp, i64, vp, vp]),
     "dcg_paged_attn_scratch_size": (sz, [i32, i32, i32, i32, i32]),
     "dcg_paged_attn_decode": (i32, [vp, vp, vp, i32, i32, vp, i32, vp, i32, i32, i32, i32, i32, f32,

@@ -50,6 +50,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) paged_attn_split_kernel(
     __shared__ float wm[ATT_WARPS][NREP], wl[ATT_WARPS][NREP];
     __shared__ __align__(16) float wacc[ATT_WARPS][NREP][HD];
 
+    pdl_wait();
     const int seq = blockIdx.x / hkv, kvh = blockIdx.x % hkv, split = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int L = ctx[seq];
@@ -142,6 +143,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) paged_attn_split_kernel(
         }
         __syncwarp();
     }
+    pdl_trigger();
     // ---- merge the warps ----
 #pragma unroll
     for (int r = 0; r < NREP; r++) {
@@ -178,6 +180,8 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) paged_attn_split_kernel(
 // out[seq][h][:] = sum_s O_s 2^(m_s - M) / sum_s l_s 2^(m_s - M); one CTA of 128 threads per (seq, h)
 __global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
                                     float* __restrict__ out, int hq, int hkv, int nrep, int splits) {
+    pdl_wait();
+    pdl_trigger();
     const int seq = blockIdx.x / hq, h = blockIdx.x % hq;
     const int kvh = h / nrep, r = h % nrep;
     const int dd = threadIdx.x;
@@ -209,6 +213,8 @@ __global__ void kv_append_kernel(const float* __restrict__ k, const float* __res
                                  int layer, const int* __restrict__ bt, int mbs,
                                  const int* __restrict__ seq_ids, const int* __restrict__ pos,
                                  int n_tok, int hkv, int hd) {
+    pdl_wait();
+    pdl_trigger();
     const int per = hkv * hd;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)n_tok * per) return;
@@ -252,10 +258,10 @@ cudaError_t launch_paged_attn(const float* q, const void* karena, const void* va
     const __half* K = (const __half*)karena;
     const __half* V = (const __half*)varena;
     float* direct = splits == 1 ? out : nullptr;
+    cudaError_t e = cudaSuccess;
 #define DCG_ATT(NR)                                                                                  \
-    paged_attn_split_kernel<NR><<<grid, ATT_WARPS * 32, 0, st>>>(q, K, V, n_layer, layer, bt, mbs,   \
-                                                                 ctx, hq, hkv, sl2, bps, splits, po, \
-                                                                 pml, direct)
+    e = launch_pdl(paged_attn_split_kernel<NR>, grid, dim3(ATT_WARPS * 32), 0, st, q, K, V, n_layer, \
+                   layer, bt, mbs, ctx, hq, hkv, sl2, bps, splits, po, pml, direct)
     switch (nrep) {
         case 1: DCG_ATT(1); break;
         case 2: DCG_ATT(2); break;
@@ -264,10 +270,9 @@ cudaError_t launch_paged_attn(const float* q, const void* karena, const void* va
         default: return cudaErrorInvalidValue;
     }
 #undef DCG_ATT
-    cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || splits == 1) return e;
-    attn_combine_kernel<<<n_seqs * hq, HD, 0, st>>>(po, pml, out, hq, hkv, nrep, splits);
-    return cudaGetLastError();
+    return launch_pdl(attn_combine_kernel, dim3(n_seqs * hq), dim3(HD), 0, st, (const float*)po,
+                      (const float*)pml, out, hq, hkv, nrep, splits);
 }
 
 cudaError_t launch_kv_append(const float* k, const float* v, void* karena, void* varena, int n_layer,
@@ -275,9 +280,8 @@ cudaError_t launch_kv_append(const float* k, const float* v, void* karena, void*
                              int n_tok, int hkv, int hd, cudaStream_t st) {
     const int64_t total = (int64_t)n_tok * hkv * hd;
     if (total == 0) return cudaSuccess;
-    kv_append_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
-        k, v, (__half*)karena, (__half*)varena, n_layer, layer, bt, mbs, seq_ids, pos, n_tok, hkv, hd);
-    return cudaGetLastError();
+    return launch_pdl(kv_append_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, k, v,
+                      (__half*)karena, (__half*)varena, n_layer, layer, bt, mbs, seq_ids, pos, n_tok, hkv, hd);
 }
 
 }  // namespace dcg

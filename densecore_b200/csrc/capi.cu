@@ -49,14 +49,31 @@ void set_error(const std::string& m) { g_last_error = m; }
 // ------------------------------------------------------------------------------------------
 // internal: enqueue quantize + GEMV chunks (no checks beyond shapes; scratch already sized)
 // ------------------------------------------------------------------------------------------
-static int enqueue_mul_mat(int type, const void* w, int64_t n, int64_t k, const float* x,
-                           int64_t m, float* y, void* scratch, cudaStream_t st) {
-    DCG_CUDA(dcg::launch_quantize_act(act_type_of(type), x, scratch, m, k, true, st), "quantize");
+// scratch of dcg_mul_mat: [quantized activation | qmm tickets + split-K partials]
+static size_t qmm_part(int type, int64_t n, int64_t k, int64_t m) {
+    return dcg::qmm_supports(type) ? dcg::qmm_scratch_bytes(type, n, k, m) : 0;
+}
+
+static int enqueue_mul_mat_q(int type, const void* w, int64_t n, int64_t k, const void* act, int64_t m,
+                             float* y, void* qscratch, cudaStream_t st) {
+    if (dcg::qmm_supports(type)) {
+        DCG_CUDA(dcg::launch_qmm(type, w, n, k, act, m, y, qscratch, st), "qmm");
+        return DCG_OK;
+    }
     for (int64_t m0 = 0; m0 < m; m0 += 8) {
         const int64_t mc = (m - m0) < 8 ? (m - m0) : 8;
-        DCG_CUDA(dcg::launch_gemv(type, w, n, k, scratch, m, m0, mc, y, st), "gemv");
+        DCG_CUDA(dcg::launch_gemv(type, w, n, k, act, m, m0, mc, y, st), "gemv");
     }
     return DCG_OK;
+}
+
+static int enqueue_mul_mat(int type, const void* w, int64_t n, int64_t k, const float* x,
+                           int64_t m, float* y, void* scratch, cudaStream_t st) {
+    void* qs = (uint8_t*)scratch + dcg::act_bytes(act_type_of(type), m, k);
+    const int nt = dcg::qmm_supports(type) ? dcg::qmm_ticket_count(type, n, m) : 0;
+    DCG_CUDA(dcg::launch_quantize_act(act_type_of(type), x, scratch, m, k, true, st, (int*)qs, nt),
+             "quantize");
+    return enqueue_mul_mat_q(type, w, n, k, scratch, m, y, qs, st);
 }
 
 extern "C" {
@@ -94,9 +111,14 @@ size_t dcg_packed_weight_size(int type, int64_t n, int64_t k) {
     return dcg::packed_weight_bytes(type, n, k);
 }
 
-size_t dcg_mul_mat_scratch_size(int type, int64_t m, int64_t k) {
-    if (!weight_type_ok(type)) return 0;
-    return dcg::act_bytes(act_type_of(type), m, k);
+size_t dcg_mul_mat_scratch_size(int type, int64_t n, int64_t k, int64_t m) {
+    if (!weight_type_ok(type) || n < 0 || k <= 0 || m < 0) return 0;
+    return dcg::act_bytes(act_type_of(type), m, k) + qmm_part(type, n, k, m);
+}
+
+size_t dcg_mul_mat_q_scratch_size(int type, int64_t n, int64_t k, int64_t m) {
+    if (!weight_type_ok(type) || n < 0 || k <= 0 || m < 0) return 0;
+    return qmm_part(type, n, k, m);
 }
 
 static int quantize_rows(int act_type, const float* x, void* y, int64_t m, int64_t k, void* stream) {
@@ -157,7 +179,7 @@ int dcg_mul_mat(int type, const void* w, int64_t n, int64_t k, const float* x, i
     if (!w || !x || !y || !scratch) return fail(DCG_EINVAL, "null pointer");
     if (!aligned(w, 256) || !aligned(scratch, 256)) return fail(DCG_EINVAL, "w and scratch must be 256-byte aligned");
     if (!aligned(x, 16) || !aligned(y, 4)) return fail(DCG_EINVAL, "x must be 16-byte aligned, y 4-byte aligned");
-    const size_t need = dcg_mul_mat_scratch_size(type, m, k);
+    const size_t need = dcg_mul_mat_scratch_size(type, n, k, m);
     if (scratch_bytes < need)
         return fail(DCG_ESCRATCH, "scratch needs " + std::to_string(need) + " bytes, got " + std::to_string(scratch_bytes));
     return enqueue_mul_mat(type, w, n, k, x, m, y, scratch, (cudaStream_t)stream);
@@ -165,7 +187,10 @@ int dcg_mul_mat(int type, const void* w, int64_t n, int64_t k, const float* x, i
 
 int dcg_device_error(int* code, int clear) {
     if (!code) return fail(DCG_EINVAL, "null pointer");
-    DCG_CUDA(dcg::gemv_device_error(code, clear != 0), "read device error flag");
+    int a = 0, b = 0;
+    DCG_CUDA(dcg::gemv_device_error(&a, clear != 0), "read device error flag");
+    DCG_CUDA(dcg::qmm_device_error(&b, clear != 0), "read device error flag");
+    *code = a ? a : b;
     return DCG_OK;
 }
 
@@ -235,18 +260,18 @@ int dcg_quantize_act(int act_type, const float* x, void* act, int64_t m, int64_t
 }
 
 int dcg_mul_mat_q(int type, const void* w, int64_t n, int64_t k, const void* act, int64_t m,
-                  float* y, void* stream) {
+                  float* y, void* scratch, size_t scratch_bytes, void* stream) {
     int rc = check_shape(type, n, k);
     if (rc) return rc;
     if (m < 0) return fail(DCG_EINVAL, "m < 0");
     if (m == 0 || n == 0) return DCG_OK;
     if (!w || !act || !y) return fail(DCG_EINVAL, "null pointer");
     if (!aligned(w, 256) || !aligned(act, 256) || !aligned(y, 4)) return fail(DCG_EINVAL, "misaligned buffer");
-    for (int64_t m0 = 0; m0 < m; m0 += 8) {
-        const int64_t mc = (m - m0) < 8 ? (m - m0) : 8;
-        DCG_CUDA(dcg::launch_gemv(type, w, n, k, act, m, m0, mc, y, (cudaStream_t)stream), "gemv");
-    }
-    return DCG_OK;
+    const size_t need = qmm_part(type, n, k, m);
+    if (need && (!scratch || scratch_bytes < need))
+        return fail(DCG_ESCRATCH, "mul_mat_q scratch needs " + std::to_string(need) + " bytes");
+    if (need && !aligned(scratch, 256)) return fail(DCG_EINVAL, "scratch must be 256-byte aligned");
+    return enqueue_mul_mat_q(type, w, n, k, act, m, y, scratch, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -10,12 +10,15 @@
 //   Q6_K : payload [n][k/256][208 B = ql|qh|scales], then fp16 d [n][k/256].
 // Device activation layout (written by the quantize kernels for mul_mat):
 //   Q8_0 act : qs [m][k] int8, then fp16 d [m][k/32].
-//   Q8_K act : qs [m][k] int8, then f32 d [m][k/256], then int16 bsums [m][k/16].
+//   Q8_K act : qs [m][k] int8, then f32 d [m][k/256], then int16 bsums [m][k/16], then int16
+//              bsums32 [m][k/32] (sums of 32: bsums[2j] + bsums[2j+1], the Q4_K min-term operand).
 // Every region starts on a 256-B boundary so every payload load is an aligned 16-B vector.
 #pragma once
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <utility>
 
 #define DCG_TYPE_F32 0
 #define DCG_TYPE_F16 1
@@ -75,11 +78,13 @@ struct ActQ {
     int8_t* qs;      // [m][k]
     void* d;         // fp16 [m][k/32] (Q8_0) or f32 [m][k/256] (Q8_K)
     int16_t* bsums;  // [m][k/16] (Q8_K only)
+    int16_t* bs32;   // [m][k/32] (Q8_K only)
 };
 __host__ __device__ inline size_t act_bytes(int act_type, int64_t m, int64_t k) {
     size_t q = align256((size_t)m * k);
     if (act_type == DCG_TYPE_Q8_0) return q + align256((size_t)m * (k / QK8_0) * 2);
-    return q + align256((size_t)m * (k / QK_K) * 4) + align256((size_t)m * (k / 16) * 2);
+    return q + align256((size_t)m * (k / QK_K) * 4) + align256((size_t)m * (k / 16) * 2) +
+           align256((size_t)m * (k / 32) * 2);
 }
 __host__ __device__ inline ActQ act_view(int act_type, void* base, int64_t m, int64_t k) {
     ActQ a;
@@ -89,9 +94,12 @@ __host__ __device__ inline ActQ act_view(int act_type, void* base, int64_t m, in
     a.d = p;
     if (act_type == DCG_TYPE_Q8_0) {
         a.bsums = nullptr;
+        a.bs32 = nullptr;
     } else {
         p += align256((size_t)m * (k / QK_K) * 4);
         a.bsums = (int16_t*)p;
+        p += align256((size_t)m * (k / 16) * 2);
+        a.bs32 = (int16_t*)p;
     }
     return a;
 }
@@ -123,6 +131,32 @@ __device__ __forceinline__ void q4k_scale_min(uint32_t s0, uint32_t s1, uint32_t
         sc = (b8 & 0xF) | (((s0 >> (8 * jj + 6)) & 3) << 4);
         m = (b8 >> 4) | (((s1 >> (8 * jj + 6)) & 3) << 4);
     }
+}
+
+// ---- programmatic dependent launch (PDL) ----
+// pdl_wait: block until the grid this one depends on has completed and its writes are visible
+// (a no-op when the kernel was not launched as a programmatic dependent).  pdl_trigger: allow the
+// next kernel in the stream to start launching.  Every kernel here calls pdl_wait before it reads
+// or writes any buffer another kernel produces or consumes; only constant weights are touched
+// before it.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// launch with the programmatic-stream-serialization attribute (kernel may overlap its predecessor)
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 }  // namespace dcg

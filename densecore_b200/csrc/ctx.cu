@@ -175,7 +175,7 @@ int dcg_ctx_mul_mat(dcg_ctx* c, dcg_weight* w, const float* x_host, int64_t m, f
     DeviceGuard g(c->device);
     std::lock_guard<std::mutex> lk(c->mu);
     const size_t xb = dcg::align256((size_t)m * w->k * 4), yb = dcg::align256((size_t)m * w->n * 4);
-    const size_t qb = dcg_mul_mat_scratch_size(w->type, m, w->k);
+    const size_t qb = dcg_mul_mat_scratch_size(w->type, w->n, w->k, m);
     int rc = grow(c, xb + qb + yb, xb + yb);
     if (rc) return rc;
     uint8_t* dx = (uint8_t*)c->scratch;

@@ -141,6 +141,8 @@ __device__ __forceinline__ float lane_dot(const WReg& r, const ActQ& a, int64_t 
 template <int TYPE, int M, int R>
 __global__ void __launch_bounds__(256) gemv_kernel(PackedW w, int64_t n, int64_t k, ActQ a,
                                                    int m0, float* __restrict__ y, int S) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int PER = UnitInfo<TYPE>::BLOCKS;
     constexpr int U = 2;  // units in flight per warp
     __shared__ float red[8][R * M];
@@ -228,6 +230,8 @@ constexpr int TMA_TILE = 24 * 1024;  // bytes per stage; 2 CTAs (2 x ~97 KB) fit
 template <int TYPE, int M>
 __global__ void __launch_bounds__(256, 2) gemv_tma_kernel(PackedW w, int64_t n, int64_t k, ActQ a,
                                                           int m0, float* __restrict__ y, int TR) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int PER = UnitInfo<TYPE>::BLOCKS;
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = (uint64_t*)smem;                                    // [STAGES]
@@ -410,6 +414,8 @@ constexpr int XR_CTAS = 3;
 template <int TYPE, int M, int UW>
 __global__ void __launch_bounds__(256, (UW <= 4 ? XR_CTAS : 2)) gemv_tma_xr_kernel(PackedW w, int64_t n, int64_t k, ActQ a,
                                                              int m0, float* __restrict__ y, int TR) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int PER = UnitInfo<TYPE>::BLOCKS;
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = (uint64_t*)smem;
@@ -537,8 +543,8 @@ static cudaError_t launch_xr(const PackedW& w, int64_t n, int64_t k, const ActQ&
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
-    gemv_tma_xr_kernel<TYPE, M, UW><<<(unsigned)grid, 256, smem, st>>>(w, n, k, a, m0, y, TR);
-    return cudaGetLastError();
+    return launch_pdl(gemv_tma_xr_kernel<TYPE, M, UW>, dim3((unsigned)grid), dim3(256), smem, st, w, n, k, a,
+                      m0, y, TR);
 }
 
 static int g_num_sms = 0;
@@ -588,8 +594,8 @@ static cudaError_t launch_gemv_tma_t(const PackedW& w, int64_t n, int64_t k, con
     while (TR * 2 * (int64_t)w.row_bytes <= TMA_TILE && TR < 64) TR *= 2;
     const int64_t n_tiles = (n + TR - 1) / TR;
     const int64_t grid = std::min<int64_t>(n_tiles, (int64_t)num_sms * 2);
-    gemv_tma_kernel<TYPE, M><<<(unsigned)grid, 256, smem, st>>>(w, n, k, a, m0, y, TR);
-    return cudaGetLastError();
+    return launch_pdl(gemv_tma_kernel<TYPE, M>, dim3((unsigned)grid), dim3(256), smem, st, w, n, k, a, m0, y,
+                      TR);
 }
 
 template <int TYPE, int M>
@@ -606,8 +612,7 @@ static cudaError_t launch_gemv_t(const PackedW& w, int64_t n, int64_t k, const A
         S *= 2;
     }
     const int64_t ctas = (n + (8 / S) * R - 1) / ((8 / S) * R);
-    gemv_kernel<TYPE, M, R><<<(unsigned)ctas, 256, 0, st>>>(w, n, k, a, m0, y, S);
-    return cudaGetLastError();
+    return launch_pdl(gemv_kernel<TYPE, M, R>, dim3((unsigned)ctas), dim3(256), 0, st, w, n, k, a, m0, y, S);
 }
 
 template <int TYPE>

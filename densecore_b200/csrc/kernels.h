@@ -5,8 +5,9 @@
 
 namespace dcg {
 
+// also zeroes zero[0 .. nzero) (the matmul's split-K tickets) in the same launch
 cudaError_t launch_quantize_act(int act_type, const float* x, void* y, int64_t m, int64_t k,
-                                bool soa, cudaStream_t st);
+                                bool soa, cudaStream_t st, int* zero = nullptr, int nzero = 0);
 cudaError_t launch_encode_weights(int type, const float* x, void* y, int64_t n, int64_t k,
                                   cudaStream_t st);
 cudaError_t launch_pack(int type, const void* src, size_t src_stride, void* dst, int64_t n,
@@ -15,6 +16,15 @@ cudaError_t launch_pack(int type, const void* src, size_t src_stride, void* dst,
 // y[m][n] = W[n] . act[m]; act in the SoA activation layout; m <= 8 per launch.
 cudaError_t launch_gemv(int type, const void* packed_w, int64_t n, int64_t k, const void* act,
                         int64_t act_m, int64_t m0, int64_t m, float* y, cudaStream_t st);
+
+// tensor-core quantized matmul (qmm.cu); cudaErrorNotSupported for types it does not cover
+size_t qmm_scratch_bytes(int type, int64_t n, int64_t k, int64_t m);
+// ints at the start of the qmm scratch that must be zero when a qmm launch starts (left zero)
+int qmm_ticket_count(int type, int64_t n, int64_t m);
+cudaError_t launch_qmm(int type, const void* packed_w, int64_t n, int64_t k, const void* act,
+                       int64_t m, float* y, void* scratch, cudaStream_t st);
+cudaError_t qmm_device_error(int* out, bool clear);
+bool qmm_supports(int type);
 
 // paged decode attention (attn.cu)
 void attn_plan(int n_seqs, int hkv, int max_ctx, int* splits, int* bps);

@@ -1,0 +1,610 @@
+// qmm.cu -- quantized weight x quantized activation matmul on the int8 tensor cores
+// (mma.sync m16n8k32 s8 -> s32), for every M: the decode GEMV (M < 16) and the batched-decode /
+// prefill GEMM.  Replaces cb_gemv_custom's vec_dot row loop and ggml_mul_mat
+// (core/src/inference.cpp:840-948, :1063, :1794-1797, :1817).
+//
+// Tiling.  A CTA (4 warps) owns 64 weight rows (16 per warp: the mma's M dimension) and 8*NT
+// activation rows (NT mma n-tiles), over a contiguous range of K super-blocks (split-K when the
+// row blocks alone cannot fill the GPU).  K is streamed in chunks of KS super-blocks: each chunk
+// is one bulk copy (TMA) per weight row into a padded shared-memory row (stride = 32 mod 128 B,
+// so the fragment loads are bank-conflict free), STAGES chunks in flight on mbarriers.
+//
+// Fragments.  The products of one 32-element sub-block are an m16n8k32 mma.  The mma's k order
+// is a permutation of the sub-block's elements chosen so that lane (gid, tig) reads its A
+// registers {a0,a2} from 8 consecutive bytes of weight row gid (and {a1,a3} from row gid+8) and
+// its B registers from 8 consecutive activation bytes: mma k slots 4*tig..+3 <-> elements
+// 8*tig..+3, slots 16+4*tig..+3 <-> elements 8*tig+4..+7.  Q4_K's sub-blocks 2g and 2g+1 share
+// their 32 bytes (low / high nibbles), so one 8-byte load per row feeds two mmas.
+//
+// Scales.  Each mma result (exact int32 dot of one sub-block) is multiplied by its 6-bit
+// sub-block scale and summed in int32 over the super-block; the Q4_K min term
+// sum_j m_j * bsum32_j uses dp2a on the packed 6-bit mins and the pair-summed Q8_K block sums;
+// then y += dx * (d * isum - dmin * msum) in fp32 once per super-block.
+//
+// Split-K partials go to scratch; the last CTA of a tile (atomic ticket) adds them in split order,
+// so results are deterministic.  Tickets must be zero when a launch starts and are left zero
+// (dcg_mul_mat clears them inside its activation-quantize launch).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tma.cuh"
+
+#include <algorithm>
+#include <mutex>
+
+namespace dcg {
+
+__device__ int g_qmm_error = 0;
+
+cudaError_t qmm_device_error(int* out, bool clear) {
+    cudaError_t e = cudaMemcpyFromSymbol(out, g_qmm_error, sizeof(int));
+    if (e == cudaSuccess && clear && *out) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(g_qmm_error, &zero, sizeof(int));
+    }
+    return e;
+}
+
+constexpr int QMM_ROWS = 64;     // weight rows per CTA
+constexpr int QMM_THREADS = 256;
+constexpr int QMM_WARPS = 8;     // 4 row groups of 16 x 2 halves of each super-block
+constexpr int QMM_KS = 2;        // super-blocks per stage
+constexpr int QMM_STAGES = 3;
+constexpr int Q4K_SROW = QMM_KS * Q4_K_BYTES;         // 288 B = 32 mod 128: conflict-free rows
+constexpr int QMM_XROW = QMM_KS * QK_K + 32;          // 544 B = 32 mod 128
+constexpr int QMM_W_BYTES = QMM_ROWS * Q4K_SROW;      // weight part of a stage
+// xc = activation rows staged per CTA (8*NT, or 1 for the M == 1 kernel)
+__host__ __device__ constexpr int qmm_stage_bytes(int xc) {
+    return QMM_W_BYTES + ((xc * QMM_XROW + xc * QMM_KS * 16 + 127) & ~127);
+}
+
+__device__ __forceinline__ void mma_s8(int* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                       uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ int byte_of(uint32_t w, int j) {  // zero-extended byte j (0..3)
+    return (int)__byte_perm(w, 0u, 0x4440u + (uint32_t)j);
+}
+
+// packed Q4_K 6-bit scales / mins of one block header (ggml get_scale_min_k4, 4 per word)
+struct Q4kScales {
+    uint32_t sc03, sc47, mn03, mn47;
+};
+__device__ __forceinline__ Q4kScales q4k_unpack(const uint4& h) {
+    Q4kScales s;
+    s.sc03 = h.y & 0x3F3F3F3Fu;
+    s.mn03 = h.z & 0x3F3F3F3Fu;
+    s.sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+    s.mn47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+    return s;
+}
+
+// DUP (M == 1 only): the single activation row is fed to all 8 mma columns, so every lane's c0 / c2
+// already hold its two rows' results; only those are scaled and only tig == 0 lanes store.
+template <int NT, bool DUP>
+__global__ void __launch_bounds__(QMM_THREADS, NT >= 4 ? 1 : (NT >= 2 ? 2 : 3))
+    qmm_q4k_kernel(const __grid_constant__ CUtensorMap wmap, int nb, int64_t n, ActQ a,
+                   int64_t k, int m, float* __restrict__ y, float* __restrict__ part,
+                   int* __restrict__ tickets, int S, int sps) {
+    constexpr int XC = DUP ? 1 : 8 * NT;          // activation rows staged per CTA
+    constexpr int SB_BYTES = qmm_stage_bytes(XC);
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = (uint64_t*)smem;             // [STAGES] bulk copies landed
+    uint64_t* empty = full + QMM_STAGES;          // [STAGES] all warps done with the stage
+    int* flag = (int*)(smem + 96);
+    uint8_t* buf = smem + 128;
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gid = lane >> 2, tig = lane & 3;
+    const int rg = warp & 3;   // row group: rows 16*rg .. +15 of the CTA
+    const int gh = warp >> 2;  // sub-block pairs g = 2*gh, 2*gh+1 (sub-blocks 4*gh .. 4*gh+3)
+    const int64_t r0 = (int64_t)blockIdx.x * QMM_ROWS;
+    const int c0 = blockIdx.y * XC;
+    const int split = blockIdx.z;
+    const int sb0 = split * sps, sb1 = min(nb, sb0 + sps);
+    const int nchunks = (sb1 - sb0 + QMM_KS - 1) / QMM_KS;
+    const int rows_here = (int)((n - r0) < QMM_ROWS ? (n - r0) : QMM_ROWS);
+    const int cols_here = min(XC, m - c0);
+
+    pdl_wait();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < QMM_STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], QMM_WARPS);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    // warp 0: weight rows, activation rows and their Q8_K pair sums of chunk c -> stage c % STAGES
+    auto issue = [&](int c) -> bool {
+        const int st = c % QMM_STAGES;
+        if (c >= QMM_STAGES && !mbar_wait(&empty[st], (uint32_t)(((c / QMM_STAGES) - 1) & 1), &g_qmm_error))
+            return false;
+        const int sbc = sb0 + c * QMM_KS;
+        const int nsb = min(QMM_KS, sb1 - sbc);
+        const uint32_t xb = (uint32_t)(nsb * QK_K), bb = (uint32_t)(nsb * 16);
+        uint8_t* dst = buf + (size_t)st * SB_BYTES;
+        // the weight box is always QMM_ROWS x QMM_KS blocks (rows past n / blocks past the row's end
+        // are zero-filled and still counted)
+        if (lane == 0) mbar_arrive_expect_tx(&full[st], (uint32_t)QMM_W_BYTES + (xb + bb) * cols_here);
+        __syncwarp();
+        fence_proxy_async_smem();
+        if (lane == 0) tma_load_2d(dst, &wmap, sbc * (Q4_K_BYTES / 4), (int)r0, &full[st]);
+        for (int cc = lane; cc < cols_here; cc += 32) {
+            const int col = c0 + cc;
+            bulk_g2s(dst + QMM_W_BYTES + cc * QMM_XROW, a.qs + (size_t)col * k + (size_t)sbc * QK_K, xb, &full[st]);
+            bulk_g2s(dst + QMM_W_BYTES + XC * QMM_XROW + cc * (QMM_KS * 16),
+                     a.bs32 + (size_t)col * (k / 32) + (size_t)sbc * 8, bb, &full[st]);
+        }
+        return true;
+    };
+    bool ok = true;
+    if (warp == 0)
+        for (int c = 0; c < QMM_STAGES - 1 && c < nchunks; c++) ok = issue(c) && ok;
+
+    float yacc[NT][4];
+#pragma unroll
+    for (int t = 0; t < NT; t++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) yacc[t][i] = 0.0f;
+
+    const int nb_act = (int)(k / QK_K);
+    const float* xd = (const float*)a.d;
+    for (int c = 0; c < nchunks && ok; c++) {
+        if (warp == 0 && c + QMM_STAGES - 1 < nchunks) ok = issue(c + QMM_STAGES - 1) && ok;
+        const int sbc = sb0 + c * QMM_KS;
+        const int nsb = min(QMM_KS, sb1 - sbc);
+        // activation block scales of this chunk (global; overlaps the wait)
+        float dxr[QMM_KS][NT][2];
+#pragma unroll
+        for (int s = 0; s < QMM_KS; s++)
+#pragma unroll
+            for (int t = 0; t < NT; t++)
+#pragma unroll
+                for (int cc = 0; cc < 2; cc++) {
+                    const int col = DUP ? c0 : c0 + t * 8 + 2 * tig + cc;
+                    dxr[s][t][cc] = (s < nsb && col < m) ? __ldg(&xd[(size_t)col * nb_act + sbc + s]) : 0.0f;
+                }
+        ok = mbar_wait(&full[c % QMM_STAGES], (uint32_t)((c / QMM_STAGES) & 1), &g_qmm_error) && ok;
+        if (!ok) break;
+        const uint8_t* stage = buf + (size_t)(c % QMM_STAGES) * SB_BYTES;
+        const uint8_t* xs = stage + QMM_W_BYTES;
+        const int16_t* bss = (const int16_t*)(stage + QMM_W_BYTES + XC * QMM_XROW);
+#ifndef DCG_QMM_NOCOMPUTE
+        // both super-blocks of the chunk, unconditionally (ILP): one that is absent (zero-filled by
+        // the tensor copy) or belongs to the next split has dx = 0 and adds nothing
+#pragma unroll
+        for (int s = 0; s < QMM_KS; s++) {
+            const uint8_t* rowA = stage + (rg * 16 + gid) * Q4K_SROW + s * Q4_K_BYTES;
+            const uint8_t* rowB = rowA + 8 * Q4K_SROW;
+            const uint4 hA = *(const uint4*)rowA, hB = *(const uint4*)rowB;
+            const Q4kScales sA = q4k_unpack(hA), sB = q4k_unpack(hB);
+            int isum[NT][4];
+#pragma unroll
+            for (int t = 0; t < NT; t++)
+#pragma unroll
+                for (int i = 0; i < 4; i++) isum[t][i] = 0;
+#pragma unroll
+            for (int gg = 0; gg < 2; gg++) {
+                const int g = 2 * gh + gg;
+                const uint2 wA = *(const uint2*)(rowA + 16 + 32 * g + 8 * tig);
+                const uint2 wB = *(const uint2*)(rowB + 16 + 32 * g + 8 * tig);
+                const uint32_t lo0 = wA.x & 0x0F0F0F0Fu, lo1 = wB.x & 0x0F0F0F0Fu;
+                const uint32_t lo2 = wA.y & 0x0F0F0F0Fu, lo3 = wB.y & 0x0F0F0F0Fu;
+                const uint32_t hi0 = (wA.x >> 4) & 0x0F0F0F0Fu, hi1 = (wB.x >> 4) & 0x0F0F0F0Fu;
+                const uint32_t hi2 = (wA.y >> 4) & 0x0F0F0F0Fu, hi3 = (wB.y >> 4) & 0x0F0F0F0Fu;
+                const uint32_t scw_A = gh == 0 ? sA.sc03 : sA.sc47, scw_B = gh == 0 ? sB.sc03 : sB.sc47;
+                const int sA0 = byte_of(scw_A, (2 * g) & 3), sA1 = byte_of(scw_A, (2 * g + 1) & 3);
+                const int sB0 = byte_of(scw_B, (2 * g) & 3), sB1 = byte_of(scw_B, (2 * g + 1) & 3);
+#pragma unroll
+                for (int t = 0; t < NT; t++) {
+                    uint2 x0 = make_uint2(0, 0), x1 = make_uint2(0, 0);
+                    if (DUP || t * 8 + gid < cols_here) {
+                        const uint8_t* xp = xs + (DUP ? 0 : (t * 8 + gid) * QMM_XROW) + s * QK_K + 64 * g + 8 * tig;
+                        x0 = *(const uint2*)xp;
+                        x1 = *(const uint2*)(xp + 32);
+                    }
+                    int c0v[4] = {0, 0, 0, 0}, c1v[4] = {0, 0, 0, 0};
+                    mma_s8(c0v, lo0, lo1, lo2, lo3, x0.x, x0.y);
+                    mma_s8(c1v, hi0, hi1, hi2, hi3, x1.x, x1.y);
+                    isum[t][0] += sA0 * c0v[0] + sA1 * c1v[0];
+                    isum[t][2] += sB0 * c0v[2] + sB1 * c1v[2];
+                    if (!DUP) {
+                        isum[t][1] += sA0 * c0v[1] + sA1 * c1v[1];
+                        isum[t][3] += sB0 * c0v[3] + sB1 * c1v[3];
+                    }
+                }
+            }
+            const float2 dA = __half22float2(*reinterpret_cast<const __half2*>(&hA.x));
+            const float2 dB = __half22float2(*reinterpret_cast<const __half2*>(&hB.x));
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+#pragma unroll
+                for (int cc = 0; cc < (DUP ? 1 : 2); cc++) {
+                    const int lc = DUP ? 0 : t * 8 + 2 * tig + cc;
+                    if (lc >= cols_here) continue;
+                    // this warp's half of the min term: sub-blocks 4*gh .. 4*gh+3
+                    const uint2 bs = *(const uint2*)(bss + lc * (QMM_KS * 8) + s * 8 + 4 * gh);
+                    const float dx = dxr[s][t][cc];
+                    const uint32_t mnA = gh == 0 ? sA.mn03 : sA.mn47, mnB = gh == 0 ? sB.mn03 : sB.mn47;
+                    const int mA = __dp2a_hi((int)bs.y, (int)mnA, __dp2a_lo((int)bs.x, (int)mnA, 0));
+                    const int mB = __dp2a_hi((int)bs.y, (int)mnB, __dp2a_lo((int)bs.x, (int)mnB, 0));
+                    yacc[t][cc] += dx * (dA.x * (float)isum[t][cc] - dA.y * (float)mA);
+                    yacc[t][2 + cc] += dx * (dB.x * (float)isum[t][2 + cc] - dB.y * (float)mB);
+                }
+            }
+        }
+#endif
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[c % QMM_STAGES]);
+    }
+    pdl_trigger();
+    ok = __syncthreads_and(ok);
+    if (!ok) return;
+    // combine the two super-block halves of each row group (stage buffers are free now)
+    float* red = (float*)buf;
+    if (gh == 1) {
+#pragma unroll
+        for (int t = 0; t < NT; t++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) red[((rg * NT + t) * 4 + i) * 32 + lane] = yacc[t][i];
+    }
+    __syncthreads();
+    const bool writer = gh == 0;  // the gh == 1 warps stay for the barriers below
+    if (writer) {
+#pragma unroll
+        for (int t = 0; t < NT; t++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) yacc[t][i] += red[((rg * NT + t) * 4 + i) * 32 + lane];
+    }
+
+    // ---- epilogue: c0/c1 -> row gid, cols 2tig,2tig+1; c2/c3 -> row gid+8 ----
+    const int64_t rowA = r0 + rg * 16 + gid, rowB = rowA + 8;
+    if (S == 1) {
+        if (!writer) return;
+#pragma unroll
+        for (int t = 0; t < NT; t++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int col = c0 + t * 8 + 2 * tig + (i & 1);
+                const int64_t row = i < 2 ? rowA : rowB;
+                if (DUP) {
+                    if (tig == 0 && (i & 1) == 0 && row < n) y[row] = yacc[t][i];
+                } else if (col < m && row < n) {
+                    y[(size_t)col * n + row] = yacc[t][i];
+                }
+            }
+        return;
+    }
+#pragma unroll
+    for (int t = 0; t < NT; t++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            if (!writer) break;
+            const int col = c0 + t * 8 + 2 * tig + (i & 1);
+            const int64_t row = i < 2 ? rowA : rowB;
+            if (DUP) {
+                if (tig == 0 && (i & 1) == 0 && row < n) part[(size_t)split * n + row] = yacc[t][i];
+            } else if (col < m && row < n) {
+                part[((size_t)split * m + col) * n + row] = yacc[t][i];
+            }
+        }
+    __threadfence();
+    __syncthreads();
+    int* ticket = &tickets[blockIdx.x * gridDim.y + blockIdx.y];
+    if (threadIdx.x == 0) *flag = (atomicAdd(ticket, 1) == S - 1);
+    __syncthreads();
+    if (!*flag) return;
+    __threadfence();
+    for (int i = threadIdx.x; i < cols_here * rows_here; i += blockDim.x) {
+        const int col = c0 + i / rows_here;
+        const int64_t row = r0 + i % rows_here;
+        float sum = 0.0f;
+        for (int q = 0; q < S; q++) sum += __ldcg(&part[((size_t)q * m + col) * n + row]);
+        y[(size_t)col * n + row] = sum;
+    }
+    if (threadIdx.x == 0) *ticket = 0;
+}
+
+// ------------------------------------------------------------------------------------------
+// M == 1 (decode GEMV): the mma's 8 columns carry the 8 sub-blocks of a super-block.
+// k slots 4*tig..+3 of an mma hold 4 elements of sub-block 2*tig (low nibbles of qs pair group
+// tig), slots 16+4*tig..+3 the same 4 elements of sub-block 2*tig+1 (high nibbles of the same
+// bytes).  B column c carries the activation of sub-block c in exactly those slots and zeros
+// elsewhere, so 8 chained mmas (elements 4i..4i+3 of every sub-block, i = 0..7) leave the exact
+// int32 dot of row r with sub-block c in C[r][c].  Lane (gid, tig) thus ends a super-block holding
+// the dots of sub-blocks 2*tig, 2*tig+1 for rows gid and gid+8 and applies their 6-bit scales and
+// mins itself; only lanes with gid>>1 == tig feed nonzero activation bytes (others read a zero pad).
+// The 4 lanes of a row add their partial sums once at the end.
+// ------------------------------------------------------------------------------------------
+constexpr int M1_WARPS = 4;        // consumer warps; warp 4 only issues the copies
+constexpr int M1_THREADS = 160;
+constexpr int M1_KS = 1;                          // super-blocks per stage
+constexpr int M1_SROW = M1_KS * Q4_K_BYTES;        // 144 B: rows gid, gid+1 hit disjoint banks
+constexpr int M1_W_BYTES = QMM_ROWS * M1_SROW;
+constexpr int M1_STAGE = M1_W_BYTES + 384;         // weights | activation (256 B) + pair sums (16 B)
+constexpr int M1_CTAS = 6;                         // resident CTAs per SM
+
+__global__ void __launch_bounds__(M1_THREADS, M1_CTAS)
+    qmm_q4k_m1_kernel(const __grid_constant__ CUtensorMap wmap, int nb, int64_t n, ActQ a, int64_t k,
+                      float* __restrict__ y, float* __restrict__ part, int* __restrict__ tickets, int S,
+                      int sps) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = (uint64_t*)smem;
+    uint64_t* empty = full + QMM_STAGES;
+    int* flag = (int*)(smem + 96);
+    uint8_t* zpad = smem + 128;   // 64 zero bytes: the activation words of inactive lanes
+    uint8_t* buf = smem + 256;
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gid = lane >> 2, tig = lane & 3;
+    const int64_t r0 = (int64_t)blockIdx.x * QMM_ROWS;
+    const int split = blockIdx.z;
+    const int sb0 = split * sps, sb1 = min(nb, sb0 + sps);
+    const int nchunks = (sb1 - sb0 + M1_KS - 1) / M1_KS;
+    const int rows_here = (int)((n - r0) < QMM_ROWS ? (n - r0) : QMM_ROWS);
+
+    if (threadIdx.x < 16) ((uint32_t*)zpad)[threadIdx.x] = 0u;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < QMM_STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], M1_WARPS);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    // Chunk c: weights (constant: may be fetched before the producing kernel finishes) and the
+    // activation slice + pair sums (after pdl_wait).
+    auto issue_w = [&](int c) {
+        const int st = c % QMM_STAGES;
+        const int sbc = sb0 + c * M1_KS;
+        const int nsb = min(M1_KS, sb1 - sbc);
+        mbar_arrive_expect_tx(&full[st], (uint32_t)M1_W_BYTES + (uint32_t)(nsb * (QK_K + 16)));
+        fence_proxy_async_smem();
+        tma_load_2d(buf + (size_t)st * M1_STAGE, &wmap, sbc * (Q4_K_BYTES / 4), (int)r0, &full[st]);
+    };
+    auto issue_x = [&](int c) {
+        const int st = c % QMM_STAGES;
+        const int sbc = sb0 + c * M1_KS;
+        const int nsb = min(M1_KS, sb1 - sbc);
+        uint8_t* dst = buf + (size_t)st * M1_STAGE;
+        bulk_g2s(dst + M1_W_BYTES, a.qs + (size_t)sbc * QK_K, (uint32_t)(nsb * QK_K), &full[st]);
+        bulk_g2s(dst + M1_W_BYTES + 256, a.bs32 + (size_t)sbc * 8, (uint32_t)(nsb * 16), &full[st]);
+    };
+    const int pre = min(QMM_STAGES, nchunks);
+    if (warp == M1_WARPS && lane == 0)
+        for (int c = 0; c < pre; c++) issue_w(c);
+    pdl_wait();
+    bool ok = true;
+    if (warp == M1_WARPS) {  // producer: keep the ring full, independent of the consumers' progress
+        if (lane == 0) {
+            for (int c = 0; c < pre; c++) issue_x(c);
+            for (int c = pre; c < nchunks && ok; c++) {
+                ok = mbar_wait(&empty[c % QMM_STAGES], (uint32_t)(((c / QMM_STAGES) - 1) & 1), &g_qmm_error);
+                if (ok) {
+                    issue_w(c);
+                    issue_x(c);
+                }
+            }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
+
+    const bool active = (gid >> 1) == tig;  // feeds column gid (sub-block gid) of every mma
+    const bool odd = gid & 1;                // ... through b1 (odd sub-block) or b0 (even)
+    float yA = 0.0f, yB = 0.0f;
+    for (int c = 0; c < nchunks && ok && warp < M1_WARPS; c++) {
+        const int sbc = sb0 + c * M1_KS;
+        const int nsb = min(M1_KS, sb1 - sbc);
+        float dxr[M1_KS];
+#pragma unroll
+        for (int s = 0; s < M1_KS; s++) dxr[s] = s < nsb ? __ldg(&((const float*)a.d)[sbc + s]) : 0.0f;
+        ok = mbar_wait(&full[c % QMM_STAGES], (uint32_t)((c / QMM_STAGES) & 1), &g_qmm_error) && ok;
+        if (!ok) break;
+        const uint8_t* stage = buf + (size_t)(c % QMM_STAGES) * M1_STAGE;
+        const uint8_t* xs = stage + M1_W_BYTES;
+        const int16_t* bss = (const int16_t*)(stage + M1_W_BYTES + 256);
+#ifndef DCG_QMM_NOCOMPUTE
+#pragma unroll
+        for (int s = 0; s < M1_KS; s++) {
+            const uint8_t* rowA = stage + (warp * 16 + gid) * M1_SROW + s * Q4_K_BYTES;
+            const uint8_t* rowB = rowA + 8 * M1_SROW;
+            const uint4 hA = *(const uint4*)rowA, hB = *(const uint4*)rowB;
+            // weight words: pair group tig, elements 4i..4i+3 (i = 0..7) of rows gid / gid+8
+            const uint4 a0 = *(const uint4*)(rowA + 16 + 32 * tig), a1 = *(const uint4*)(rowA + 32 + 32 * tig);
+            const uint4 b0 = *(const uint4*)(rowB + 16 + 32 * tig), b1 = *(const uint4*)(rowB + 32 + 32 * tig);
+            const uint32_t wa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const uint32_t wb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+            // activation words of sub-block gid (active lanes) or zeros
+            const uint8_t* xsrc = active ? xs + s * QK_K + 32 * gid : zpad;
+            const uint4 x0 = *(const uint4*)xsrc, x1 = *(const uint4*)(xsrc + 16);
+            const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const uint32_t xv0 = odd ? 0u : xw[i], xv1 = odd ? xw[i] : 0u;
+                mma_s8(acc, wa[i] & 0x0F0F0F0Fu, wb[i] & 0x0F0F0F0Fu, (wa[i] >> 4) & 0x0F0F0F0Fu,
+                       (wb[i] >> 4) & 0x0F0F0F0Fu, xv0, xv1);
+            }
+            // acc: [0] row gid / sub-block 2tig, [1] row gid / 2tig+1, [2] row gid+8 / 2tig, [3] ...
+            const Q4kScales sA = q4k_unpack(hA), sB = q4k_unpack(hB);
+            const int sh = 16 * (tig & 1);
+            const uint32_t scA = ((tig < 2 ? sA.sc03 : sA.sc47) >> sh) & 0xFFFFu;
+            const uint32_t scB = ((tig < 2 ? sB.sc03 : sB.sc47) >> sh) & 0xFFFFu;
+            const uint32_t mnA = ((tig < 2 ? sA.mn03 : sA.mn47) >> sh) & 0xFFFFu;
+            const uint32_t mnB = ((tig < 2 ? sB.mn03 : sB.mn47) >> sh) & 0xFFFFu;
+            const int isA = (int)(scA & 0xFF) * acc[0] + (int)(scA >> 8) * acc[1];
+            const int isB = (int)(scB & 0xFF) * acc[2] + (int)(scB >> 8) * acc[3];
+            const int bsp = *(const int*)(bss + s * 8 + 2 * tig);  // pair sums of sub-blocks 2tig, 2tig+1
+            const int msA = __dp2a_lo(bsp, (int)mnA, 0), msB = __dp2a_lo(bsp, (int)mnB, 0);
+            const float2 dA = __half22float2(*reinterpret_cast<const __half2*>(&hA.x));
+            const float2 dB = __half22float2(*reinterpret_cast<const __half2*>(&hB.x));
+            yA += dxr[s] * (dA.x * (float)isA - dA.y * (float)msA);
+            yB += dxr[s] * (dB.x * (float)isB - dB.y * (float)msB);
+        }
+#endif
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[c % QMM_STAGES]);
+    }
+    pdl_trigger();
+    ok = __syncthreads_and(ok);
+    if (!ok) return;
+    yA += __shfl_xor_sync(0xffffffffu, yA, 1);
+    yA += __shfl_xor_sync(0xffffffffu, yA, 2);
+    yB += __shfl_xor_sync(0xffffffffu, yB, 1);
+    yB += __shfl_xor_sync(0xffffffffu, yB, 2);
+    const int64_t rowA = r0 + warp * 16 + gid, rowB = rowA + 8;
+    float* dst = S == 1 ? y : part + (size_t)split * n;
+    if (tig == 0 && warp < M1_WARPS) {
+        if (rowA < n) dst[rowA] = yA;
+        if (rowB < n) dst[rowB] = yB;
+    }
+    if (S == 1) return;
+    __threadfence();
+    __syncthreads();
+    int* ticket = &tickets[blockIdx.x];
+    if (threadIdx.x == 0) *flag = (atomicAdd(ticket, 1) == S - 1);
+    __syncthreads();
+    if (!*flag) return;
+    __threadfence();
+    for (int i = threadIdx.x; i < rows_here; i += blockDim.x) {
+        float sum = 0.0f;
+        for (int q = 0; q < S; q++) sum += __ldcg(&part[(size_t)q * n + r0 + i]);
+        y[r0 + i] = sum;
+    }
+    if (threadIdx.x == 0) *ticket = 0;
+}
+
+// split-K count: as many splits as still fit one wave of resident CTAs (ctas_per_sm x 148 SMs),
+// keeping >= 2 super-blocks per split
+static int qmm_splits(int tiles, int nb, int ctas_per_sm = 3) {
+    const int slots = ctas_per_sm * 148;
+    int S = slots / tiles;
+    S = S < 1 ? 1 : S;
+    S = S > nb / 2 ? (nb / 2 > 0 ? nb / 2 : 1) : S;
+    const int sps = (nb + S - 1) / S;
+    return (nb + sps - 1) / sps;
+}
+
+int qmm_ticket_count(int type, int64_t n, int64_t m) {
+    (void)type;
+    const int rb = (int)((n + QMM_ROWS - 1) / QMM_ROWS);
+    const int nt = m <= 8 ? 1 : (m <= 16 ? 2 : (m <= 32 ? 4 : 8));
+    const int cb = (int)((m + 8 * nt - 1) / (8 * nt));
+    return rb * cb;
+}
+
+size_t qmm_scratch_bytes(int type, int64_t n, int64_t k, int64_t m) {
+    (void)type;
+    const int nb = (int)(k / QK_K);
+    const int rb = (int)((n + QMM_ROWS - 1) / QMM_ROWS);
+    const int nt = m <= 8 ? 1 : (m <= 16 ? 2 : (m <= 32 ? 4 : 8));
+    const int cb = (int)((m + 8 * nt - 1) / (8 * nt));
+    const int S = m == 1 ? qmm_splits(rb, nb, M1_CTAS) : qmm_splits(rb * cb, nb);
+    return align256((size_t)rb * cb * 4) + (S > 1 ? align256((size_t)S * m * n * 4) : 0);
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link)
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    });
+    return fn;
+}
+
+// weight rows as a 2-D u32 tensor [n][row_bytes/4]; box = QMM_KS blocks x QMM_ROWS rows
+static cudaError_t make_wmap(CUtensorMap* map, const void* W, int64_t n, size_t row_bytes,
+                             int box_blocks = QMM_KS) {
+    auto fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 4), (cuuint64_t)n};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    const cuuint32_t box[2] = {(cuuint32_t)(box_blocks * Q4_K_BYTES / 4), (cuuint32_t)QMM_ROWS};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(W), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <int NT, bool DUP>
+static cudaError_t launch_q4k_t(const uint8_t* W, int64_t n, int64_t k, const ActQ& a, int m, float* y,
+                                void* scratch, cudaStream_t st) {
+    static bool attr = false;
+    const size_t smem = 128 + (size_t)QMM_STAGES * qmm_stage_bytes(DUP ? 1 : 8 * NT);
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(qmm_q4k_kernel<NT, DUP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    const int nb = (int)(k / QK_K);
+    const int rb = (int)((n + QMM_ROWS - 1) / QMM_ROWS);
+    const int cb = (m + 8 * NT - 1) / (8 * NT);
+    int S = qmm_splits(rb * cb, nb);
+    const int sps = (nb + S - 1) / S;
+    S = (nb + sps - 1) / sps;
+    int* tickets = (int*)scratch;
+    float* part = (float*)((uint8_t*)scratch + align256((size_t)rb * cb * 4));
+    CUtensorMap wmap;
+    cudaError_t e = make_wmap(&wmap, W, n, (size_t)nb * Q4_K_BYTES);
+    if (e != cudaSuccess) return e;
+    dim3 grid(rb, cb, S);
+    return launch_pdl(qmm_q4k_kernel<NT, DUP>, grid, dim3(QMM_THREADS), smem, st, wmap, nb, n, a, k, m, y,
+                      part, tickets, S, sps);
+}
+
+static cudaError_t launch_q4k_m1(const uint8_t* W, int64_t n, int64_t k, const ActQ& a, float* y,
+                                 void* scratch, cudaStream_t st) {
+    static bool attr = false;
+    const size_t smem = 256 + (size_t)QMM_STAGES * M1_STAGE;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(qmm_q4k_m1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    const int nb = (int)(k / QK_K);
+    const int rb = (int)((n + QMM_ROWS - 1) / QMM_ROWS);
+    int S = qmm_splits(rb, nb, M1_CTAS);
+    const int sps = (nb + S - 1) / S;
+    S = (nb + sps - 1) / sps;
+    int* tickets = (int*)scratch;
+    float* part = (float*)((uint8_t*)scratch + align256((size_t)rb * 4));
+    CUtensorMap wmap;
+    cudaError_t e = make_wmap(&wmap, W, n, (size_t)nb * Q4_K_BYTES, M1_KS);
+    if (e != cudaSuccess) return e;
+    dim3 grid(rb, 1, S);
+    return launch_pdl(qmm_q4k_m1_kernel, grid, dim3(M1_THREADS), smem, st, wmap, nb, n, a, k, y, part,
+                      tickets, S, sps);
+}
+
+bool qmm_supports(int type) { return type == DCG_TYPE_Q4_K; }
+
+cudaError_t launch_qmm(int type, const void* packed_w, int64_t n, int64_t k, const void* act,
+                       int64_t m, float* y, void* scratch, cudaStream_t st) {
+    if (type != DCG_TYPE_Q4_K) return cudaErrorNotSupported;
+    const ActQ a = act_view(DCG_TYPE_Q8_K, const_cast<void*>(act), m, k);
+    const uint8_t* W = (const uint8_t*)packed_w;
+    if (m == 1) return launch_q4k_m1(W, n, k, a, y, scratch, st);
+    if (m <= 8) return launch_q4k_t<1, false>(W, n, k, a, (int)m, y, scratch, st);
+    if (m <= 16) return launch_q4k_t<2, false>(W, n, k, a, (int)m, y, scratch, st);
+    if (m <= 32) return launch_q4k_t<4, false>(W, n, k, a, (int)m, y, scratch, st);
+    return launch_q4k_t<8, false>(W, n, k, a, (int)m, y, scratch, st);
+}
+
+}  // namespace dcg

@@ -20,9 +20,13 @@ namespace dcg {
 __global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float* __restrict__ x,
                                                             uint8_t* __restrict__ y,
                                                             int64_t n_blocks, int64_t m, int64_t k,
-                                                            bool out_soa) {
+                                                            bool out_soa, int* zero, int nzero) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int64_t b = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nzero; i += (int64_t)gridDim.x * blockDim.x)
+        zero[i] = 0;
     if (b >= n_blocks) return;
     const float v = x[b * QK8_0 + lane];
     float amax = fabsf(v);
@@ -49,9 +53,13 @@ __global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float* __restr
 __global__ void __launch_bounds__(256) quantize_q8_K_kernel(const float* __restrict__ x,
                                                             uint8_t* __restrict__ y,
                                                             int64_t n_blocks, int64_t m, int64_t k,
-                                                            bool out_soa) {
+                                                            bool out_soa, int* zero, int nzero) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int64_t b = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nzero; i += (int64_t)gridDim.x * blockDim.x)
+        zero[i] = 0;
     if (b >= n_blocks) return;
     const float4* xp = (const float4*)(x + b * QK_K + lane * 8);
     const float4 v0 = xp[0], v1 = xp[1];
@@ -103,6 +111,8 @@ __global__ void __launch_bounds__(256) quantize_q8_K_kernel(const float* __restr
         ActQ a = act_view(DCG_TYPE_Q8_K, y, m, k);
         *(uint2*)(a.qs + b * QK_K + lane * 8) = make_uint2(w0, w1);
         if ((lane & 1) == 0) a.bsums[b * 16 + (lane >> 1)] = (int16_t)s;
+        const int s32 = s + __shfl_xor_sync(0xffffffffu, s, 2);
+        if ((lane & 3) == 0) a.bs32[b * 8 + (lane >> 2)] = (int16_t)s32;
         if (lane == 0) ((float*)a.d)[b] = d;
     }
 }
@@ -270,14 +280,14 @@ __global__ void pack_kernel(int type, const uint8_t* __restrict__ src, size_t sr
 // launchers
 // ------------------------------------------------------------------------------------------
 cudaError_t launch_quantize_act(int act_type, const float* x, void* y, int64_t m, int64_t k,
-                                bool soa, cudaStream_t st) {
+                                bool soa, cudaStream_t st, int* zero, int nzero) {
     const int64_t nblk = m * k / (act_type == DCG_TYPE_Q8_0 ? QK8_0 : QK_K);
     if (nblk == 0) return cudaSuccess;
     const unsigned grid = (unsigned)((nblk + 7) / 8);
     if (act_type == DCG_TYPE_Q8_0)
-        quantize_q8_0_kernel<<<grid, 256, 0, st>>>(x, (uint8_t*)y, nblk, m, k, soa);
+        return launch_pdl(quantize_q8_0_kernel, dim3(grid), dim3(256), 0, st, x, (uint8_t*)y, nblk, m, k, soa, zero, nzero);
     else
-        quantize_q8_K_kernel<<<grid, 256, 0, st>>>(x, (uint8_t*)y, nblk, m, k, soa);
+        return launch_pdl(quantize_q8_K_kernel, dim3(grid), dim3(256), 0, st, x, (uint8_t*)y, nblk, m, k, soa, zero, nzero);
     return cudaGetLastError();
 }
 

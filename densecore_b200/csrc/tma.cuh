@@ -33,6 +33,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  : "memory");
 }
 
+// plain arrive (one of the barrier's expected arrivals)
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // global -> shared bulk copy completing on `bar`; src/dst 16-B aligned, bytes % 16 == 0
 __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, uint32_t bytes,
                                          uint64_t* bar) {
@@ -40,6 +45,17 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, uint32
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
             smem_u32(dst_smem)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// 2-D tiled tensor copy global -> shared (box given by the tensor map), completing on `bar`.
+// No multicast.  x is the innermost coordinate (elements), y the row.
+__device__ __forceinline__ void tma_load_2d(void* dst_smem, const void* tmap, int x, int y,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst_smem)),
+        "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
 }
 

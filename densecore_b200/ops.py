@@ -105,8 +105,12 @@ class QuantWeight:
         return self.n * row_size(self.qtype, self.k)
 
 
-def mul_mat_scratch_size(qtype: int, m: int, k: int) -> int:
-    return int(_lib.load().dcg_mul_mat_scratch_size(qtype, m, k))
+def mul_mat_scratch_size(qtype: int, n: int, k: int, m: int) -> int:
+    return int(_lib.load().dcg_mul_mat_scratch_size(qtype, n, k, m))
+
+
+def mul_mat_q_scratch_size(qtype: int, n: int, k: int, m: int) -> int:
+    return int(_lib.load().dcg_mul_mat_q_scratch_size(qtype, n, k, m))
 
 
 def mul_mat(w: QuantWeight, x: torch.Tensor, out: torch.Tensor | None = None,
@@ -118,7 +122,7 @@ def mul_mat(w: QuantWeight, x: torch.Tensor, out: torch.Tensor | None = None,
     m = x.numel() // w.k
     if out is None:
         out = torch.empty((m, w.n), dtype=torch.float32, device=x.device)
-    need = mul_mat_scratch_size(w.qtype, m, w.k)
+    need = mul_mat_scratch_size(w.qtype, w.n, w.k, m)
     if scratch is None:
         scratch = torch.empty(need, dtype=torch.uint8, device=x.device)
     _lib.check(_lib.load().dcg_mul_mat(w.qtype, _ptr(w.packed), w.n, w.k, _ptr(x), m, _ptr(out),
@@ -139,12 +143,16 @@ def quantize_act(x: torch.Tensor, act_type: int, out: torch.Tensor | None = None
 
 
 def mul_mat_q(w: QuantWeight, act: torch.Tensor, m: int, out: torch.Tensor | None = None,
-              stream=None) -> torch.Tensor:
+              scratch: torch.Tensor | None = None, stream=None) -> torch.Tensor:
     """y[m, n] = W . act with act from quantize_act(x, VEC_DOT_TYPE[w.qtype])."""
     if out is None:
         out = torch.empty((m, w.n), dtype=torch.float32, device=act.device)
+    if scratch is None:
+        scratch = torch.zeros(max(1, mul_mat_q_scratch_size(w.qtype, w.n, w.k, m)),
+                              dtype=torch.uint8, device=act.device)
     _lib.check(_lib.load().dcg_mul_mat_q(w.qtype, _ptr(w.packed), w.n, w.k, _ptr(act), m,
-                                         _ptr(out), _stream(stream)), "dcg_mul_mat_q")
+                                         _ptr(out), _ptr(scratch), scratch.numel(),
+                                         _stream(stream)), "dcg_mul_mat_q")
     return out
 
 

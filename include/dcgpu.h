@@ -58,8 +58,10 @@ int dcg_device_error(int* code, int clear);
 size_t dcg_row_size(int type, int64_t k);
 /* bytes of an n x k weight in the device layout (see dcg_weight_pack). */
 size_t dcg_packed_weight_size(int type, int64_t n, int64_t k);
-/* scratch bytes dcg_mul_mat needs for m activation rows of length k. */
-size_t dcg_mul_mat_scratch_size(int type, int64_t m, int64_t k);
+/* scratch bytes dcg_mul_mat needs for an n x k weight and m activation rows. */
+size_t dcg_mul_mat_scratch_size(int type, int64_t n, int64_t k, int64_t m);
+/* scratch bytes dcg_mul_mat_q needs (0 when the kernel takes none). */
+size_t dcg_mul_mat_q_scratch_size(int type, int64_t n, int64_t k, int64_t m);
 
 /* ---------------------------------------------------------------------------------------------
  * Activation quantization -- ggml type-trait from_float for the vec_dot_type of the weight
@@ -88,7 +90,7 @@ int dcg_weight_unpack(int type, const void* packed, int64_t n, int64_t k, void* 
  *   y[m][n] = sum_k W[n][k] * x[m][k], x quantized on the fly to Q8_0 (Q8_0 weights) or Q8_K
  *   (Q4_K / Q6_K weights), integer block dots, fp32 scaling and accumulation.
  * w: device layout (dcg_weight_pack) of an n x k weight; k % 256 == 0 (k % 32 for Q8_0).
- * scratch: >= dcg_mul_mat_scratch_size(type, m, k) bytes of device memory, 256-B aligned.
+ * scratch: >= dcg_mul_mat_scratch_size(type, n, k, m) bytes of device memory, 256-B aligned.
  * ------------------------------------------------------------------------------------------- */
 int dcg_mul_mat(int type, const void* w, int64_t n, int64_t k, const float* x, int64_t m, float* y,
                 void* scratch, size_t scratch_bytes, void* stream);
@@ -99,11 +101,13 @@ int dcg_mul_mat(int type, const void* w, int64_t n, int64_t k, const float* x, i
  * scales, then Q8_K block sums) that dcg_mul_mat_q reads; act_type is the vec_dot_type
  * (DCG_TYPE_Q8_0 or DCG_TYPE_Q8_K); act must hold dcg_act_size(act_type, m, k) bytes, 256-B
  * aligned.  dcg_mul_mat_q is ComputeDotProductBatch's job (core/src/simd_ops.cpp:140-197) for all
- * rows and all m activation rows at once. */
+ * rows and all m activation rows at once.  Its scratch (dcg_mul_mat_q_scratch_size bytes) must be
+ * zero-filled before its first use; every call leaves it ready for the next (dcg_mul_mat needs no
+ * such preparation). */
 size_t dcg_act_size(int act_type, int64_t m, int64_t k);
 int dcg_quantize_act(int act_type, const float* x, void* act, int64_t m, int64_t k, void* stream);
 int dcg_mul_mat_q(int type, const void* w, int64_t n, int64_t k, const void* act, int64_t m,
-                  float* y, void* stream);
+                  float* y, void* scratch, size_t scratch_bytes, void* stream);
 
 /* dcg_mul_mat without scratch: for callers that cannot allocate device memory where they run the
  * matmul (a ggml custom-op callback inside the compute thread pool, a plugin host that forbids
