@@ -60,6 +60,10 @@ static int enqueue_mul_mat_q(int type, const void* w, int64_t n, int64_t k, cons
         DCG_CUDA(dcg::launch_qmm(type, w, n, k, act, m, y, qscratch, st), "qmm");
         return DCG_OK;
     }
+    if (dcg::qmm_rd_supports(type, k, m)) {
+        DCG_CUDA(dcg::launch_qmm_rd(type, w, n, k, act, m, y, st), "qmm_rd");
+        return DCG_OK;
+    }
     for (int64_t m0 = 0; m0 < m; m0 += 8) {
         const int64_t mc = (m - m0) < 8 ? (m - m0) : 8;
         DCG_CUDA(dcg::launch_gemv(type, w, n, k, act, m, m0, mc, y, st), "gemv");

@@ -26,6 +26,11 @@ cudaError_t launch_qmm(int type, const void* packed_w, int64_t n, int64_t k, con
 cudaError_t qmm_device_error(int* out, bool clear);
 bool qmm_supports(int type);
 
+// register-direct tensor-core matmul for Q8_0 / Q6_K (qmm_rd.cu), M >= 2, k % 256 == 0
+bool qmm_rd_supports(int type, int64_t k, int64_t m);
+cudaError_t launch_qmm_rd(int type, const void* packed_w, int64_t n, int64_t k, const void* act,
+                          int64_t m, float* y, cudaStream_t st);
+
 // paged decode attention (attn.cu)
 void attn_plan(int n_seqs, int hkv, int max_ctx, int* splits, int* bps);
 size_t attn_scratch_bytes(int n_seqs, int hq, int hkv, int max_ctx);

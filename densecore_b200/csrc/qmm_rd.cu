@@ -1,0 +1,270 @@
+// qmm_rd.cu -- tensor-core matmul for Q8_0 and Q6_K weights (batched decode / prefill, any M),
+// register-direct: each warp streams the A fragments of its own 16 weight rows from global memory
+// into registers (one super-block ahead) and reuses them across NT mma n-tiles of activations,
+// whose B fragments come through L1 (every warp of the GPU reads the same small activation).
+// Replaces ggml_mul_mat / vec_dot_{q8_0_q8_0,q6_K_q8_K} (core/src/inference.cpp:1063,
+// :1794-1797, :1817; simd_ops.cpp:82-93) for these formats.
+//
+// Q8_0: one m16n8k32 mma per 32-element block; k order permuted so lane (gid, tig) supplies
+//       bytes 8*tig..8*tig+7 of its rows' block (a0|a2, a1|a3) and of the activation column
+//       (b0|b1).  y += d_w * d_x * C in fp32 per block.
+// Q6_K: one m16n8k16 mma per 16-element sub-block (lane: elements 4*tig..+3 of it); the 6-bit
+//       value is (ql nibble | qh 2 bits << 4) - 32; isum += scale_s * C (int32) over the
+//       super-block, y += d_w * d_x * isum.
+// Device weight layout (common.cuh): payload rows + separate fp16 scale array.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dcg {
+
+constexpr int RD_WARPS = 4;  // 64 rows per CTA
+
+__device__ __forceinline__ void mma_k32(int* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_k16(int* c, uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(b0));
+}
+
+__device__ __forceinline__ uint2 ldg64_stream(const void* p) {
+    uint2 r;
+    asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+    return r;
+}
+__device__ __forceinline__ uint32_t ldg32_stream(const void* p) {
+    uint32_t r;
+    asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+    return r;
+}
+
+// ------------------------------------------------------------------------------------------
+// Q8_0.  A super-block here is 8 blocks (256 elements) so the loop shape matches Q6_K.
+// ------------------------------------------------------------------------------------------
+struct Q80Frag {
+    uint2 a[8], b[8];   // rows gid / gid+8, blocks 0..7: bytes 8*tig..+7
+    uint4 dA, dB;       // fp16 scales of the 8 blocks, rows gid / gid+8
+};
+
+__device__ __forceinline__ void q80_load(Q80Frag& f, const PackedW& w, int64_t rowA, int64_t rowB,
+                                         int64_t n, int sb, int tig) {
+    const int64_t ra = rowA < n ? rowA : n - 1, rb = rowB < n ? rowB : n - 1;
+    const uint8_t* pa = w.payload + ra * w.row_bytes + (size_t)sb * 256 + 8 * tig;
+    const uint8_t* pb = w.payload + rb * w.row_bytes + (size_t)sb * 256 + 8 * tig;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        f.a[j] = ldg64_stream(pa + 32 * j);
+        f.b[j] = ldg64_stream(pb + 32 * j);
+    }
+    f.dA = __ldg((const uint4*)(w.d + ra * w.nb + (size_t)sb * 8));
+    f.dB = __ldg((const uint4*)(w.d + rb * w.nb + (size_t)sb * 8));
+}
+
+__device__ __forceinline__ float h_at(const uint4& v, int j) {  // fp16 j (0..7) of 8 packed
+    const uint32_t w = j < 2 ? v.x : (j < 4 ? v.y : (j < 6 ? v.z : v.w));
+    const __half2 h = *reinterpret_cast<const __half2*>(&w);
+    return (j & 1) ? __high2float(h) : __low2float(h);
+}
+
+template <int NT>
+__global__ void __launch_bounds__(RD_WARPS * 32) qmm_q8_0_rd_kernel(PackedW w, int64_t n, int64_t k,
+                                                                   ActQ a, int m, float* __restrict__ y) {
+    pdl_wait();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gid = lane >> 2, tig = lane & 3;
+    const int64_t rowA = ((int64_t)blockIdx.x * RD_WARPS + warp) * 16 + gid, rowB = rowA + 8;
+    const int c0 = blockIdx.y * 8 * NT;
+    const int nsb = (int)(k / 256);
+    const int nbx = (int)(k / QK8_0);
+    const __half* xd = (const __half*)a.d;
+    float acc[NT][4];
+#pragma unroll
+    for (int t = 0; t < NT; t++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[t][i] = 0.0f;
+    if (rowA - gid >= n) return;
+
+    Q80Frag cur, nxt;
+    q80_load(cur, w, rowA, rowB, n, 0, tig);
+    for (int sb = 0; sb < nsb; sb++) {
+        if (sb + 1 < nsb) q80_load(nxt, w, rowA, rowB, n, sb + 1, tig);
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            const int colB = c0 + t * 8 + gid;  // B column of this lane
+            const int cA = c0 + t * 8 + 2 * tig;  // C columns 2tig, 2tig+1
+            const int8_t* xb = a.qs + (size_t)(colB < m ? colB : 0) * k + (size_t)sb * 256 + 8 * tig;
+            uint4 dx0 = make_uint4(0, 0, 0, 0), dx1 = make_uint4(0, 0, 0, 0);
+            if (cA < m) dx0 = __ldg((const uint4*)(xd + (size_t)cA * nbx + (size_t)sb * 8));
+            if (cA + 1 < m) dx1 = __ldg((const uint4*)(xd + (size_t)(cA + 1) * nbx + (size_t)sb * 8));
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                uint2 xv = make_uint2(0, 0);
+                if (colB < m) xv = __ldg((const uint2*)(xb + 32 * j));
+                int c[4] = {0, 0, 0, 0};
+                mma_k32(c, cur.a[j].x, cur.b[j].x, cur.a[j].y, cur.b[j].y, xv.x, xv.y);
+                const float wa = h_at(cur.dA, j), wb = h_at(cur.dB, j);
+                const float x0 = h_at(dx0, j), x1 = h_at(dx1, j);
+                acc[t][0] += (wa * x0) * (float)c[0];
+                acc[t][1] += (wa * x1) * (float)c[1];
+                acc[t][2] += (wb * x0) * (float)c[2];
+                acc[t][3] += (wb * x1) * (float)c[3];
+            }
+        }
+        if (sb + 1 < nsb) cur = nxt;
+    }
+    pdl_trigger();
+#pragma unroll
+    for (int t = 0; t < NT; t++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int col = c0 + t * 8 + 2 * tig + (i & 1);
+            const int64_t row = i < 2 ? rowA : rowB;
+            if (col < m && row < n) y[(size_t)col * n + row] = acc[t][i];
+        }
+}
+
+// ------------------------------------------------------------------------------------------
+// Q6_K.  Sub-block s (16 elements): half h = s>>3, group grp = (s&7)>>1, l-range 16*(s&1)..+15.
+// Lane tig takes elements 4*tig..+3 of it: one ql word (nibble grp>>1) and one qh word (bits 2*grp).
+// ------------------------------------------------------------------------------------------
+struct Q6Frag {
+    uint32_t ql[2][8];  // [row A/B][h*4 + (grp&1)*2 + half]
+    uint32_t qh[2][4];  // [row][h*2 + half]
+    uint4 sc[2];        // int8 scales of the 16 sub-blocks
+    float d[2];
+};
+
+__device__ __forceinline__ void q6_load(Q6Frag& f, const PackedW& w, int64_t rowA, int64_t rowB,
+                                        int64_t n, int sb, int tig) {
+    const int64_t rows[2] = {rowA < n ? rowA : n - 1, rowB < n ? rowB : n - 1};
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const uint8_t* p = w.payload + rows[r] * w.row_bytes + (size_t)sb * Q6_K_PAYLOAD + 4 * tig;
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+#pragma unroll
+            for (int q = 0; q < 2; q++)
+#pragma unroll
+                for (int half = 0; half < 2; half++)
+                    f.ql[r][h * 4 + q * 2 + half] = ldg32_stream(p + h * 64 + q * 32 + half * 16);
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+#pragma unroll
+            for (int half = 0; half < 2; half++)
+                f.qh[r][h * 2 + half] = ldg32_stream(p + 128 + h * 32 + half * 16);
+        f.sc[r] = __ldg((const uint4*)(w.payload + rows[r] * w.row_bytes + (size_t)sb * Q6_K_PAYLOAD + 192));
+        f.d[r] = __half2float(w.d[rows[r] * w.nb + sb]);
+    }
+}
+
+__device__ __forceinline__ uint32_t q6_word(const Q6Frag& f, int r, int s) {
+    const int h = s >> 3, grp = (s & 7) >> 1, half = s & 1;
+    const uint32_t ql = f.ql[r][h * 4 + (grp & 1) * 2 + half];
+    const uint32_t qh = f.qh[r][h * 2 + half];
+    const uint32_t q = ((ql >> (4 * (grp >> 1))) & 0x0F0F0F0Fu) | (((qh >> (2 * grp)) & 0x03030303u) << 4);
+    return __vsub4(q, 0x20202020u);
+}
+
+__device__ __forceinline__ int sc_at(const uint4& v, int s) {  // signed int8 scale s (0..15)
+    const uint32_t w = s < 4 ? v.x : (s < 8 ? v.y : (s < 12 ? v.z : v.w));
+    return (int)(int8_t)((w >> (8 * (s & 3))) & 0xFF);
+}
+
+template <int NT>
+__global__ void __launch_bounds__(RD_WARPS * 32) qmm_q6k_rd_kernel(PackedW w, int64_t n, int64_t k,
+                                                                  ActQ a, int m, float* __restrict__ y) {
+    pdl_wait();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gid = lane >> 2, tig = lane & 3;
+    const int64_t rowA = ((int64_t)blockIdx.x * RD_WARPS + warp) * 16 + gid, rowB = rowA + 8;
+    const int c0 = blockIdx.y * 8 * NT;
+    const int nsb = (int)(k / QK_K);
+    const float* xd = (const float*)a.d;
+    float acc[NT][4];
+#pragma unroll
+    for (int t = 0; t < NT; t++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[t][i] = 0.0f;
+    if (rowA - gid >= n) return;
+
+    Q6Frag cur, nxt;
+    q6_load(cur, w, rowA, rowB, n, 0, tig);
+    for (int sb = 0; sb < nsb; sb++) {
+        if (sb + 1 < nsb) q6_load(nxt, w, rowA, rowB, n, sb + 1, tig);
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            const int colB = c0 + t * 8 + gid;
+            const int cA = c0 + t * 8 + 2 * tig;
+            const int8_t* xb = a.qs + (size_t)(colB < m ? colB : 0) * k + (size_t)sb * QK_K + 4 * tig;
+            int is[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int s = 0; s < 16; s++) {
+                const uint32_t xv = colB < m ? __ldg((const uint32_t*)(xb + 16 * s)) : 0u;
+                int c[4] = {0, 0, 0, 0};
+                mma_k16(c, q6_word(cur, 0, s), q6_word(cur, 1, s), xv);
+                const int sa = sc_at(cur.sc[0], s), sbb = sc_at(cur.sc[1], s);
+                is[0] += sa * c[0];
+                is[1] += sa * c[1];
+                is[2] += sbb * c[2];
+                is[3] += sbb * c[3];
+            }
+            const float x0 = cA < m ? xd[(size_t)cA * nsb + sb] : 0.0f;
+            const float x1 = cA + 1 < m ? xd[(size_t)(cA + 1) * nsb + sb] : 0.0f;
+            acc[t][0] += (cur.d[0] * x0) * (float)is[0];
+            acc[t][1] += (cur.d[0] * x1) * (float)is[1];
+            acc[t][2] += (cur.d[1] * x0) * (float)is[2];
+            acc[t][3] += (cur.d[1] * x1) * (float)is[3];
+        }
+        if (sb + 1 < nsb) cur = nxt;
+    }
+    pdl_trigger();
+#pragma unroll
+    for (int t = 0; t < NT; t++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int col = c0 + t * 8 + 2 * tig + (i & 1);
+            const int64_t row = i < 2 ? rowA : rowB;
+            if (col < m && row < n) y[(size_t)col * n + row] = acc[t][i];
+        }
+}
+
+template <int TYPE, int NT>
+static cudaError_t launch_rd_t(const PackedW& w, int64_t n, int64_t k, const ActQ& a, int m, float* y,
+                               cudaStream_t st) {
+    dim3 grid((unsigned)((n + RD_WARPS * 16 - 1) / (RD_WARPS * 16)), (unsigned)((m + 8 * NT - 1) / (8 * NT)));
+    if (TYPE == DCG_TYPE_Q8_0)
+        return launch_pdl(qmm_q8_0_rd_kernel<NT>, grid, dim3(RD_WARPS * 32), 0, st, w, n, k, a, m, y);
+    return launch_pdl(qmm_q6k_rd_kernel<NT>, grid, dim3(RD_WARPS * 32), 0, st, w, n, k, a, m, y);
+}
+
+bool qmm_rd_supports(int type, int64_t k, int64_t m) {
+    return (type == DCG_TYPE_Q8_0 || type == DCG_TYPE_Q6_K) && k % 256 == 0 && m >= 2;
+}
+
+cudaError_t launch_qmm_rd(int type, const void* packed_w, int64_t n, int64_t k, const void* act,
+                          int64_t m, float* y, cudaStream_t st) {
+    const PackedW w = packed_view(type, packed_w, n, k);
+    const int act_type = type == DCG_TYPE_Q8_0 ? DCG_TYPE_Q8_0 : DCG_TYPE_Q8_K;
+    const ActQ a = act_view(act_type, const_cast<void*>(act), m, k);
+    // column blocks of 8*NT activation rows run as grid.y: CTAs over the same weight rows share
+    // them through L2
+    const int mi = (int)m;
+    if (type == DCG_TYPE_Q8_0) {
+        if (mi <= 8) return launch_rd_t<DCG_TYPE_Q8_0, 1>(w, n, k, a, mi, y, st);
+        if (mi <= 16) return launch_rd_t<DCG_TYPE_Q8_0, 2>(w, n, k, a, mi, y, st);
+        return launch_rd_t<DCG_TYPE_Q8_0, 4>(w, n, k, a, mi, y, st);
+    }
+    if (mi <= 8) return launch_rd_t<DCG_TYPE_Q6_K, 1>(w, n, k, a, mi, y, st);
+    if (mi <= 16) return launch_rd_t<DCG_TYPE_Q6_K, 2>(w, n, k, a, mi, y, st);
+    return launch_rd_t<DCG_TYPE_Q6_K, 4>(w, n, k, a, mi, y, st);
+}
+
+}  // namespace dcg

@@ -88,6 +88,14 @@ MATMUL_CASES = [
     (O.Q6_K, 1024, 4096, 1),
     (O.Q6_K, 200, 9728, 7),
     (O.Q6_K, 64, 2560, 16),
+    # batched decode / prefill shapes (tensor-core GEMM paths)
+    (O.Q8_0, 1024, 1024, 64),     # Qwen3-0.6B q/k/v-like, decode batch 64
+    (O.Q8_0, 300, 3072, 33),      # ragged n and m
+    (O.Q6_K, 512, 2560, 32),      # Qwen3-4B attn_v-like, decode batch 32
+    (O.Q6_K, 100, 9728, 5),
+    (O.Q4_K, 1024, 2560, 64),
+    (O.Q4_K, 256, 4096, 256),     # config-2 M=256 (reduced n)
+    (O.Q4_K, 130, 14336, 17),
 ]
 
 
