@@ -140,6 +140,47 @@ def cpu_reference(budget_s: float):
                       f"host threads, oracle restatement of ggml vec_dot_q4_K_q8_K"}
 
 
+def decode_bench(which: str, steps: int, dev):
+    """Batched decode tokens/s of a random-init Qwen3-architecture decoder (BASELINE configs 3/4):
+    KV history is seeded random fp16 (prefill is not timed), contexts from the config's seed."""
+    import numpy as np
+    import torch
+
+    from densecore_b200 import decoder as D
+    if which == "3":
+        cfg, batch = D.QWEN3_0_6B, 64
+        ctx = np.random.default_rng(2).integers(128, 2049, batch)
+    else:
+        cfg, batch = D.QWEN3_4B, 32
+        ctx = np.random.default_rng(3).integers(2048, 4097, batch)
+    max_ctx = int(ctx.max()) + steps + 1
+    dec = D.Decoder(cfg, batch, max_ctx, seed=int(which), device=dev)
+    dec.fill_kv_random()
+    dec.tokens.copy_(torch.from_numpy(np.random.default_rng(4).integers(0, cfg.vocab, batch)))
+    dec.ctx_lens.copy_(torch.from_numpy(ctx.astype(np.int32)))
+    dec.capture()
+    for _ in range(3):
+        dec.graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        dec.graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    nbytes = dec.step_bytes(ctx)
+    out = {"model": cfg.name + " architecture (random init)", "batch": batch,
+           "weights": "Q8_0" if which == "3" else "Q4_K_M (Q6_K attn_v/ffn_down in even layers, Q6_K head)",
+           "contexts": f"{int(ctx.min())}-{int(ctx.max())} (sum {int(ctx.sum())})",
+           "ms_per_step": round(ms, 4), "tokens_per_s": round(batch / (ms * 1e-3), 1),
+           "min_bytes_per_step": nbytes, "achieved_gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+           "note": "same context lengths every step (the graph replays one step shape)"}
+    del dec
+    torch.cuda.empty_cache()
+    return out
+
+
 def _dist():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -284,6 +325,10 @@ def run_ours(args):
             "gpu_launches": 4 * steps,
             "clocks": clk.summary(),
         }
+        if not args.no_decode:
+            out["decode"] = {"config3": decode_bench("3", 20, dev)}
+            if not args.quick:
+                out["decode"]["config4"] = decode_bench("4", 10, dev)
         if not args.no_cpu_baseline:
             out["cpu_baseline"] = cpu_reference(args.cpu_seconds)
         print(json.dumps(out), flush=True)
@@ -343,6 +388,44 @@ def profile_case(args):
     print("profile case done", qtype, n, k, m)
 
 
+def attn_case(which: str, iters: int):
+    """One layer of config-3/4 paged decode attention (n_layer = 1 arena), eager, for ncu."""
+    import numpy as np
+    import torch
+
+    from densecore_b200 import ops
+    torch.cuda.set_device(0)
+    if which == "3":
+        ctx, hq, hkv = np.random.default_rng(2).integers(128, 2049, 64), 16, 8
+    else:
+        ctx, hq, hkv = np.random.default_rng(3).integers(2048, 4097, 32), 32, 8
+    B = len(ctx)
+    mbs = (int(ctx.max()) + 15) // 16
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    ka = torch.randn((B * mbs, 16, hkv, 128), generator=g, device="cuda").half()
+    va = torch.randn((B * mbs, 16, hkv, 128), generator=g, device="cuda").half()
+    bt = torch.randperm(B * mbs, device="cuda").view(B, mbs).int()
+    q = torch.randn((B, hq, 128), device="cuda")
+    cl = torch.from_numpy(ctx.astype(np.int32)).cuda()
+    out = torch.empty_like(q)
+    scr = torch.empty(max(1, ops.paged_attn_scratch_size(B, hq, hkv, int(ctx.max()))), dtype=torch.uint8,
+                      device="cuda")
+    for _ in range(iters):
+        ops.paged_attn_decode(q, ka, va, 1, 0, bt, cl, hkv, int(ctx.max()), out=out, scratch=scr)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(20):
+        ops.paged_attn_decode(q, ka, va, 1, 0, bt, cl, hkv, int(ctx.max()), out=out, scratch=scr)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / 20
+    kv = int(ctx.sum()) * hkv * 128 * 2 * 2
+    print(json.dumps({"attn_config": which, "us": round(us, 2), "kv_bytes": kv,
+                      "gbs": round(kv / us / 1e3, 1)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -352,14 +435,28 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-step-seconds", type=float, default=2.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the config-3/4 decode tokens/s")
+    ap.add_argument("--quick", action="store_true", help="decode: config 3 only")
     ap.add_argument("--profile-type", default=None, choices=["q4k", "q8_0", "q6k"],
                     help="run only a small eager GEMV case (for ncu) and exit")
     ap.add_argument("--profile-shape", default="up", choices=["up", "down", "sq"])
     ap.add_argument("--profile-m", type=int, default=1)
     ap.add_argument("--profile-iters", type=int, default=6)
+    ap.add_argument("--profile-attn", default=None, choices=["3", "4"],
+                    help="run only one layer's paged decode attention of config 3/4 (for ncu)")
+    ap.add_argument("--profile-decode", default=None, choices=["3", "4"],
+                    help="run only the config-3/4 decode measurement (for ncu) and exit")
     args = ap.parse_args()
     if args.profile_type:
         profile_case(args)
+        return
+    if args.profile_attn:
+        attn_case(args.profile_attn, args.profile_iters)
+        return
+    if args.profile_decode:
+        import torch
+        torch.cuda.set_device(0)
+        print(json.dumps(decode_bench(args.profile_decode, args.profile_iters, torch.device("cuda", 0))))
         return
     if args.impl == "reference":
         # bounded: each timed step is a ~2 s sample of the CPU workload

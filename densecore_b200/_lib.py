@@ -39,8 +39,8 @@ SIGNATURES = {
     "dcg_mul_mat_q": (i32, [i32, vp, i64, i64, vp, i64, vp, vp, sz, vp]),
     "dcg_mul_mat_noalloc": (i32, [i32, vp, i64, i64, vp, i64, vp, vp]),
     "dcg_paged_attn_scratch_size": (sz, [i32, i32, i32, i32, i32]),
-    "dcg_paged_attn_decode": (i32, [vp, vp, vp, i32, i32, vp, i32, vp, i32, i32, i32, i32, i32, f32,
-                                    vp, vp, sz, vp]),
+    "dcg_paged_attn_decode": (i32, [vp, vp, vp, i64, i32, i32, vp, i32, vp, i32, i32, i32, i32, i32,
+                                    f32, vp, vp, sz, vp]),
     "dcg_kv_append": (i32, [vp, vp, vp, vp, i32, i32, vp, i32, vp, vp, i32, i32, i32, vp]),
     "dcg_ctx_create": (i32, [i32, ctypes.POINTER(vp)]),
     "dcg_ctx_destroy": (i32, [vp]),

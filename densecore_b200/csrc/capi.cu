@@ -191,10 +191,11 @@ int dcg_mul_mat(int type, const void* w, int64_t n, int64_t k, const float* x, i
 
 int dcg_device_error(int* code, int clear) {
     if (!code) return fail(DCG_EINVAL, "null pointer");
-    int a = 0, b = 0;
+    int a = 0, b = 0, c = 0;
     DCG_CUDA(dcg::gemv_device_error(&a, clear != 0), "read device error flag");
     DCG_CUDA(dcg::qmm_device_error(&b, clear != 0), "read device error flag");
-    *code = a ? a : b;
+    DCG_CUDA(dcg::attn_device_error(&c, clear != 0), "read device error flag");
+    *code = a ? a : (b ? b : c);
     return DCG_OK;
 }
 
@@ -203,8 +204,9 @@ size_t dcg_paged_attn_scratch_size(int n_seqs, int hq, int hkv, int head_dim, in
     return dcg::attn_scratch_bytes(n_seqs, hq, hkv, max_ctx);
 }
 
-int dcg_paged_attn_decode(const float* q, const void* k_arena, const void* v_arena, int n_layer,
-                          int layer, const int32_t* block_tables, int max_blocks_per_seq,
+int dcg_paged_attn_decode(const float* q, const void* k_arena, const void* v_arena,
+                          int64_t n_arena_blocks, int n_layer, int layer,
+                          const int32_t* block_tables, int max_blocks_per_seq,
                           const int32_t* ctx_lens, int n_seqs, int hq, int hkv, int head_dim,
                           int max_ctx, float scale, float* out, void* scratch, size_t scratch_bytes,
                           void* stream) {
@@ -217,6 +219,7 @@ int dcg_paged_attn_decode(const float* q, const void* k_arena, const void* v_are
     const int nrep = hq / hkv;
     if (nrep != 1 && nrep != 2 && nrep != 4 && nrep != 8) return fail(DCG_EINVAL, "hq/hkv must be 1, 2, 4 or 8");
     if (n_layer <= 0 || layer < 0 || layer >= n_layer) return fail(DCG_EINVAL, "bad layer");
+    if (n_arena_blocks <= 0) return fail(DCG_EINVAL, "n_arena_blocks must be > 0");
     if (max_ctx < 0 || max_ctx > 16 * max_blocks_per_seq) return fail(DCG_EINVAL, "max_ctx exceeds the block table");
     if (!aligned(k_arena, 16) || !aligned(v_arena, 16) || !aligned(q, 16) || !aligned(out, 16))
         return fail(DCG_EINVAL, "q, out and the arenas must be 16-byte aligned");
@@ -226,7 +229,7 @@ int dcg_paged_attn_decode(const float* q, const void* k_arena, const void* v_are
     if (need && !aligned(scratch, 256)) return fail(DCG_EINVAL, "scratch must be 256-byte aligned");
     DCG_CUDA(dcg::launch_paged_attn(q, k_arena, v_arena, n_layer, layer, block_tables,
                                     max_blocks_per_seq, ctx_lens, n_seqs, hq, hkv, max_ctx, scale, out,
-                                    scratch, (cudaStream_t)stream), "paged_attn_decode");
+                                    scratch, (cudaStream_t)stream, n_arena_blocks), "paged_attn_decode");
     return DCG_OK;
 }
 

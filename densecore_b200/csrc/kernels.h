@@ -31,13 +31,14 @@ bool qmm_rd_supports(int type, int64_t k, int64_t m);
 cudaError_t launch_qmm_rd(int type, const void* packed_w, int64_t n, int64_t k, const void* act,
                           int64_t m, float* y, cudaStream_t st);
 
-// paged decode attention (attn.cu)
+// paged decode attention (attn.cu); n_arena_blocks = physical KV blocks in the arena
+cudaError_t attn_device_error(int* out, bool clear);
 void attn_plan(int n_seqs, int hkv, int max_ctx, int* splits, int* bps);
 size_t attn_scratch_bytes(int n_seqs, int hq, int hkv, int max_ctx);
 cudaError_t launch_paged_attn(const float* q, const void* karena, const void* varena, int n_layer,
                               int layer, const int* bt, int mbs, const int* ctx, int n_seqs, int hq,
                               int hkv, int max_ctx, float scale, float* out, void* scratch,
-                              cudaStream_t st);
+                              cudaStream_t st, int64_t n_arena_blocks);
 cudaError_t launch_kv_append(const float* k, const float* v, void* karena, void* varena, int n_layer,
                              int layer, const int* bt, int mbs, const int* seq_ids, const int* pos,
                              int n_tok, int hkv, int hd, cudaStream_t st);

@@ -514,7 +514,7 @@ size_t qmm_scratch_bytes(int type, int64_t n, int64_t k, int64_t m) {
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link)
-static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
     std::call_once(once, [] {

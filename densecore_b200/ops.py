@@ -181,8 +181,9 @@ def paged_attn_decode(q: torch.Tensor, k_arena: torch.Tensor, v_arena: torch.Ten
     need = paged_attn_scratch_size(n_seqs, hq, hkv, max_ctx, hd)
     if scratch is None:
         scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+    n_arena_blocks = k_arena.numel() // (16 * hkv * hd * n_layer)
     _lib.check(_lib.load().dcg_paged_attn_decode(
-        _ptr(q), _ptr(k_arena), _ptr(v_arena), n_layer, layer, _ptr(block_tables),
+        _ptr(q), _ptr(k_arena), _ptr(v_arena), n_arena_blocks, n_layer, layer, _ptr(block_tables),
         block_tables.shape[1], _ptr(ctx_lens), n_seqs, hq, hkv, hd, max_ctx, scale, _ptr(out),
         _ptr(scratch), scratch.numel(), _stream()), "dcg_paged_attn_decode")
     return out

@@ -130,14 +130,17 @@ int dcg_mul_mat_noalloc(int type, const void* w, int64_t n, int64_t k, const flo
  *   k/v_arena    fp16, element (block, layer, slot, head, dim) at
  *                ((block*n_layer + layer)*16 + slot)*hkv*head_dim + head*head_dim + dim
  *                (kv_cache.cpp:353-370, the declared WriteKSlot(block_id, layer, ...) order)
+ *   n_arena_blocks  physical blocks in each arena (PagedKVCache max_blocks, kv_cache.h:164); every
+ *                block id in block_tables must be < n_arena_blocks
  *   block_tables [n_seqs][max_blocks_per_seq] int32 physical block ids
  *   ctx_lens     [n_seqs] int32, each <= max_ctx and <= 16*max_blocks_per_seq
  *   out          [n_seqs][hq][head_dim] f32
  * head_dim must be 128 and hq/hkv one of 1, 2, 4, 8.  scratch: dcg_paged_attn_scratch_size bytes
  * (0 is valid when that size is 0), 256-B aligned.  All pointers are device pointers. */
 size_t dcg_paged_attn_scratch_size(int n_seqs, int hq, int hkv, int head_dim, int max_ctx);
-int dcg_paged_attn_decode(const float* q, const void* k_arena, const void* v_arena, int n_layer,
-                          int layer, const int32_t* block_tables, int max_blocks_per_seq,
+int dcg_paged_attn_decode(const float* q, const void* k_arena, const void* v_arena,
+                          int64_t n_arena_blocks, int n_layer, int layer,
+                          const int32_t* block_tables, int max_blocks_per_seq,
                           const int32_t* ctx_lens, int n_seqs, int hq, int hkv, int head_dim,
                           int max_ctx, float scale, float* out, void* scratch, size_t scratch_bytes,
                           void* stream);
