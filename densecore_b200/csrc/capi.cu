@@ -250,6 +250,50 @@ int dcg_kv_append(const float* k, const float* v, void* k_arena, void* v_arena, 
     return DCG_OK;
 }
 
+static bool act_shape_ok(int act_type, int64_t k) {
+    return (act_type == DCG_TYPE_Q8_0 && k % QK8_0 == 0) || (act_type == DCG_TYPE_Q8_K && k % QK_K == 0);
+}
+
+int dcg_add_rmsnorm_quantize(float* x, const float* delta, const float* weight, float eps, int64_t m,
+                             int64_t k, int act_type, void* act, void* stream) {
+    if (!x || !weight || !act) return fail(DCG_EINVAL, "null pointer");
+    if (m < 0 || k <= 0 || !act_shape_ok(act_type, k)) return fail(DCG_EINVAL, "bad shape or act_type");
+    if (m == 0) return DCG_OK;
+    if (!aligned(act, 256)) return fail(DCG_EINVAL, "act must be 256-byte aligned");
+    DCG_CUDA(dcg::launch_add_rmsnorm_quant(x, delta, weight, eps, m, k, act_type, act, (cudaStream_t)stream),
+             "add_rmsnorm_quantize");
+    return DCG_OK;
+}
+
+int dcg_swiglu_quantize(const float* gate, const float* up, int64_t ld, int64_t m, int64_t ffn,
+                        int act_type, void* act, void* stream) {
+    if (!gate || !up || !act) return fail(DCG_EINVAL, "null pointer");
+    if (m < 0 || ffn <= 0 || ld < ffn || !act_shape_ok(act_type, ffn)) return fail(DCG_EINVAL, "bad shape or act_type");
+    if (m == 0) return DCG_OK;
+    if (!aligned(act, 256)) return fail(DCG_EINVAL, "act must be 256-byte aligned");
+    DCG_CUDA(dcg::launch_swiglu_quant(gate, up, ld, m, ffn, act_type, act, (cudaStream_t)stream), "swiglu_quantize");
+    return DCG_OK;
+}
+
+int dcg_qk_norm_rope_kv_append(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v,
+                               int64_t ldv, int n_seqs, int hq, int hkv, int head_dim,
+                               const float* q_norm_w, const float* k_norm_w, float eps, float rope_theta,
+                               const int32_t* positions, float* q_out, void* k_arena, void* v_arena,
+                               int n_layer, int layer, const int32_t* block_tables,
+                               int max_blocks_per_seq, void* stream) {
+    if (!q || !k || !v || !q_norm_w || !k_norm_w || !positions || !q_out || !k_arena || !v_arena || !block_tables)
+        return fail(DCG_EINVAL, "null pointer");
+    if (head_dim != 128) return fail(DCG_EINVAL, "head_dim must be 128");
+    if (n_seqs < 0 || hq <= 0 || hkv <= 0 || n_layer <= 0 || layer < 0 || layer >= n_layer || max_blocks_per_seq <= 0)
+        return fail(DCG_EINVAL, "bad shape");
+    if (n_seqs == 0) return DCG_OK;
+    DCG_CUDA(dcg::launch_qk_rope_append(q, ldq, k, ldk, v, ldv, n_seqs, hq, hkv, q_norm_w, k_norm_w, eps,
+                                        rope_theta, positions, q_out, k_arena, v_arena, n_layer, layer,
+                                        block_tables, max_blocks_per_seq, (cudaStream_t)stream),
+             "qk_norm_rope_kv_append");
+    return DCG_OK;
+}
+
 size_t dcg_act_size(int act_type, int64_t m, int64_t k) {
     if (act_type != DCG_TYPE_Q8_0 && act_type != DCG_TYPE_Q8_K) return 0;
     return dcg::act_bytes(act_type, m, k);

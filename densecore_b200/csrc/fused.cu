@@ -1,0 +1,183 @@
+// fused.cu -- the element-wise work around the matmuls of a decode step, fused into the kernels
+// that produce the matmul inputs (the reference fuses the same steps on CPU: AddRMSNorm and the
+// QKV path of simd_ops.h, and BuildTransformerGraph's rms_norm / QK-norm / RoPE / SwiGLU nodes,
+// core/src/inference.cpp:1124-1313, :1790-1797):
+//
+//   add_rmsnorm_quant_kernel   x += delta (optional); act = quantize(x * rsqrt(mean(x^2)+eps) * w)
+//   swiglu_quant_kernel        act = quantize(silu(gate) * up)
+//   qk_rope_append_kernel      q, k: per-head RMSNorm (Qwen3 QK-norm) and NeoX RoPE at the
+//                              sequence's position; q -> q_out, k and v -> fp16 paged KV slots
+//
+// The quantized activation goes straight to the SoA layout the matmuls read.
+#include <math.h>
+
+#include "../../include/dcgpu.h"
+#include "common.cuh"
+#include "kernels.h"
+#include "quant_dev.cuh"
+
+namespace dcg {
+
+constexpr int FUSE_THREADS = 256;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += red[w];
+    __syncthreads();
+    return t;
+}
+
+// one CTA per activation row
+__global__ void __launch_bounds__(FUSE_THREADS) add_rmsnorm_quant_kernel(
+    float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w, float eps,
+    int64_t k, int act_type, ActQ a) {
+    __shared__ float red[FUSE_THREADS / 32];
+    pdl_wait();
+    pdl_trigger();
+    const int64_t row = blockIdx.x;
+    float* xr = x + row * k;
+    float ss = 0.0f;
+    for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
+        float v = xr[i];
+        if (delta) {
+            v += delta[row * k + i];
+            xr[i] = v;
+        }
+        ss += v * v;
+    }
+    const float rs = rsqrtf(block_sum(ss, red) / (float)k + eps);  // also orders the x writes above
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (act_type == DCG_TYPE_Q8_0) {
+        for (int64_t b = warp; b < k / QK8_0; b += nw) {
+            const int64_t i = b * QK8_0 + lane;
+            warp_q8_0_store(xr[i] * rs * w[i], lane, a, row * (k / QK8_0) + b);
+        }
+    } else {
+        for (int64_t b = warp; b < k / QK_K; b += nw) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int64_t i = b * QK_K + lane * 8 + j;
+                v[j] = xr[i] * rs * w[i];
+            }
+            warp_q8_K_store(v, lane, a, row * (k / QK_K) + b);
+        }
+    }
+}
+
+// act = quantize(silu(g) * u); g, u rows of `ffn` with row stride ld; one warp per block
+__global__ void __launch_bounds__(FUSE_THREADS) swiglu_quant_kernel(
+    const float* __restrict__ g, const float* __restrict__ u, int64_t ld, int64_t m, int64_t ffn,
+    int act_type, ActQ a) {
+    pdl_wait();
+    pdl_trigger();
+    const int lane = threadIdx.x & 31;
+    const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t per_row = act_type == DCG_TYPE_Q8_0 ? ffn / QK8_0 : ffn / QK_K;
+    if (gw >= m * per_row) return;
+    const int64_t row = gw / per_row, b = gw % per_row;
+    const float* gr = g + row * ld;
+    const float* ur = u + row * ld;
+    if (act_type == DCG_TYPE_Q8_0) {
+        const int64_t i = b * QK8_0 + lane;
+        const float gv = gr[i];
+        warp_q8_0_store(gv / (1.0f + expf(-gv)) * ur[i], lane, a, row * per_row + b);
+    } else {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int64_t i = b * QK_K + lane * 8 + j;
+            const float gv = gr[i];
+            v[j] = gv / (1.0f + expf(-gv)) * ur[i];
+        }
+        warp_q8_K_store(v, lane, a, row * per_row + b);
+    }
+}
+
+// one warp per (sequence, head) over hq + hkv heads; lane owns dims {2l, 2l+1, 64+2l, 65+2l}
+__global__ void __launch_bounds__(FUSE_THREADS) qk_rope_append_kernel(
+    const float* __restrict__ q, int64_t ldq, const float* __restrict__ k, int64_t ldk,
+    const float* __restrict__ v, int64_t ldv, int n_seqs, int hq, int hkv, const float* __restrict__ qw,
+    const float* __restrict__ kw, float eps, float theta, const int* __restrict__ pos,
+    float* __restrict__ q_out, __half* __restrict__ karena, __half* __restrict__ varena, int n_layer,
+    int layer, const int* __restrict__ bt, int mbs) {
+    constexpr int D = 128;
+    pdl_wait();
+    pdl_trigger();
+    const int lane = threadIdx.x & 31;
+    const int gw = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    const int heads = hq + hkv;
+    if (gw >= n_seqs * heads) return;
+    const int s = gw / heads, h = gw % heads;
+    const bool is_q = h < hq;
+    const int hh = is_q ? h : h - hq;
+    const float* src = is_q ? q + (int64_t)s * ldq + hh * D : k + (int64_t)s * ldk + hh * D;
+    const float* nw = is_q ? qw : kw;
+    const int d0 = 2 * lane, d1 = 64 + 2 * lane;
+    float x0 = src[d0], x1 = src[d0 + 1], y0 = src[d1], y1 = src[d1 + 1];
+    float ss = x0 * x0 + x1 * x1 + y0 * y0 + y1 * y1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rs = rsqrtf(ss / (float)D + eps);
+    x0 *= rs * nw[d0];
+    x1 *= rs * nw[d0 + 1];
+    y0 *= rs * nw[d1];
+    y1 *= rs * nw[d1 + 1];
+    // NeoX rotate-half: (x_i, x_{i+64}) at angle p * theta^(-2i/D)
+    const float p = (float)pos[s];
+    const float f0 = (float)exp2(-(double)(2 * d0) / D * log2((double)theta));
+    const float f1 = (float)exp2(-(double)(2 * (d0 + 1)) / D * log2((double)theta));
+    float s0, c0, s1, c1;
+    sincosf(p * f0, &s0, &c0);
+    sincosf(p * f1, &s1, &c1);
+    const float r0 = x0 * c0 - y0 * s0, r1 = x1 * c1 - y1 * s1;
+    const float r2 = y0 * c0 + x0 * s0, r3 = y1 * c1 + x1 * s1;
+    if (is_q) {
+        float* dst = q_out + ((int64_t)s * hq + hh) * D;
+        *(float2*)(dst + d0) = make_float2(r0, r1);
+        *(float2*)(dst + d1) = make_float2(r2, r3);
+        return;
+    }
+    const int ps = pos[s];
+    const int phys = bt[(int64_t)s * mbs + ps / 16];
+    const size_t slot = (((size_t)phys * n_layer + layer) * 16 + (ps % 16)) * (size_t)hkv * D + (size_t)hh * D;
+    *(__half2*)(karena + slot + d0) = __floats2half2_rn(r0, r1);
+    *(__half2*)(karena + slot + d1) = __floats2half2_rn(r2, r3);
+    const float* vr = v + (int64_t)s * ldv + hh * D;
+    *(__half2*)(varena + slot + d0) = __floats2half2_rn(vr[d0], vr[d0 + 1]);
+    *(__half2*)(varena + slot + d1) = __floats2half2_rn(vr[d1], vr[d1 + 1]);
+}
+
+cudaError_t launch_add_rmsnorm_quant(float* x, const float* delta, const float* w, float eps, int64_t m,
+                                     int64_t k, int act_type, void* act, cudaStream_t st) {
+    const ActQ a = act_view(act_type, act, m, k);
+    return launch_pdl(add_rmsnorm_quant_kernel, dim3((unsigned)m), dim3(FUSE_THREADS), 0, st, x, delta, w, eps,
+                      k, act_type, a);
+}
+
+cudaError_t launch_swiglu_quant(const float* g, const float* u, int64_t ld, int64_t m, int64_t ffn,
+                                int act_type, void* act, cudaStream_t st) {
+    const ActQ a = act_view(act_type, act, m, ffn);
+    const int64_t warps = m * (act_type == DCG_TYPE_Q8_0 ? ffn / QK8_0 : ffn / QK_K);
+    const unsigned grid = (unsigned)((warps * 32 + FUSE_THREADS - 1) / FUSE_THREADS);
+    return launch_pdl(swiglu_quant_kernel, dim3(grid), dim3(FUSE_THREADS), 0, st, g, u, ld, m, ffn, act_type, a);
+}
+
+cudaError_t launch_qk_rope_append(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v,
+                                  int64_t ldv, int n_seqs, int hq, int hkv, const float* qw, const float* kw,
+                                  float eps, float theta, const int* pos, float* q_out, void* karena,
+                                  void* varena, int n_layer, int layer, const int* bt, int mbs,
+                                  cudaStream_t st) {
+    const int64_t warps = (int64_t)n_seqs * (hq + hkv);
+    const unsigned grid = (unsigned)((warps * 32 + FUSE_THREADS - 1) / FUSE_THREADS);
+    return launch_pdl(qk_rope_append_kernel, dim3(grid), dim3(FUSE_THREADS), 0, st, q, ldq, k, ldk, v, ldv,
+                      n_seqs, hq, hkv, qw, kw, eps, theta, pos, q_out, (__half*)karena, (__half*)varena,
+                      n_layer, layer, bt, mbs);
+}
+
+}  // namespace dcg

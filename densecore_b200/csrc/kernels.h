@@ -43,6 +43,17 @@ cudaError_t launch_kv_append(const float* k, const float* v, void* karena, void*
                              int layer, const int* bt, int mbs, const int* seq_ids, const int* pos,
                              int n_tok, int hkv, int hd, cudaStream_t st);
 
+// fused pre-matmul element-wise kernels (fused.cu)
+cudaError_t launch_add_rmsnorm_quant(float* x, const float* delta, const float* w, float eps, int64_t m,
+                                     int64_t k, int act_type, void* act, cudaStream_t st);
+cudaError_t launch_swiglu_quant(const float* g, const float* u, int64_t ld, int64_t m, int64_t ffn,
+                                int act_type, void* act, cudaStream_t st);
+cudaError_t launch_qk_rope_append(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v,
+                                  int64_t ldv, int n_seqs, int hq, int hkv, const float* qw, const float* kw,
+                                  float eps, float theta, const int* pos, float* q_out, void* karena,
+                                  void* varena, int n_layer, int layer, const int* bt, int mbs,
+                                  cudaStream_t st);
+
 // error flag of the bounded waits of the GEMV kernels (0 = none); optionally cleared
 cudaError_t gemv_device_error(int* out, bool clear);
 

@@ -4,16 +4,16 @@ This is the caller side of the hot path -- what DenseCore's BuildTransformerGrap
 step (core/src/inference.cpp:1116-1817) for every sequence of a continuous batch -- rebuilt around
 the B200 kernels:
 
-  per layer:  h = rmsnorm(x)                      (torch)
-              act = quantize_act(h)                (dcgpu, one Q8 activation for q/k/v)
-              q, k, v = mul_mat_q(W_q|W_k|W_v, act)  (dcgpu tensor-core matmul)
-              q, k = qk_norm, rope(q, k)           (torch; Qwen3 per-head RMSNorm, NeoX RoPE)
-              kv_append(k, v)                      (dcgpu, fp16 paged slots)
-              o = paged_attn_decode(q, cache)      (dcgpu)
-              x += mul_mat(W_o, o)
-              h = rmsnorm(x); act = quantize_act(h)
-              x += mul_mat(W_down, silu(mul_mat_q(W_gate, act)) * mul_mat_q(W_up, act))
-  logits = mul_mat(W_out, rmsnorm(x)) (tied embeddings); next = argmax(logits)
+  per layer:  act = add_rmsnorm_quantize(x += delta)     (fused: residual, RMSNorm, Q8 quantize)
+              qkv = mul_mat_q(W_q|W_k|W_v, act)           (one stacked tensor-core matmul)
+              qk_norm_rope_kv_append(qkv)                 (fused: Qwen3 QK-norm, NeoX RoPE, fp16 slots)
+              o = paged_attn_decode(q, cache)
+              yo = mul_mat_q(W_o, quantize(o))
+              act = add_rmsnorm_quantize(x += yo)
+              gu = mul_mat_q(W_gate|W_up, act)            (one stacked matmul)
+              delta = mul_mat_q(W_down, swiglu_quantize(gu))
+  logits = mul_mat(W_out, rmsnorm(x += delta)) (tied embeddings); next = argmax(logits)
+  (all dcgpu kernels; torch only gathers the embedding rows and takes the argmax)
 
 Each sequence attends to its own history through its own block table (per-sequence semantics; the
 reference's batched path reads seq_id[0]'s history for every sequence).  Weights are random-init
@@ -79,23 +79,29 @@ class Decoder:
 
         self.layers = []
         for li in range(cfg.n_layer):
-            L = {
-                "attn_q": qw(qd, H, _wtype(cfg, li, "attn_q")),
-                "attn_k": qw(kvd, H, _wtype(cfg, li, "attn_k")),
-                "attn_v": qw(kvd, H, _wtype(cfg, li, "attn_v")),
-                "attn_output": qw(H, qd, _wtype(cfg, li, "attn_output")),
-                "ffn_gate": qw(cfg.ffn, H, _wtype(cfg, li, "ffn_gate")),
-                "ffn_up": qw(cfg.ffn, H, _wtype(cfg, li, "ffn_up")),
-                "ffn_down": qw(H, cfg.ffn, _wtype(cfg, li, "ffn_down")),
-            }
+            t_q, t_k, t_v = (_wtype(cfg, li, nm) for nm in ("attn_q", "attn_k", "attn_v"))
+            wq = torch.randn((qd, H), generator=g, device=dev) * 0.02
+            wk = torch.randn((kvd, H), generator=g, device=dev) * 0.02
+            wv = torch.randn((kvd, H), generator=g, device=dev) * 0.02
+            L = {"qkv_split": t_v != t_q}
+            if t_v == t_q:  # one stacked [q; k; v] weight: rows are quantized independently
+                L["attn_qkv"] = ops.QuantWeight.from_float(torch.cat([wq, wk, wv]), t_q)
+            else:
+                L["attn_qk"] = ops.QuantWeight.from_float(torch.cat([wq, wk]), t_q)
+                L["attn_v"] = ops.QuantWeight.from_float(wv, t_v)
+            del wq, wk, wv
+            L["attn_output"] = qw(H, qd, _wtype(cfg, li, "attn_output"))
+            wg = torch.randn((cfg.ffn, H), generator=g, device=dev) * 0.02
+            wu = torch.randn((cfg.ffn, H), generator=g, device=dev) * 0.02
+            L["ffn_gate_up"] = ops.QuantWeight.from_float(torch.cat([wg, wu]), _wtype(cfg, li, "ffn_gate"))
+            del wg, wu
+            L["ffn_down"] = qw(H, cfg.ffn, _wtype(cfg, li, "ffn_down"))
             self.layers.append(L)
         # tied embeddings: the LM head is the quantized token embedding; lookups dequantize it
         self.output = qw(cfg.vocab, H, cfg.wtype if cfg.wtype == Q8_0 else Q6_K)
         self.tok_embd = self._dequant_rows(self.output)
         self.ones_h = torch.ones(H, device=dev)
         self.ones_d = torch.ones(D, device=dev)
-        inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, D, 2, device=dev, dtype=torch.float64) / D))
-        self.inv_freq = inv.float()
 
         # paged KV arena (kv_cache.cpp:353-370 layout): [(block*n_layer + layer)][16][hkv][D] fp16
         self.blocks_per_seq = (max_ctx + KV_BLOCK - 1) // KV_BLOCK
@@ -147,68 +153,86 @@ class Decoder:
             self._scratch[key] = t
         return t
 
-    def _rms(self, x, w, eps):
-        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
-
-    def _rope(self, x, pos):
-        # NeoX rotate-half over head_dim; x [B, H, D], pos [B]
-        ang = pos.float()[:, None] * self.inv_freq[None, :]  # [B, D/2]
-        cos, sin = torch.cos(ang)[:, None, :], torch.sin(ang)[:, None, :]
-        x1, x2 = x[..., : x.shape[-1] // 2], x[..., x.shape[-1] // 2:]
-        return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1)
-
     def _mm(self, key, w: ops.QuantWeight, act, m):
         out = self._buf(("y", key), (m, w.n))
         scr = self._buf(("qs", key), (max(1, ops.mul_mat_q_scratch_size(w.qtype, w.n, w.k, m)),),
                         torch.uint8, zero=True)
         return ops.mul_mat_q(w, act, m, out=out, scratch=scr)
 
-    def _act(self, key, x, qtype):
-        at = VEC_DOT_TYPE[qtype]
-        m, k = x.shape
-        buf = self._buf(("act", key, at), (int(ops._lib.load().dcg_act_size(at, m, k)),), torch.uint8)
-        return ops.quantize_act(x.contiguous(), at, out=buf)
-
     # ---------------------------------------------------------------- the step
+    def ggml_rows(self, li: int, name: str):
+        """(ggml rows as numpy, type, k) of one logical weight (unstacking the fused ones)."""
+        cfg, D = self.cfg, self.cfg.head_dim
+        qd, kvd = cfg.n_head * D, cfg.n_head_kv * D
+        L = self.layers[li]
+        spans = {"attn_q": (0, qd), "attn_k": (qd, qd + kvd), "attn_v": (qd + kvd, qd + 2 * kvd),
+                 "ffn_gate": (0, cfg.ffn), "ffn_up": (cfg.ffn, 2 * cfg.ffn)}
+        if name in ("attn_output", "ffn_down") or (name == "attn_v" and L["qkv_split"]):
+            w = L[name]
+            return w.to_ggml().cpu().numpy(), w.qtype, w.k
+        key = "ffn_gate_up" if name.startswith("ffn") else ("attn_qk" if L["qkv_split"] else "attn_qkv")
+        w = L[key]
+        a, b = spans[name]
+        return w.to_ggml().cpu().numpy()[a:b], w.qtype, w.k
+
     def step(self):
         """One decode token for every sequence: reads self.tokens / self.ctx_lens, writes
-        self.next_tokens and self.logits, appends K/V at position ctx_len-1."""
+        self.next_tokens and self.logits, appends K/V at position ctx_len-1.  Per layer: fused
+        add+RMSNorm+quantize, stacked QKV matmul, fused QK-norm+RoPE+KV append, paged attention,
+        quantize, O matmul, fused add+RMSNorm+quantize, stacked gate|up matmul, fused
+        SwiGLU+quantize, down matmul (its output is added by the next layer's norm kernel)."""
         cfg, B = self.cfg, self.batch
-        D, hq, hkv = cfg.head_dim, cfg.n_head, cfg.n_head_kv
-        pos = (self.ctx_lens - 1).to(torch.int32)
-        x = self.tok_embd[self.tokens].float()
+        D, hq, hkv, H = cfg.head_dim, cfg.n_head, cfg.n_head_kv, cfg.hidden
+        qd, kvd = hq * D, hkv * D
+        pos = self._buf("pos", (B,), torch.int32)
+        torch.sub(self.ctx_lens, 1, out=pos)
+        x = self._buf("x", (B, H))
+        x.copy_(self.tok_embd[self.tokens])
         scale = 1.0 / math.sqrt(D)
+        q_rot = self._buf("q_rot", (B, hq, D))
         attn_out = self._buf("attn_out", (B, hq, D))
         attn_scr = self._buf("attn_scr", (max(1, ops.paged_attn_scratch_size(B, hq, hkv, self.max_ctx)),),
                              torch.uint8)
+        delta = None
         for li, L in enumerate(self.layers):
-            h = self._rms(x, self.ones_h, cfg.rms_eps)
-            a_q = self._act(("attn", L["attn_q"].qtype), h, L["attn_q"].qtype)
-            a_v = a_q if VEC_DOT_TYPE[L["attn_v"].qtype] == VEC_DOT_TYPE[L["attn_q"].qtype] else \
-                self._act(("attn_v", L["attn_v"].qtype), h, L["attn_v"].qtype)
-            q = self._mm(("q", li), L["attn_q"], a_q, B).view(B, hq, D)
-            k = self._mm(("k", li), L["attn_k"], a_q, B).view(B, hkv, D)
-            v = self._mm(("v", li), L["attn_v"], a_v, B).view(B, hkv, D)
-            q = self._rope(self._rms(q, self.ones_d, cfg.rms_eps), pos).contiguous()
-            k = self._rope(self._rms(k, self.ones_d, cfg.rms_eps), pos).contiguous()
-            ops.kv_append(k, v.contiguous(), self.k_arena, self.v_arena, cfg.n_layer, li,
-                          self.block_tables, self.seq_ids, pos)
-            ops.paged_attn_decode(q, self.k_arena, self.v_arena, cfg.n_layer, li, self.block_tables,
-                                  self.ctx_lens, hkv, self.max_ctx, scale, out=attn_out,
-                                  scratch=attn_scr)
-            a_o = self._act(("o", L["attn_output"].qtype), attn_out.view(B, hq * D), L["attn_output"].qtype)
-            x = x + self._mm(("o", li), L["attn_output"], a_o, B)
-            h = self._rms(x, self.ones_h, cfg.rms_eps)
-            a_f = self._act(("ffn", L["ffn_gate"].qtype), h, L["ffn_gate"].qtype)
-            gate = self._mm(("gate", li), L["ffn_gate"], a_f, B)
-            up = self._mm(("up", li), L["ffn_up"], a_f, B)
-            hf = torch.nn.functional.silu(gate) * up
-            a_d = self._act(("down", L["ffn_down"].qtype), hf, L["ffn_down"].qtype)
-            x = x + self._mm(("down", li), L["ffn_down"], a_d, B)
-        h = self._rms(x, self.ones_h, cfg.rms_eps)
-        a_h = self._act(("head", self.output.qtype), h, self.output.qtype)
-        self.logits.copy_(self._mm(("head",), self.output, a_h, B))
+            wqk = L["attn_qk"] if L["qkv_split"] else L["attn_qkv"]
+            act = self._actbuf(("attn", wqk.qtype), B, H, wqk.qtype)
+            ops.add_rmsnorm_quantize(x, self.ones_h, cfg.rms_eps, VEC_DOT_TYPE[wqk.qtype], act, delta)
+            yqk = self._mm(("qkv", li), wqk, act, B)
+            if L["qkv_split"]:
+                wv = L["attn_v"]
+                act_v = act
+                if VEC_DOT_TYPE[wv.qtype] != VEC_DOT_TYPE[wqk.qtype]:
+                    act_v = self._actbuf(("attn_v", wv.qtype), B, H, wv.qtype)
+                    ops.add_rmsnorm_quantize(x, self.ones_h, cfg.rms_eps, VEC_DOT_TYPE[wv.qtype], act_v)
+                yv, ldv = self._mm(("v", li), wv, act_v, B), kvd
+            else:
+                yv, ldv = yqk[:, qd + kvd:], wqk.n
+            ops.qk_norm_rope_kv_append(yqk, wqk.n, yqk[:, qd:], wqk.n, yv, ldv, B, hq, hkv, self.ones_d,
+                                       self.ones_d, cfg.rms_eps, cfg.rope_theta, pos, q_rot,
+                                       self.k_arena, self.v_arena, cfg.n_layer, li, self.block_tables)
+            ops.paged_attn_decode(q_rot, self.k_arena, self.v_arena, cfg.n_layer, li, self.block_tables,
+                                  self.ctx_lens, hkv, self.max_ctx, scale, out=attn_out, scratch=attn_scr)
+            wo = L["attn_output"]
+            act_o = self._actbuf(("o", wo.qtype), B, qd, wo.qtype)
+            ops.quantize_act(attn_out.view(B, qd), VEC_DOT_TYPE[wo.qtype], out=act_o)
+            yo = self._mm(("o", li), wo, act_o, B)
+            wgu = L["ffn_gate_up"]
+            act_f = self._actbuf(("ffn", wgu.qtype), B, H, wgu.qtype)
+            ops.add_rmsnorm_quantize(x, self.ones_h, cfg.rms_eps, VEC_DOT_TYPE[wgu.qtype], act_f, yo)
+            ygu = self._mm(("gu", li), wgu, act_f, B)
+            wd = L["ffn_down"]
+            act_d = self._actbuf(("down", wd.qtype), B, cfg.ffn, wd.qtype)
+            ops.swiglu_quantize(ygu, ygu[:, cfg.ffn:], 2 * cfg.ffn, B, cfg.ffn, VEC_DOT_TYPE[wd.qtype], act_d)
+            delta = self._mm(("down", li), wd, act_d, B)
+        act_h = self._actbuf(("head", self.output.qtype), B, H, self.output.qtype)
+        ops.add_rmsnorm_quantize(x, self.ones_h, cfg.rms_eps, VEC_DOT_TYPE[self.output.qtype], act_h, delta)
+        self.logits.copy_(self._mm(("head",), self.output, act_h, B))
         self.next_tokens.copy_(torch.argmax(self.logits, dim=-1))
+
+    def _actbuf(self, key, m, k, wtype):
+        at = VEC_DOT_TYPE[wtype]
+        return self._buf(("act", key, at, k), (int(ops._lib.load().dcg_act_size(at, m, k)),), torch.uint8)
 
     def capture(self):
         """Capture step() into a CUDA graph (buffers are static)."""
@@ -237,7 +261,8 @@ class Decoder:
 
     # bytes one decode step must read at least (weights + KV history), for the roofline
     def step_bytes(self, ctx_lens) -> int:
-        w = sum(wt.nbytes for L in self.layers for wt in L.values()) + self.output.nbytes
+        w = sum(wt.nbytes for L in self.layers for wt in L.values()
+                if isinstance(wt, ops.QuantWeight)) + self.output.nbytes
         kv = int(sum(int(c) for c in ctx_lens)) * self.cfg.n_layer * 2 * self.cfg.n_head_kv * \
             self.cfg.head_dim * 2
         return w + kv

@@ -202,6 +202,33 @@ def kv_append(k: torch.Tensor, v: torch.Tensor, k_arena: torch.Tensor, v_arena: 
         "dcg_kv_append")
 
 
+def add_rmsnorm_quantize(x: torch.Tensor, weight: torch.Tensor, eps: float, act_type: int,
+                         act: torch.Tensor, delta: torch.Tensor | None = None) -> torch.Tensor:
+    """x += delta (in place, optional); act = quantize(rmsnorm(x) * weight)."""
+    m, k = x.shape
+    _lib.check(_lib.load().dcg_add_rmsnorm_quantize(
+        _ptr(x), _ptr(delta) if delta is not None else None, _ptr(weight), eps, m, k, act_type,
+        _ptr(act), _stream()), "dcg_add_rmsnorm_quantize")
+    return act
+
+
+def swiglu_quantize(gate: torch.Tensor, up: torch.Tensor, ld: int, m: int, ffn: int, act_type: int,
+                    act: torch.Tensor) -> torch.Tensor:
+    """act = quantize(silu(gate) * up) over rows of `ffn` values with row stride `ld`."""
+    _lib.check(_lib.load().dcg_swiglu_quantize(_ptr(gate), _ptr(up), ld, m, ffn, act_type, _ptr(act),
+                                               _stream()), "dcg_swiglu_quantize")
+    return act
+
+
+def qk_norm_rope_kv_append(q, ldq, k, ldk, v, ldv, n_seqs, hq, hkv, q_norm_w, k_norm_w, eps, theta,
+                           positions, q_out, k_arena, v_arena, n_layer, layer, block_tables):
+    """Per-head RMSNorm + NeoX RoPE of q and k; q -> q_out, k/v -> fp16 paged slots."""
+    _lib.check(_lib.load().dcg_qk_norm_rope_kv_append(
+        _ptr(q), ldq, _ptr(k), ldk, _ptr(v), ldv, n_seqs, hq, hkv, 128, _ptr(q_norm_w), _ptr(k_norm_w),
+        eps, theta, _ptr(positions), _ptr(q_out), _ptr(k_arena), _ptr(v_arena), n_layer, layer,
+        _ptr(block_tables), block_tables.shape[1], _stream()), "dcg_qk_norm_rope_kv_append")
+
+
 class HostContext:
     """The synchronous host boundary: weights registered once by host pointer, per-call host
     activations in and host results out (dcg_ctx_*)."""

@@ -154,6 +154,31 @@ int dcg_kv_append(const float* k, const float* v, void* k_arena, void* v_arena, 
                   int head_dim, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
+ * Fused element-wise producers of the matmul inputs (the reference's AddRMSNorm / fused QKV on CPU,
+ * core/include/simd_ops.h:2437-2763, and the rms_norm / QK-norm / RoPE / SwiGLU graph nodes of
+ * BuildTransformerGraph, core/src/inference.cpp:1124-1313, :1790-1797).  All device pointers.
+ *
+ * dcg_add_rmsnorm_quantize: x[m][k] += delta (if delta != NULL; x updated in place), then
+ *   act = quantize(x * rsqrt(mean(x^2) + eps) * weight) in the dcg_quantize_act layout of act_type.
+ * dcg_swiglu_quantize: act = quantize(silu(gate) * up); gate/up rows of ffn values, row stride ld
+ *   (they may be the two halves of one stacked matmul output).
+ * dcg_qk_norm_rope_kv_append: for each sequence s, query heads and key heads of q/k (row strides
+ *   ldq/ldk, head_dim 128) get a per-head RMSNorm (weights q_norm_w / k_norm_w, Qwen3 QK-norm) and
+ *   NeoX (rotate-half) RoPE at positions[s] with base rope_theta; q goes to q_out[n_seqs][hq][128],
+ *   k and v (row stride ldv) are written as fp16 to slot positions[s] of sequence s (the
+ *   dcg_kv_append layout). */
+int dcg_add_rmsnorm_quantize(float* x, const float* delta, const float* weight, float eps, int64_t m,
+                             int64_t k, int act_type, void* act, void* stream);
+int dcg_swiglu_quantize(const float* gate, const float* up, int64_t ld, int64_t m, int64_t ffn,
+                        int act_type, void* act, void* stream);
+int dcg_qk_norm_rope_kv_append(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v,
+                               int64_t ldv, int n_seqs, int hq, int hkv, int head_dim,
+                               const float* q_norm_w, const float* k_norm_w, float eps, float rope_theta,
+                               const int32_t* positions, float* q_out, void* k_arena, void* v_arena,
+                               int n_layer, int layer, const int32_t* block_tables,
+                               int max_blocks_per_seq, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
  * Host boundary (drop-in for the CPU call sites; synchronous).
  * ------------------------------------------------------------------------------------------- */
 typedef struct dcg_ctx dcg_ctx;

@@ -36,29 +36,30 @@ def reference_step(dec, tokens, ctx_lens):
         x1, x2 = x[..., : D // 2], x[..., D // 2:]
         return np.concatenate([x1 * c - x2 * s, x2 * c + x1 * s], -1)
 
-    def mm(w, x):
-        t = w.qtype
-        rows = w.to_ggml().cpu().numpy()
+    def mm(li, name, x):
+        rows, t, kk = dec.ggml_rows(li, name) if li is not None else (
+            dec.output.to_ggml().cpu().numpy(), dec.output.qtype, dec.output.k)
+        rows = np.ascontiguousarray(rows)
         xq = O.quantize(x.astype(np.float32), O.VEC_DOT_TYPE[t])
-        return O.mul_mat(t, rows, w.k, xq, x.shape[0], nthreads=8).astype(np.float64)
+        return O.mul_mat(t, rows, kk, xq, x.shape[0], nthreads=8).astype(np.float64)
 
     x = dec.tok_embd.cpu().float().numpy().astype(np.float64)[tokens]
-    for li, L in enumerate(dec.layers):
+    for li in range(cfg.n_layer):
         h = rms(x)
-        q = mm(L["attn_q"], h).reshape(B, hq, D)
-        k = mm(L["attn_k"], h).reshape(B, hkv, D)
-        v = mm(L["attn_v"], h).reshape(B, hkv, D)
+        q = mm(li, "attn_q", h).reshape(B, hq, D)
+        k = mm(li, "attn_k", h).reshape(B, hkv, D)
+        v = mm(li, "attn_v", h).reshape(B, hkv, D)
         q, k = rope(rms(q)), rope(rms(k))
         O.kv_append(k.astype(np.float32), v.astype(np.float32), ka, va, cfg.n_layer, li, bt,
                     np.arange(B, dtype=np.int32), pos.astype(np.int32))
         att = O.paged_attn_decode(q.astype(np.float32), ka, va, cfg.n_layer, li, bt,
                                   np.array(ctx_lens, np.int32), hkv, 1.0 / math.sqrt(D), nthreads=8)
-        x = x + mm(L["attn_output"], att.reshape(B, hq * D).astype(np.float64))
+        x = x + mm(li, "attn_output", att.reshape(B, hq * D).astype(np.float64))
         h = rms(x)
-        g = mm(L["ffn_gate"], h)
-        u = mm(L["ffn_up"], h)
-        x = x + mm(L["ffn_down"], g / (1.0 + np.exp(-g)) * u)
-    return mm(dec.output, rms(x))
+        g = mm(li, "ffn_gate", h)
+        u = mm(li, "ffn_up", h)
+        x = x + mm(li, "ffn_down", g / (1.0 + np.exp(-g)) * u)
+    return mm(None, None, rms(x))
 
 
 @pytest.mark.parametrize("layout", ["q8_0", "q4_k_m"])
