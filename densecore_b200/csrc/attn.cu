@@ -19,6 +19,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <math.h>
+#include <stdlib.h>
 
 #include "../../include/dcgpu.h"
 #include "common.cuh"
@@ -378,6 +379,250 @@ __global__ void __launch_bounds__((AT_CONS + 1) * 32) paged_attn_tma_kernel(
     }
 }
 
+// ------------------------------------------------------------------------------------------
+// Tensor-core variant (the one launched).  Per 16-token KV block, per consumer warp:
+//   S^T[rep][t] = Q K^T : mma m16n8k16 f16 -> f32, A = Q (NREP query heads as rows, zero-padded to
+//                 16; k = 16 dims per step; held in registers), B = K rows via ldmatrix.x4;
+//   online softmax on the S^T accumulators (each lane: one head, 4 tokens);
+//   O += P V   : the S^T accumulator layout is the A-fragment layout of P (FlashAttention-2's
+//                register reuse), B = V via ldmatrix.x4.trans.
+// Q and P enter the f16 mma as hi + lo halves (x = hi + lo exactly to ~2^-22), K and V are exact
+// fp16, accumulation is fp32: results match an fp32 computation to ~1e-6.
+// Tiles arrive by TMA with 128-byte swizzle (two 64-dim halves per tile) so every ldmatrix is
+// bank-conflict free: 16-byte chunk c of row r sits at chunk c ^ (r & 7).
+// ------------------------------------------------------------------------------------------
+constexpr int MA_CONS = 8;                 // consumer warps (+1 producer)
+constexpr int MA_STAGES = 8;
+constexpr int MA_HALF = KVB * 64 * 2;      // 2 KB: 16 rows x 64 dims
+constexpr int MA_STAGE = 4 * MA_HALF;      // K lo | K hi | V lo | V hi = 8 KB
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void mma_f16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// (x0, x1) -> hi = fp16x2(x), lo = fp16x2(x - hi)
+__device__ __forceinline__ void split_h2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+// smem byte address of 16-byte chunk c (0..15 over 128 dims) of row r in a swizzled half pair
+__device__ __forceinline__ uint32_t swz(uint32_t tile, int r, int c) {
+    const uint32_t half = tile + (uint32_t)(c >> 3) * MA_HALF;
+    return half + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+}
+
+template <int NREP>
+__global__ void __launch_bounds__((MA_CONS + 1) * 32, 2) paged_attn_mma_kernel(
+    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+    const float* __restrict__ q, int n_layer, int layer, const int* __restrict__ bt, int mbs,
+    const int* __restrict__ ctx, int hq, int hkv, float scale_log2, int bps, int splits,
+    float* __restrict__ part_o, float* __restrict__ part_ml, float* __restrict__ out) {
+    extern __shared__ __align__(128) uint8_t dsm[];
+    uint64_t* full = (uint64_t*)dsm;
+    uint64_t* empty = full + MA_STAGES;
+    // ring at the first 1024-byte boundary past the barriers: the 128-byte swizzle repeats per 1 KB
+    const uint32_t dsm_s = smem_u32(dsm);
+    uint8_t* ring = dsm + ((((dsm_s + 256 + 1023) & ~1023u)) - dsm_s);
+    __shared__ float wm[MA_CONS][NREP], wl[MA_CONS][NREP];
+    __shared__ __align__(16) uint4 qfrag[8][32];  // per k-step, per lane: {hi a0, hi a2, lo a0, lo a2}
+
+    pdl_wait();
+    const int seq = blockIdx.x / hkv, kvh = blockIdx.x % hkv, split = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gid = lane >> 2, tig = lane & 3;
+    const int L = ctx[seq];
+    const int nblk = (L + KVB - 1) / KVB;
+    const int b0 = split * bps, b1 = min(nblk, b0 + bps);
+    const int nbh = max(0, b1 - b0);
+    const size_t pidx = ((size_t)blockIdx.x * splits + split) * NREP;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < MA_STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    // Q as the mma A operand: row gid = query head kvh*NREP + gid (zero rows beyond NREP);
+    // k-step j covers dims 16j .. 16j+15: a0 <- dims 16j+2tig,+1 ; a2 <- dims 16j+8+2tig,+1.
+    // Built once by warp 0 into shared memory (registers go to the O accumulators).
+    if (warp == 0) {
+        const float* qr = q + ((size_t)seq * hq + kvh * NREP + (gid < NREP ? gid : 0)) * HD;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            uint32_t h[2], l[2];
+#pragma unroll
+            for (int hlf = 0; hlf < 2; hlf++) {
+                const int d = 16 * j + 8 * hlf + 2 * tig;
+                float x0 = 0.0f, x1 = 0.0f;
+                if (gid < NREP) {
+                    x0 = qr[d] * scale_log2;
+                    x1 = qr[d + 1] * scale_log2;
+                }
+                split_h2(x0, x1, h[hlf], l[hlf]);
+            }
+            qfrag[j][lane] = make_uint4(h[0], h[1], l[0], l[1]);
+        }
+    }
+    __syncthreads();
+
+    bool ok = true;
+    if (warp == MA_CONS) {  // producer: 4 swizzled half-tiles per block
+        if (lane == 0) {
+            for (int i = 0; i < nbh && ok; i++) {
+                const int st = i % MA_STAGES;
+                if (i >= MA_STAGES)
+                    ok = mbar_wait(&empty[st], (uint32_t)(((i / MA_STAGES) - 1) & 1), &g_attn_error);
+                if (!ok) break;
+                const int phys = bt[(size_t)seq * mbs + b0 + i];
+                const int slot = (phys * n_layer + layer) * KVB;
+                uint8_t* dst = ring + (size_t)st * MA_STAGE;
+                mbar_arrive_expect_tx(&full[st], MA_STAGE);
+                tma_load_3d(dst, &kmap, 0, kvh, slot, &full[st]);
+                tma_load_3d(dst + MA_HALF, &kmap, 64, kvh, slot, &full[st]);
+                tma_load_3d(dst + 2 * MA_HALF, &vmap, 0, kvh, slot, &full[st]);
+                tma_load_3d(dst + 3 * MA_HALF, &vmap, 64, kvh, slot, &full[st]);
+            }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
+
+    float o[16][2];  // O[head gid][dims 8n + 2tig, +1]
+#pragma unroll
+    for (int n = 0; n < 16; n++) o[n][0] = o[n][1] = 0.0f;
+    float mrow = -INFINITY, lrow = 0.0f;
+    const uint32_t ring_s = smem_u32(ring);
+    // ldmatrix lane roles: matrix mi = lane >> 3, row within matrix = lane & 7
+    const int mi = lane >> 3, mr = lane & 7;
+
+    for (int i = warp; i < nbh && warp < MA_CONS && ok; i += MA_CONS) {
+        const int st = i % MA_STAGES;
+        ok = mbar_wait(&full[st], (uint32_t)((i / MA_STAGES) & 1), &g_attn_error);
+        if (!ok) break;
+        const uint32_t kt = ring_s + (uint32_t)st * MA_STAGE;
+        const uint32_t vt = kt + 2 * MA_HALF;
+        const int ntok = min(KVB, L - (b0 + i) * KVB);
+        // ---- S^T = Q K^T: two token tiles (0-7, 8-15) ----
+        float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            // matrices: m0 tok 0-7 dims 16j.., m1 tok 0-7 dims 16j+8.., m2 tok 8-15 dims 16j.., m3 tok 8-15 dims 16j+8..
+            const int tok = (mi >> 1) * 8 + mr, ch = 2 * j + (mi & 1);
+            uint32_t k0, k1, k2, k3;
+            ldsm_x4(swz(kt, tok, ch), k0, k1, k2, k3);
+            const uint4 qf = qfrag[j][lane];
+            mma_f16(sacc[0], qf.x, 0u, qf.y, 0u, k0, k1);
+            mma_f16(sacc[0], qf.z, 0u, qf.w, 0u, k0, k1);
+            mma_f16(sacc[1], qf.x, 0u, qf.y, 0u, k2, k3);
+            mma_f16(sacc[1], qf.z, 0u, qf.w, 0u, k2, k3);
+        }
+        // lane: head gid, tokens 2tig, 2tig+1 (tile 0) and 8+2tig, 9+2tig (tile 1)
+        float sv[4] = {sacc[0][0], sacc[0][1], sacc[1][0], sacc[1][1]};
+        const int tk[4] = {2 * tig, 2 * tig + 1, 8 + 2 * tig, 9 + 2 * tig};
+        float mx = -INFINITY;
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            if (tk[u] >= ntok) sv[u] = -INFINITY;
+            mx = fmaxf(mx, sv[u]);
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float mn = fmaxf(mrow, mx);  // finite: the block has >= 1 token
+        const float corr = exp2f(mrow - mn);
+        float p[4], ps = 0.0f;
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            p[u] = tk[u] < ntok ? exp2f(sv[u] - mn) : 0.0f;
+            ps += p[u];
+        }
+        ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+        lrow = lrow * corr + ps;
+        mrow = mn;
+#pragma unroll
+        for (int n = 0; n < 16; n++) {
+            o[n][0] *= corr;
+            o[n][1] *= corr;
+        }
+        // ---- O += P V: A = P (head rows, k = 16 tokens), B = V^T via ldmatrix.trans ----
+        uint32_t ph0, pl0, ph1, pl1;
+        split_h2(p[0], p[1], ph0, pl0);   // a0: tokens 2tig, 2tig+1
+        split_h2(p[2], p[3], ph1, pl1);   // a2: tokens 8+2tig, 9+2tig
+#pragma unroll
+        for (int n2 = 0; n2 < 8; n2++) {
+            // matrices: m0 tok 0-7 dims 16n2.., m1 tok 8-15 dims 16n2.., m2 tok 0-7 dims 16n2+8.., m3 tok 8-15 dims 16n2+8..
+            const int tok = (mi & 1) * 8 + mr, ch = 2 * n2 + (mi >> 1);
+            uint32_t v0, v1, v2, v3;
+            ldsm_x4_t(swz(vt, tok, ch), v0, v1, v2, v3);
+            float c0[4] = {o[2 * n2][0], o[2 * n2][1], 0.f, 0.f};
+            float c1[4] = {o[2 * n2 + 1][0], o[2 * n2 + 1][1], 0.f, 0.f};
+            mma_f16(c0, ph0, 0u, ph1, 0u, v0, v1);
+            mma_f16(c0, pl0, 0u, pl1, 0u, v0, v1);
+            mma_f16(c1, ph0, 0u, ph1, 0u, v2, v3);
+            mma_f16(c1, pl0, 0u, pl1, 0u, v2, v3);
+            o[2 * n2][0] = c0[0];
+            o[2 * n2][1] = c0[1];
+            o[2 * n2 + 1][0] = c1[0];
+            o[2 * n2 + 1][1] = c1[1];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    pdl_trigger();
+    ok = __syncthreads_and(ok);
+    if (!ok) return;
+    // ---- merge the consumer warps (stage ring reused as [warp][head][dim]) ----
+    float* wacc = (float*)ring;
+    if (warp < MA_CONS && gid < NREP) {
+        if (tig == 0) { wm[warp][gid] = mrow; wl[warp][gid] = lrow; }
+#pragma unroll
+        for (int n = 0; n < 16; n++)
+            *(float2*)&wacc[((size_t)warp * NREP + gid) * HD + 8 * n + 2 * tig] = make_float2(o[n][0], o[n][1]);
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < NREP * HD; idx += blockDim.x) {
+        const int r = idx / HD, dd = idx % HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < MA_CONS; w++) M = fmaxf(M, wm[w][r]);
+        float Ls = 0.0f, O = 0.0f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < MA_CONS; w++) {
+                const float f = wl[w][r] > 0.0f ? exp2f(wm[w][r] - M) : 0.0f;
+                Ls += wl[w][r] * f;
+                O += wacc[((size_t)w * NREP + r) * HD + dd] * f;
+            }
+        }
+        if (out) {
+            out[((size_t)seq * hq + kvh * NREP + r) * HD + dd] = Ls > 0.0f ? O / Ls : 0.0f;
+        } else {
+            part_o[(pidx + r) * HD + dd] = O;
+            if (dd == 0) {
+                part_ml[(pidx + r) * 2] = M;
+                part_ml[(pidx + r) * 2 + 1] = Ls;
+            }
+        }
+    }
+}
+
 // out[seq][h][:] = sum_s O_s 2^(m_s - M) / sum_s l_s 2^(m_s - M); one CTA of 128 threads per (seq, h)
 __global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
                                     float* __restrict__ out, int hq, int hkv, int nrep, int splits) {
@@ -427,10 +672,14 @@ __global__ void kv_append_kernel(const float* __restrict__ k, const float* __res
     varena[dst] = __float2half_rn(v[i]);
 }
 
+// split planner: enough CTAs for `target` (default 4 x 148) and at most `maxb` (default 64) KV blocks per CTA
+// (DCG_ATTN_TARGET / DCG_ATTN_MAXB override both, for tuning)
 void attn_plan(int n_seqs, int hkv, int max_ctx, int* splits, int* bps) {
+    static const int target = getenv("DCG_ATTN_TARGET") ? atoi(getenv("DCG_ATTN_TARGET")) : 4 * 148;
+    static const int maxb = getenv("DCG_ATTN_MAXB") ? atoi(getenv("DCG_ATTN_MAXB")) : 64;
     const int max_nblk = max(1, (max_ctx + KVB - 1) / KVB);
-    int sp = max(1, (4 * 148 + n_seqs * hkv - 1) / (n_seqs * hkv));
-    sp = max(sp, (max_nblk + 31) / 32);  // at most 32 blocks (512 tokens) per CTA
+    int sp = max(1, (target + n_seqs * hkv - 1) / (n_seqs * hkv));
+    sp = max(sp, (max_nblk + maxb - 1) / maxb);
     sp = min(sp, max_nblk);
     *splits = sp;
     *bps = (max_nblk + sp - 1) / sp;
@@ -446,18 +695,35 @@ size_t attn_scratch_bytes(int n_seqs, int hq, int hkv, int max_ctx) {
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn();  // qmm.cu
 
-// arena as a 3-D fp16 tensor: [slots][hkv][HD]; box = 16 slots x 1 head x HD
+// arena as a 3-D fp16 tensor: [slots][hkv][HD]; box = 16 slots x 1 head x 64 dims, 128-byte swizzle
 static cudaError_t make_kv_map(CUtensorMap* map, const void* arena, int hkv, int64_t n_slots) {
     auto fn = encode_fn();
     if (!fn) return cudaErrorNotSupported;
     const cuuint64_t dims[3] = {(cuuint64_t)HD, (cuuint64_t)hkv, (cuuint64_t)n_slots};
     const cuuint64_t strides[2] = {(cuuint64_t)HD * 2, (cuuint64_t)hkv * HD * 2};
-    const cuuint32_t box[3] = {(cuuint32_t)HD, 1, (cuuint32_t)KVB};
+    const cuuint32_t box[3] = {64, 1, (cuuint32_t)KVB};
     const cuuint32_t es[3] = {1, 1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(arena), dims, strides, box,
-                    es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                    es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <int NR>
+static cudaError_t launch_attn_mma(dim3 grid, cudaStream_t st, const CUtensorMap& km, const CUtensorMap& vm,
+                                   const float* q, int n_layer, int layer, const int* bt, int mbs,
+                                   const int* ctx, int hq, int hkv, float sl2, int bps, int splits,
+                                   float* po, float* pml, float* direct) {
+    static bool attr = false;
+    const size_t dyn = 2048 + (size_t)MA_STAGES * MA_STAGE;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(paged_attn_mma_kernel<NR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)dyn);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    return launch_pdl(paged_attn_mma_kernel<NR>, grid, dim3((MA_CONS + 1) * 32), dyn, st, km, vm, q, n_layer,
+                      layer, bt, mbs, ctx, hq, hkv, sl2, bps, splits, po, pml, direct);
 }
 
 template <int NR>
@@ -496,10 +762,10 @@ cudaError_t launch_paged_attn(const float* q, const void* karena, const void* va
     if (e == cudaSuccess) e = make_kv_map(&vm, varena, hkv, n_slots);
     if (e != cudaSuccess) return e;
     switch (nrep) {
-        case 1: e = launch_attn_tma<1>(grid, st, km, vm, q, n_layer, layer, bt, mbs, ctx, hq, hkv, sl2, bps, splits, po, pml, direct); break;
-        case 2: e = launch_attn_tma<2>(grid, st, km, vm, q, n_layer, layer, bt, mbs, ctx, hq, hkv, sl2, bps, splits, po, pml, direct); break;
-        case 4: e = launch_attn_tma<4>(grid, st, km, vm, q, n_layer, layer, bt, mbs, ctx, hq, hkv, sl2, bps, splits, po, pml, direct); break;
-        case 8: e = launch_attn_tma<8>(grid, st, km, vm, q, n_layer, layer, bt, mbs, ctx, hq, hkv, sl2, bps, splits, po, pml, direct); break;
+        case 1: e = launch_attn_mma<1>(grid, st, km, vm, q, n_layer, layer, bt, mbs, ctx, hq, hkv, sl2, bps, splits, po, pml, direct); break;
+        case 2: e = launch_attn_mma<2>(grid, st, km, vm, q, n_layer, layer, bt, mbs, ctx, hq, hkv, sl2, bps, splits, po, pml, direct); break;
+        case 4: e = launch_attn_mma<4>(grid, st, km, vm, q, n_layer, layer, bt, mbs, ctx, hq, hkv, sl2, bps, splits, po, pml, direct); break;
+        case 8: e = launch_attn_mma<8>(grid, st, km, vm, q, n_layer, layer, bt, mbs, ctx, hq, hkv, sl2, bps, splits, po, pml, direct); break;
         default: return cudaErrorInvalidValue;
     }
     if (e != cudaSuccess || splits == 1) return e;
