@@ -281,8 +281,9 @@ int dcg_qk_norm_rope_kv_append(const float* q, int64_t ldq, const float* k, int6
                                const int32_t* positions, float* q_out, void* k_arena, void* v_arena,
                                int n_layer, int layer, const int32_t* block_tables,
                                int max_blocks_per_seq, void* stream) {
-    if (!q || !k || !v || !q_norm_w || !k_norm_w || !positions || !q_out || !k_arena || !v_arena || !block_tables)
+    if (!q || !k || !v || !positions || !q_out || !k_arena || !v_arena || !block_tables)
         return fail(DCG_EINVAL, "null pointer");
+    if (!q_norm_w != !k_norm_w) return fail(DCG_EINVAL, "give both QK-norm weights or neither");
     if (head_dim != 128) return fail(DCG_EINVAL, "head_dim must be 128");
     if (n_seqs < 0 || hq <= 0 || hkv <= 0 || n_layer <= 0 || layer < 0 || layer >= n_layer || max_blocks_per_seq <= 0)
         return fail(DCG_EINVAL, "bad shape");

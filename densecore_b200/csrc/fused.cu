@@ -120,14 +120,16 @@ __global__ void __launch_bounds__(FUSE_THREADS) qk_rope_append_kernel(
     const float* nw = is_q ? qw : kw;
     const int d0 = 2 * lane, d1 = 64 + 2 * lane;
     float x0 = src[d0], x1 = src[d0 + 1], y0 = src[d1], y1 = src[d1 + 1];
-    float ss = x0 * x0 + x1 * x1 + y0 * y0 + y1 * y1;
+    if (nw) {  // QK-norm (Qwen3); skipped when no norm weight is given (Llama)
+        float ss = x0 * x0 + x1 * x1 + y0 * y0 + y1 * y1;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float rs = rsqrtf(ss / (float)D + eps);
-    x0 *= rs * nw[d0];
-    x1 *= rs * nw[d0 + 1];
-    y0 *= rs * nw[d1];
-    y1 *= rs * nw[d1 + 1];
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float rs = rsqrtf(ss / (float)D + eps);
+        x0 *= rs * nw[d0];
+        x1 *= rs * nw[d0 + 1];
+        y0 *= rs * nw[d1];
+        y1 *= rs * nw[d1 + 1];
+    }
     // NeoX rotate-half: (x_i, x_{i+64}) at angle p * theta^(-2i/D)
     const float p = (float)pos[s];
     const float f0 = (float)exp2(-(double)(2 * d0) / D * log2((double)theta));

@@ -48,11 +48,34 @@ class DecoderConfig:
     # per-layer weight types: default for every linear, overrides by (layer parity, name)
     wtype: int = Q8_0
     q6k_alternate: tuple = ()  # names that are Q6_K in even layers (Q4_K_M layout)
+    qk_norm: bool = True       # Qwen3 per-head RMSNorm of q and k
+    tied: bool = True          # LM head = token embedding
+    out_type: int = -1         # LM head type (-1: Q8_0 for Q8_0 models, else Q6_K)
 
 
 QWEN3_0_6B = DecoderConfig("Qwen3-0.6B", 28, 1024, 16, 8, 128, 3072, 151936, wtype=Q8_0)
 QWEN3_4B = DecoderConfig("Qwen3-4B", 36, 2560, 32, 8, 128, 9728, 151936, wtype=Q4_K,
                          q6k_alternate=("attn_v", "ffn_down"))
+LLAMA3_70B = DecoderConfig("Llama-3-70B", 80, 8192, 64, 8, 128, 28672, 128256, rope_theta=5e5,
+                           rms_eps=1e-5, wtype=Q4_K, qk_norm=False, tied=False, out_type=Q4_K)
+
+
+def tp_plan(cfg: DecoderConfig, rank: int, size: int) -> dict:
+    """Megatron-style tensor-parallel shard of every weight for rank `rank` of `size`:
+    rows (output features) of q/k/v (by kv-head groups), gate/up and the LM head; columns (input
+    features, 256-aligned so every Q4_K/Q6_K/Q8_0 block stays whole) of attn_output and ffn_down,
+    which are followed by an all-reduce.  Values are (start, stop) half-open ranges."""
+    D = cfg.head_dim
+    if cfg.n_head_kv % size or cfg.n_head % size or cfg.ffn % size or cfg.vocab % size:
+        raise ValueError(f"{cfg.name} does not split {size} ways")
+    hq, hkv, ffn, voc = cfg.n_head // size, cfg.n_head_kv // size, cfg.ffn // size, cfg.vocab // size
+    if (hq * D) % 256 or ffn % 256:
+        raise ValueError("K-split shards must be multiples of 256")
+    r = rank
+    return {"q_rows": (r * hq * D, (r + 1) * hq * D), "kv_rows": (r * hkv * D, (r + 1) * hkv * D),
+            "o_cols": (r * hq * D, (r + 1) * hq * D), "ffn_rows": (r * ffn, (r + 1) * ffn),
+            "down_cols": (r * ffn, (r + 1) * ffn), "vocab_rows": (r * voc, (r + 1) * voc),
+            "hq": hq, "hkv": hkv, "ffn": ffn, "vocab": voc}
 
 
 def _wtype(cfg: DecoderConfig, layer: int, name: str) -> int:
@@ -65,24 +88,47 @@ class Decoder:
     """Weights, paged KV cache and the captured decode step for `batch` sequences."""
 
     def __init__(self, cfg: DecoderConfig, batch: int, max_ctx: int, seed: int = 0,
-                 device: str | torch.device = "cuda"):
+                 device: str | torch.device = "cuda", tp_rank: int = 0, tp_size: int = 1,
+                 tp_group=None, shard_init: str = "slice"):
+        """tp_size > 1: this process holds shard tp_rank of every weight (tp_plan) and the KV heads
+        of its query-head group; two all-reduces per layer (after attn_output and ffn_down) and an
+        all-gather of the logits over tp_group (NCCL).  shard_init = "slice": every rank draws the
+        full random weights and keeps its slice (bitwise the tp_size = 1 model); "local": each rank
+        draws only its shard (faster; a different random model)."""
         self.cfg, self.batch, self.max_ctx = cfg, batch, max_ctx
+        self.tp_rank, self.tp_size, self.tp_group = tp_rank, tp_size, tp_group
         dev = self.device = torch.device(device)
         g = torch.Generator(device=dev)
-        g.manual_seed(seed)
+        g.manual_seed(seed if shard_init == "slice" else seed * 1009 + tp_rank)
         H, D = cfg.hidden, cfg.head_dim
-        qd, kvd = cfg.n_head * D, cfg.n_head_kv * D
+        plan = self.plan = tp_plan(cfg, tp_rank, tp_size)
+        local = shard_init == "local"
+        self.hq, self.hkv, self.ffn, self.vocab_r = plan["hq"], plan["hkv"], plan["ffn"], plan["vocab"]
+        qd_full, kvd_full = cfg.n_head * D, cfg.n_head_kv * D
+        qd, kvd = self.hq * D, self.hkv * D
 
-        def qw(n, k, t):
+        def draw(n, k, rows=None, cols=None):
+            """fp32 N(0, 0.02) weight restricted to this rank's rows / cols."""
+            if local:
+                n2 = rows[1] - rows[0] if rows else n
+                k2 = cols[1] - cols[0] if cols else k
+                return torch.randn((n2, k2), generator=g, device=dev) * 0.02
             w = torch.randn((n, k), generator=g, device=dev) * 0.02
-            return ops.QuantWeight.from_float(w, t)
+            if rows:
+                w = w[rows[0]:rows[1]]
+            if cols:
+                w = w[:, cols[0]:cols[1]]
+            return w.contiguous()
+
+        def qw(n, k, t, rows=None, cols=None):
+            return ops.QuantWeight.from_float(draw(n, k, rows, cols), t)
 
         self.layers = []
         for li in range(cfg.n_layer):
             t_q, t_k, t_v = (_wtype(cfg, li, nm) for nm in ("attn_q", "attn_k", "attn_v"))
-            wq = torch.randn((qd, H), generator=g, device=dev) * 0.02
-            wk = torch.randn((kvd, H), generator=g, device=dev) * 0.02
-            wv = torch.randn((kvd, H), generator=g, device=dev) * 0.02
+            wq = draw(qd_full, H, plan["q_rows"])
+            wk = draw(kvd_full, H, plan["kv_rows"])
+            wv = draw(kvd_full, H, plan["kv_rows"])
             L = {"qkv_split": t_v != t_q}
             if t_v == t_q:  # one stacked [q; k; v] weight: rows are quantized independently
                 L["attn_qkv"] = ops.QuantWeight.from_float(torch.cat([wq, wk, wv]), t_q)
@@ -90,23 +136,36 @@ class Decoder:
                 L["attn_qk"] = ops.QuantWeight.from_float(torch.cat([wq, wk]), t_q)
                 L["attn_v"] = ops.QuantWeight.from_float(wv, t_v)
             del wq, wk, wv
-            L["attn_output"] = qw(H, qd, _wtype(cfg, li, "attn_output"))
-            wg = torch.randn((cfg.ffn, H), generator=g, device=dev) * 0.02
-            wu = torch.randn((cfg.ffn, H), generator=g, device=dev) * 0.02
+            L["attn_output"] = qw(H, qd_full, _wtype(cfg, li, "attn_output"), cols=plan["o_cols"])
+            wg = draw(cfg.ffn, H, plan["ffn_rows"])
+            wu = draw(cfg.ffn, H, plan["ffn_rows"])
             L["ffn_gate_up"] = ops.QuantWeight.from_float(torch.cat([wg, wu]), _wtype(cfg, li, "ffn_gate"))
             del wg, wu
-            L["ffn_down"] = qw(H, cfg.ffn, _wtype(cfg, li, "ffn_down"))
+            L["ffn_down"] = qw(H, cfg.ffn, _wtype(cfg, li, "ffn_down"), cols=plan["down_cols"])
             self.layers.append(L)
-        # tied embeddings: the LM head is the quantized token embedding; lookups dequantize it
-        self.output = qw(cfg.vocab, H, cfg.wtype if cfg.wtype == Q8_0 else Q6_K)
-        self.tok_embd = self._dequant_rows(self.output)
+        out_t = cfg.out_type if cfg.out_type >= 0 else (Q8_0 if cfg.wtype == Q8_0 else Q6_K)
+        if cfg.tied:
+            # the LM head is the quantized token embedding; lookups dequantize it (all vocab rows)
+            full = ops.QuantWeight.from_float(draw(cfg.vocab, H) if not local else
+                                              torch.randn((cfg.vocab, H), generator=g, device=dev) * 0.02,
+                                              out_t)
+            self.tok_embd = self._dequant_rows(full)
+            if tp_size == 1:
+                self.output = full
+            else:
+                a, b = plan["vocab_rows"]
+                self.output = ops.QuantWeight.from_ggml(full.to_ggml()[a:b].contiguous(), out_t, H)
+            del full
+        else:
+            self.tok_embd = (torch.randn((cfg.vocab, H), generator=g, device=dev) * 0.02).half()
+            self.output = qw(cfg.vocab, H, out_t, rows=plan["vocab_rows"])
         self.ones_h = torch.ones(H, device=dev)
-        self.ones_d = torch.ones(D, device=dev)
+        self.ones_d = torch.ones(D, device=dev) if cfg.qk_norm else None
 
         # paged KV arena (kv_cache.cpp:353-370 layout): [(block*n_layer + layer)][16][hkv][D] fp16
         self.blocks_per_seq = (max_ctx + KV_BLOCK - 1) // KV_BLOCK
         self.n_blocks = batch * self.blocks_per_seq
-        shape = (self.n_blocks * cfg.n_layer, KV_BLOCK, cfg.n_head_kv, D)
+        shape = (self.n_blocks * cfg.n_layer, KV_BLOCK, self.hkv, D)
         self.k_arena = torch.empty(shape, dtype=torch.float16, device=dev)
         self.v_arena = torch.empty(shape, dtype=torch.float16, device=dev)
         # each sequence owns a shuffled set of physical blocks
@@ -119,6 +178,8 @@ class Decoder:
         self.seq_ids = torch.arange(batch, dtype=torch.int32, device=dev)
         self.next_tokens = torch.zeros(batch, dtype=torch.long, device=dev)
         self.logits = torch.empty((batch, cfg.vocab), device=dev)
+        self.logits_r = torch.empty((batch, self.vocab_r), device=dev)
+        self.gathered = torch.empty((tp_size, batch, self.vocab_r), device=dev)
         self._scratch = {}
         self.graph = None
 
@@ -162,11 +223,11 @@ class Decoder:
     # ---------------------------------------------------------------- the step
     def ggml_rows(self, li: int, name: str):
         """(ggml rows as numpy, type, k) of one logical weight (unstacking the fused ones)."""
-        cfg, D = self.cfg, self.cfg.head_dim
-        qd, kvd = cfg.n_head * D, cfg.n_head_kv * D
+        D = self.cfg.head_dim
+        qd, kvd = self.hq * D, self.hkv * D
         L = self.layers[li]
         spans = {"attn_q": (0, qd), "attn_k": (qd, qd + kvd), "attn_v": (qd + kvd, qd + 2 * kvd),
-                 "ffn_gate": (0, cfg.ffn), "ffn_up": (cfg.ffn, 2 * cfg.ffn)}
+                 "ffn_gate": (0, self.ffn), "ffn_up": (self.ffn, 2 * self.ffn)}
         if name in ("attn_output", "ffn_down") or (name == "attn_v" and L["qkv_split"]):
             w = L[name]
             return w.to_ggml().cpu().numpy(), w.qtype, w.k
@@ -182,7 +243,7 @@ class Decoder:
         quantize, O matmul, fused add+RMSNorm+quantize, stacked gate|up matmul, fused
         SwiGLU+quantize, down matmul (its output is added by the next layer's norm kernel)."""
         cfg, B = self.cfg, self.batch
-        D, hq, hkv, H = cfg.head_dim, cfg.n_head, cfg.n_head_kv, cfg.hidden
+        D, hq, hkv, H, ffn = cfg.head_dim, self.hq, self.hkv, cfg.hidden, self.ffn
         qd, kvd = hq * D, hkv * D
         pos = self._buf("pos", (B,), torch.int32)
         torch.sub(self.ctx_lens, 1, out=pos)
@@ -216,19 +277,32 @@ class Decoder:
             wo = L["attn_output"]
             act_o = self._actbuf(("o", wo.qtype), B, qd, wo.qtype)
             ops.quantize_act(attn_out.view(B, qd), VEC_DOT_TYPE[wo.qtype], out=act_o)
-            yo = self._mm(("o", li), wo, act_o, B)
+            yo = self._allreduce(self._mm(("o", li), wo, act_o, B))
             wgu = L["ffn_gate_up"]
             act_f = self._actbuf(("ffn", wgu.qtype), B, H, wgu.qtype)
             ops.add_rmsnorm_quantize(x, self.ones_h, cfg.rms_eps, VEC_DOT_TYPE[wgu.qtype], act_f, yo)
             ygu = self._mm(("gu", li), wgu, act_f, B)
             wd = L["ffn_down"]
-            act_d = self._actbuf(("down", wd.qtype), B, cfg.ffn, wd.qtype)
-            ops.swiglu_quantize(ygu, ygu[:, cfg.ffn:], 2 * cfg.ffn, B, cfg.ffn, VEC_DOT_TYPE[wd.qtype], act_d)
-            delta = self._mm(("down", li), wd, act_d, B)
+            act_d = self._actbuf(("down", wd.qtype), B, ffn, wd.qtype)
+            ops.swiglu_quantize(ygu, ygu[:, ffn:], 2 * ffn, B, ffn, VEC_DOT_TYPE[wd.qtype], act_d)
+            delta = self._allreduce(self._mm(("down", li), wd, act_d, B))
         act_h = self._actbuf(("head", self.output.qtype), B, H, self.output.qtype)
         ops.add_rmsnorm_quantize(x, self.ones_h, cfg.rms_eps, VEC_DOT_TYPE[self.output.qtype], act_h, delta)
-        self.logits.copy_(self._mm(("head",), self.output, act_h, B))
+        if self.tp_size == 1:
+            self.logits.copy_(self._mm(("head",), self.output, act_h, B))
+        else:  # vocab-split LM head: gather the shards' columns
+            import torch.distributed as dist
+            self.logits_r.copy_(self._mm(("head",), self.output, act_h, B))
+            dist.all_gather_into_tensor(self.gathered, self.logits_r, group=self.tp_group)
+            self.logits.copy_(self.gathered.permute(1, 0, 2).reshape(B, -1))
         self.next_tokens.copy_(torch.argmax(self.logits, dim=-1))
+
+    def _allreduce(self, y):
+        """Sum the K-split partial outputs of attn_output / ffn_down over the tensor-parallel group."""
+        if self.tp_size > 1:
+            import torch.distributed as dist
+            dist.all_reduce(y, group=self.tp_group)
+        return y
 
     def _actbuf(self, key, m, k, wtype):
         at = VEC_DOT_TYPE[wtype]

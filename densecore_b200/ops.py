@@ -224,7 +224,9 @@ def qk_norm_rope_kv_append(q, ldq, k, ldk, v, ldv, n_seqs, hq, hkv, q_norm_w, k_
                            positions, q_out, k_arena, v_arena, n_layer, layer, block_tables):
     """Per-head RMSNorm + NeoX RoPE of q and k; q -> q_out, k/v -> fp16 paged slots."""
     _lib.check(_lib.load().dcg_qk_norm_rope_kv_append(
-        _ptr(q), ldq, _ptr(k), ldk, _ptr(v), ldv, n_seqs, hq, hkv, 128, _ptr(q_norm_w), _ptr(k_norm_w),
+        _ptr(q), ldq, _ptr(k), ldk, _ptr(v), ldv, n_seqs, hq, hkv, 128,
+        _ptr(q_norm_w) if q_norm_w is not None else None,
+        _ptr(k_norm_w) if k_norm_w is not None else None,
         eps, theta, _ptr(positions), _ptr(q_out), _ptr(k_arena), _ptr(v_arena), n_layer, layer,
         _ptr(block_tables), block_tables.shape[1], _stream()), "dcg_qk_norm_rope_kv_append")
 

@@ -163,7 +163,8 @@ int dcg_kv_append(const float* k, const float* v, void* k_arena, void* v_arena, 
  * dcg_swiglu_quantize: act = quantize(silu(gate) * up); gate/up rows of ffn values, row stride ld
  *   (they may be the two halves of one stacked matmul output).
  * dcg_qk_norm_rope_kv_append: for each sequence s, query heads and key heads of q/k (row strides
- *   ldq/ldk, head_dim 128) get a per-head RMSNorm (weights q_norm_w / k_norm_w, Qwen3 QK-norm) and
+ *   ldq/ldk, head_dim 128) get a per-head RMSNorm (weights q_norm_w / k_norm_w, Qwen3 QK-norm; both
+ *   NULL skips it, as for Llama) and
  *   NeoX (rotate-half) RoPE at positions[s] with base rope_theta; q goes to q_out[n_seqs][hq][128],
  *   k and v (row stride ldv) are written as fp16 to slot positions[s] of sequence s (the
  *   dcg_kv_append layout). */
