@@ -15,6 +15,7 @@ vec_dot / quantize_row_q8_K, all host threads) on a bounded sample of the same w
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import statistics
@@ -179,6 +180,59 @@ def decode_bench(which: str, steps: int, dev):
     del dec
     torch.cuda.empty_cache()
     return out
+
+
+def decode_70b(args):
+    """Config 5: Llama-3-70B architecture (random init, Q4_K), decode batch 128, contexts
+    U[1024, 4096] (seed 5), tensor-parallel over the torchrun ranks (NCCL all-reduce x2 per layer)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from densecore_b200 import decoder as D
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    batch, steps = 128, args.steps_70b
+    ctx = np.random.default_rng(5).integers(1024, 4097, batch)
+    cfg = D.LLAMA3_70B if args.layers_70b <= 0 else dataclasses.replace(D.LLAMA3_70B, n_layer=args.layers_70b)
+    dec = D.Decoder(cfg, batch, int(ctx.max()) + steps + 1, seed=5, device=dev, tp_rank=rank,
+                    tp_size=ws, tp_group=dist.group.WORLD if ws > 1 else None, shard_init="local",
+                    seq_tokens=ctx + steps + 1)
+    dec.fill_kv_random()
+    dec.tokens.copy_(torch.from_numpy(np.random.default_rng(6).integers(0, D.LLAMA3_70B.vocab, batch)))
+    dec.ctx_lens.copy_(torch.from_numpy(ctx.astype(np.int32)))
+    dec.capture()
+    for _ in range(2):
+        dec.graph.replay()
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        dec.graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1) / steps], device=dev, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    if rank == 0:
+        per_gpu = dec.step_bytes(ctx)
+        print(json.dumps({"metric": "batched decode tokens/s (Llama-3-70B arch, Q4_K, TP)",
+                          "value": round(batch / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": ws,
+                          "ms_per_step": round(ms, 3), "batch": batch,
+                          "contexts": f"{int(ctx.min())}-{int(ctx.max())} (sum {int(ctx.sum())})",
+                          "min_bytes_per_step_per_gpu": per_gpu,
+                          "achieved_gbs_per_gpu": round(per_gpu / (ms * 1e-3) / 1e9, 1),
+                          "parallelism": f"tp{ws} (2 NCCL all-reduces / layer, logits all-gather)",
+                          "data": "synthetic (random-init weights, seeded random KV history)"}), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def _dist():
@@ -437,6 +491,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3/4 decode tokens/s")
     ap.add_argument("--quick", action="store_true", help="decode: config 3 only")
+    ap.add_argument("--decode-70b", action="store_true",
+                    help="only config 5 (Llama-3-70B arch) tensor-parallel decode over the torchrun ranks")
+    ap.add_argument("--steps-70b", type=int, default=10)
+    ap.add_argument("--layers-70b", type=int, default=0, help="profiling only: fewer layers")
     ap.add_argument("--profile-type", default=None, choices=["q4k", "q8_0", "q6k"],
                     help="run only a small eager GEMV case (for ncu) and exit")
     ap.add_argument("--profile-shape", default="up", choices=["up", "down", "sq"])
@@ -449,6 +507,9 @@ def main():
     args = ap.parse_args()
     if args.profile_type:
         profile_case(args)
+        return
+    if args.decode_70b:
+        decode_70b(args)
         return
     if args.profile_attn:
         attn_case(args.profile_attn, args.profile_iters)

@@ -33,6 +33,7 @@
 
 #include <algorithm>
 #include <mutex>
+#include <stdlib.h>
 
 namespace dcg {
 
@@ -53,12 +54,7 @@ constexpr int QMM_WARPS = 8;     // 4 row groups of 16 x 2 halves of each super-
 constexpr int QMM_KS = 2;        // super-blocks per stage
 constexpr int QMM_STAGES = 3;
 constexpr int Q4K_SROW = QMM_KS * Q4_K_BYTES;         // 288 B = 32 mod 128: conflict-free rows
-constexpr int QMM_XROW = QMM_KS * QK_K + 32;          // 544 B = 32 mod 128
 constexpr int QMM_W_BYTES = QMM_ROWS * Q4K_SROW;      // weight part of a stage
-// xc = activation rows staged per CTA (8*NT, or 1 for the M == 1 kernel)
-__host__ __device__ constexpr int qmm_stage_bytes(int xc) {
-    return QMM_W_BYTES + ((xc * QMM_XROW + xc * QMM_KS * 16 + 127) & ~127);
-}
 
 __device__ __forceinline__ void mma_s8(int* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                        uint32_t b0, uint32_t b1) {
@@ -86,15 +82,13 @@ __device__ __forceinline__ Q4kScales q4k_unpack(const uint4& h) {
     return s;
 }
 
-// DUP (M == 1 only): the single activation row is fed to all 8 mma columns, so every lane's c0 / c2
-// already hold its two rows' results; only those are scaled and only tig == 0 lanes store.
-template <int NT, bool DUP>
+template <int NT>
 __global__ void __launch_bounds__(QMM_THREADS, NT >= 4 ? 1 : (NT >= 2 ? 2 : 3))
     qmm_q4k_kernel(const __grid_constant__ CUtensorMap wmap, int nb, int64_t n, ActQ a,
                    int64_t k, int m, float* __restrict__ y, float* __restrict__ part,
                    int* __restrict__ tickets, int S, int sps) {
-    constexpr int XC = DUP ? 1 : 8 * NT;          // activation rows staged per CTA
-    constexpr int SB_BYTES = qmm_stage_bytes(XC);
+    constexpr int XC = 8 * NT;                    // activation rows staged per CTA
+    constexpr int SB_BYTES = QMM_W_BYTES;         // weights only: activations come through L1
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = (uint64_t*)smem;             // [STAGES] bulk copies landed
     uint64_t* empty = full + QMM_STAGES;          // [STAGES] all warps done with the stage
@@ -105,8 +99,10 @@ __global__ void __launch_bounds__(QMM_THREADS, NT >= 4 ? 1 : (NT >= 2 ? 2 : 3))
     const int gid = lane >> 2, tig = lane & 3;
     const int rg = warp & 3;   // row group: rows 16*rg .. +15 of the CTA
     const int gh = warp >> 2;  // sub-block pairs g = 2*gh, 2*gh+1 (sub-blocks 4*gh .. 4*gh+3)
-    const int64_t r0 = (int64_t)blockIdx.x * QMM_ROWS;
-    const int c0 = blockIdx.y * XC;
+    // grid.x = activation column block (fastest: CTAs over the same weight rows run together and
+    // share them through L2), grid.y = row block
+    const int64_t r0 = (int64_t)blockIdx.y * QMM_ROWS;
+    const int c0 = blockIdx.x * XC;
     const int split = blockIdx.z;
     const int sb0 = split * sps, sb1 = min(nb, sb0 + sps);
     const int nchunks = (sb1 - sb0 + QMM_KS - 1) / QMM_KS;
@@ -130,20 +126,15 @@ __global__ void __launch_bounds__(QMM_THREADS, NT >= 4 ? 1 : (NT >= 2 ? 2 : 3))
             return false;
         const int sbc = sb0 + c * QMM_KS;
         const int nsb = min(QMM_KS, sb1 - sbc);
-        const uint32_t xb = (uint32_t)(nsb * QK_K), bb = (uint32_t)(nsb * 16);
         uint8_t* dst = buf + (size_t)st * SB_BYTES;
         // the weight box is always QMM_ROWS x QMM_KS blocks (rows past n / blocks past the row's end
         // are zero-filled and still counted)
-        if (lane == 0) mbar_arrive_expect_tx(&full[st], (uint32_t)QMM_W_BYTES + (xb + bb) * cols_here);
-        __syncwarp();
-        fence_proxy_async_smem();
-        if (lane == 0) tma_load_2d(dst, &wmap, sbc * (Q4_K_BYTES / 4), (int)r0, &full[st]);
-        for (int cc = lane; cc < cols_here; cc += 32) {
-            const int col = c0 + cc;
-            bulk_g2s(dst + QMM_W_BYTES + cc * QMM_XROW, a.qs + (size_t)col * k + (size_t)sbc * QK_K, xb, &full[st]);
-            bulk_g2s(dst + QMM_W_BYTES + XC * QMM_XROW + cc * (QMM_KS * 16),
-                     a.bs32 + (size_t)col * (k / 32) + (size_t)sbc * 8, bb, &full[st]);
+        if (lane == 0) {
+            mbar_arrive_expect_tx(&full[st], (uint32_t)QMM_W_BYTES);
+            fence_proxy_async_smem();
+            tma_load_2d(dst, &wmap, sbc * (Q4_K_BYTES / 4), (int)r0, &full[st]);
         }
+        __syncwarp();
         return true;
     };
     bool ok = true;
@@ -170,14 +161,12 @@ __global__ void __launch_bounds__(QMM_THREADS, NT >= 4 ? 1 : (NT >= 2 ? 2 : 3))
             for (int t = 0; t < NT; t++)
 #pragma unroll
                 for (int cc = 0; cc < 2; cc++) {
-                    const int col = DUP ? c0 : c0 + t * 8 + 2 * tig + cc;
+                    const int col = c0 + t * 8 + 2 * tig + cc;
                     dxr[s][t][cc] = (s < nsb && col < m) ? __ldg(&xd[(size_t)col * nb_act + sbc + s]) : 0.0f;
                 }
         ok = mbar_wait(&full[c % QMM_STAGES], (uint32_t)((c / QMM_STAGES) & 1), &g_qmm_error) && ok;
         if (!ok) break;
         const uint8_t* stage = buf + (size_t)(c % QMM_STAGES) * SB_BYTES;
-        const uint8_t* xs = stage + QMM_W_BYTES;
-        const int16_t* bss = (const int16_t*)(stage + QMM_W_BYTES + XC * QMM_XROW);
 #ifndef DCG_QMM_NOCOMPUTE
         // both super-blocks of the chunk, unconditionally (ILP): one that is absent (zero-filled by
         // the tensor copy) or belongs to the next split has dx = 0 and adds nothing
@@ -187,11 +176,14 @@ __global__ void __launch_bounds__(QMM_THREADS, NT >= 4 ? 1 : (NT >= 2 ? 2 : 3))
             const uint8_t* rowB = rowA + 8 * Q4K_SROW;
             const uint4 hA = *(const uint4*)rowA, hB = *(const uint4*)rowB;
             const Q4kScales sA = q4k_unpack(hA), sB = q4k_unpack(hB);
-            int isum[NT][4];
+            // scale folding: sc = 8*sh + sl (sh, sl in 0..7), q*sh and q*sl fit int8 and one 32-bit
+            // multiply scales 4 nibbles at once, so all sub-blocks of the super-block accumulate in
+            // two mma accumulators (no per-sub-block integer epilogue): isum = 8*Ch + Cl
+            int ch[NT][4], cl[NT][4];
 #pragma unroll
             for (int t = 0; t < NT; t++)
 #pragma unroll
-                for (int i = 0; i < 4; i++) isum[t][i] = 0;
+                for (int i = 0; i < 4; i++) ch[t][i] = cl[t][i] = 0;
 #pragma unroll
             for (int gg = 0; gg < 2; gg++) {
                 const int g = 2 * gh + gg;
@@ -202,37 +194,45 @@ __global__ void __launch_bounds__(QMM_THREADS, NT >= 4 ? 1 : (NT >= 2 ? 2 : 3))
                 const uint32_t hi0 = (wA.x >> 4) & 0x0F0F0F0Fu, hi1 = (wB.x >> 4) & 0x0F0F0F0Fu;
                 const uint32_t hi2 = (wA.y >> 4) & 0x0F0F0F0Fu, hi3 = (wB.y >> 4) & 0x0F0F0F0Fu;
                 const uint32_t scw_A = gh == 0 ? sA.sc03 : sA.sc47, scw_B = gh == 0 ? sB.sc03 : sB.sc47;
-                const int sA0 = byte_of(scw_A, (2 * g) & 3), sA1 = byte_of(scw_A, (2 * g + 1) & 3);
-                const int sB0 = byte_of(scw_B, (2 * g) & 3), sB1 = byte_of(scw_B, (2 * g + 1) & 3);
+                const uint32_t sA0 = byte_of(scw_A, (2 * g) & 3), sA1 = byte_of(scw_A, (2 * g + 1) & 3);
+                const uint32_t sB0 = byte_of(scw_B, (2 * g) & 3), sB1 = byte_of(scw_B, (2 * g + 1) & 3);
+                // sub-block 2g (low nibbles) and 2g+1 (high nibbles), rows A / B, high / low scale part
+                const uint32_t h0a = lo0 * (sA0 >> 3), h0b = lo1 * (sB0 >> 3), h0c = lo2 * (sA0 >> 3), h0d = lo3 * (sB0 >> 3);
+                const uint32_t l0a = lo0 * (sA0 & 7), l0b = lo1 * (sB0 & 7), l0c = lo2 * (sA0 & 7), l0d = lo3 * (sB0 & 7);
+                const uint32_t h1a = hi0 * (sA1 >> 3), h1b = hi1 * (sB1 >> 3), h1c = hi2 * (sA1 >> 3), h1d = hi3 * (sB1 >> 3);
+                const uint32_t l1a = hi0 * (sA1 & 7), l1b = hi1 * (sB1 & 7), l1c = hi2 * (sA1 & 7), l1d = hi3 * (sB1 & 7);
 #pragma unroll
                 for (int t = 0; t < NT; t++) {
                     uint2 x0 = make_uint2(0, 0), x1 = make_uint2(0, 0);
-                    if (DUP || t * 8 + gid < cols_here) {
-                        const uint8_t* xp = xs + (DUP ? 0 : (t * 8 + gid) * QMM_XROW) + s * QK_K + 64 * g + 8 * tig;
-                        x0 = *(const uint2*)xp;
-                        x1 = *(const uint2*)(xp + 32);
+                    if (t * 8 + gid < cols_here && s < nsb) {
+                        const int8_t* xp = a.qs + (size_t)(c0 + t * 8 + gid) * k + (size_t)(sbc + s) * QK_K +
+                                           64 * g + 8 * tig;
+                        x0 = __ldg((const uint2*)xp);
+                        x1 = __ldg((const uint2*)(xp + 32));
                     }
-                    int c0v[4] = {0, 0, 0, 0}, c1v[4] = {0, 0, 0, 0};
-                    mma_s8(c0v, lo0, lo1, lo2, lo3, x0.x, x0.y);
-                    mma_s8(c1v, hi0, hi1, hi2, hi3, x1.x, x1.y);
-                    isum[t][0] += sA0 * c0v[0] + sA1 * c1v[0];
-                    isum[t][2] += sB0 * c0v[2] + sB1 * c1v[2];
-                    if (!DUP) {
-                        isum[t][1] += sA0 * c0v[1] + sA1 * c1v[1];
-                        isum[t][3] += sB0 * c0v[3] + sB1 * c1v[3];
-                    }
+                    mma_s8(ch[t], h0a, h0b, h0c, h0d, x0.x, x0.y);
+                    mma_s8(cl[t], l0a, l0b, l0c, l0d, x0.x, x0.y);
+                    mma_s8(ch[t], h1a, h1b, h1c, h1d, x1.x, x1.y);
+                    mma_s8(cl[t], l1a, l1b, l1c, l1d, x1.x, x1.y);
                 }
             }
+            int isum[NT][4];
+#pragma unroll
+            for (int t = 0; t < NT; t++)
+#pragma unroll
+                for (int i = 0; i < 4; i++) isum[t][i] = 8 * ch[t][i] + cl[t][i];
             const float2 dA = __half22float2(*reinterpret_cast<const __half2*>(&hA.x));
             const float2 dB = __half22float2(*reinterpret_cast<const __half2*>(&hB.x));
 #pragma unroll
             for (int t = 0; t < NT; t++) {
 #pragma unroll
-                for (int cc = 0; cc < (DUP ? 1 : 2); cc++) {
-                    const int lc = DUP ? 0 : t * 8 + 2 * tig + cc;
+                for (int cc = 0; cc < 2; cc++) {
+                    const int lc = t * 8 + 2 * tig + cc;
                     if (lc >= cols_here) continue;
                     // this warp's half of the min term: sub-blocks 4*gh .. 4*gh+3
-                    const uint2 bs = *(const uint2*)(bss + lc * (QMM_KS * 8) + s * 8 + 4 * gh);
+                    if (s >= nsb) continue;
+                    const uint2 bs = __ldg((const uint2*)(a.bs32 + (size_t)(c0 + lc) * (k / 32) +
+                                                          (size_t)(sbc + s) * 8 + 4 * gh));
                     const float dx = dxr[s][t][cc];
                     const uint32_t mnA = gh == 0 ? sA.mn03 : sA.mn47, mnB = gh == 0 ? sB.mn03 : sB.mn47;
                     const int mA = __dp2a_hi((int)bs.y, (int)mnA, __dp2a_lo((int)bs.x, (int)mnA, 0));
@@ -276,11 +276,7 @@ __global__ void __launch_bounds__(QMM_THREADS, NT >= 4 ? 1 : (NT >= 2 ? 2 : 3))
             for (int i = 0; i < 4; i++) {
                 const int col = c0 + t * 8 + 2 * tig + (i & 1);
                 const int64_t row = i < 2 ? rowA : rowB;
-                if (DUP) {
-                    if (tig == 0 && (i & 1) == 0 && row < n) y[row] = yacc[t][i];
-                } else if (col < m && row < n) {
-                    y[(size_t)col * n + row] = yacc[t][i];
-                }
+                if (col < m && row < n) y[(size_t)col * n + row] = yacc[t][i];
             }
         return;
     }
@@ -291,15 +287,11 @@ __global__ void __launch_bounds__(QMM_THREADS, NT >= 4 ? 1 : (NT >= 2 ? 2 : 3))
             if (!writer) break;
             const int col = c0 + t * 8 + 2 * tig + (i & 1);
             const int64_t row = i < 2 ? rowA : rowB;
-            if (DUP) {
-                if (tig == 0 && (i & 1) == 0 && row < n) part[(size_t)split * n + row] = yacc[t][i];
-            } else if (col < m && row < n) {
-                part[((size_t)split * m + col) * n + row] = yacc[t][i];
-            }
+            if (col < m && row < n) part[((size_t)split * m + col) * n + row] = yacc[t][i];
         }
     __threadfence();
     __syncthreads();
-    int* ticket = &tickets[blockIdx.x * gridDim.y + blockIdx.y];
+    int* ticket = &tickets[blockIdx.y * gridDim.x + blockIdx.x];
     if (threadIdx.x == 0) *flag = (atomicAdd(ticket, 1) == S - 1);
     __syncthreads();
     if (!*flag) return;
@@ -498,7 +490,7 @@ static int qmm_splits(int tiles, int nb, int ctas_per_sm = 3) {
 int qmm_ticket_count(int type, int64_t n, int64_t m) {
     (void)type;
     const int rb = (int)((n + QMM_ROWS - 1) / QMM_ROWS);
-    const int nt = m <= 8 ? 1 : (m <= 16 ? 2 : (m <= 32 ? 4 : 8));
+    const int nt = m <= 8 ? 1 : (m <= 16 ? 2 : 4);
     const int cb = (int)((m + 8 * nt - 1) / (8 * nt));
     return rb * cb;
 }
@@ -507,7 +499,7 @@ size_t qmm_scratch_bytes(int type, int64_t n, int64_t k, int64_t m) {
     (void)type;
     const int nb = (int)(k / QK_K);
     const int rb = (int)((n + QMM_ROWS - 1) / QMM_ROWS);
-    const int nt = m <= 8 ? 1 : (m <= 16 ? 2 : (m <= 32 ? 4 : 8));
+    const int nt = m <= 8 ? 1 : (m <= 16 ? 2 : 4);
     const int cb = (int)((m + 8 * nt - 1) / (8 * nt));
     const int S = m == 1 ? qmm_splits(rb, nb, M1_CTAS) : qmm_splits(rb * cb, nb);
     return align256((size_t)rb * cb * 4) + (S > 1 ? align256((size_t)S * m * n * 4) : 0);
@@ -542,13 +534,13 @@ static cudaError_t make_wmap(CUtensorMap* map, const void* W, int64_t n, size_t 
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <int NT, bool DUP>
+template <int NT>
 static cudaError_t launch_q4k_t(const uint8_t* W, int64_t n, int64_t k, const ActQ& a, int m, float* y,
                                 void* scratch, cudaStream_t st) {
     static bool attr = false;
-    const size_t smem = 128 + (size_t)QMM_STAGES * qmm_stage_bytes(DUP ? 1 : 8 * NT);
+    const size_t smem = 128 + (size_t)QMM_STAGES * QMM_W_BYTES;
     if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(qmm_q4k_kernel<NT, DUP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(qmm_q4k_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
         if (e != cudaSuccess) return e;
         attr = true;
@@ -564,8 +556,8 @@ static cudaError_t launch_q4k_t(const uint8_t* W, int64_t n, int64_t k, const Ac
     CUtensorMap wmap;
     cudaError_t e = make_wmap(&wmap, W, n, (size_t)nb * Q4_K_BYTES);
     if (e != cudaSuccess) return e;
-    dim3 grid(rb, cb, S);
-    return launch_pdl(qmm_q4k_kernel<NT, DUP>, grid, dim3(QMM_THREADS), smem, st, wmap, nb, n, a, k, m, y,
+    dim3 grid(cb, rb, S);
+    return launch_pdl(qmm_q4k_kernel<NT>, grid, dim3(QMM_THREADS), smem, st, wmap, nb, n, a, k, m, y,
                       part, tickets, S, sps);
 }
 
@@ -601,10 +593,9 @@ cudaError_t launch_qmm(int type, const void* packed_w, int64_t n, int64_t k, con
     const ActQ a = act_view(DCG_TYPE_Q8_K, const_cast<void*>(act), m, k);
     const uint8_t* W = (const uint8_t*)packed_w;
     if (m == 1) return launch_q4k_m1(W, n, k, a, y, scratch, st);
-    if (m <= 8) return launch_q4k_t<1, false>(W, n, k, a, (int)m, y, scratch, st);
-    if (m <= 16) return launch_q4k_t<2, false>(W, n, k, a, (int)m, y, scratch, st);
-    if (m <= 32) return launch_q4k_t<4, false>(W, n, k, a, (int)m, y, scratch, st);
-    return launch_q4k_t<8, false>(W, n, k, a, (int)m, y, scratch, st);
+    if (m <= 8) return launch_q4k_t<1>(W, n, k, a, (int)m, y, scratch, st);
+    if (m <= 16) return launch_q4k_t<2>(W, n, k, a, (int)m, y, scratch, st);
+    return launch_q4k_t<4>(W, n, k, a, (int)m, y, scratch, st);
 }
 
 }  // namespace dcg

@@ -89,12 +89,13 @@ class Decoder:
 
     def __init__(self, cfg: DecoderConfig, batch: int, max_ctx: int, seed: int = 0,
                  device: str | torch.device = "cuda", tp_rank: int = 0, tp_size: int = 1,
-                 tp_group=None, shard_init: str = "slice"):
+                 tp_group=None, shard_init: str = "slice", seq_tokens=None):
         """tp_size > 1: this process holds shard tp_rank of every weight (tp_plan) and the KV heads
         of its query-head group; two all-reduces per layer (after attn_output and ffn_down) and an
         all-gather of the logits over tp_group (NCCL).  shard_init = "slice": every rank draws the
         full random weights and keeps its slice (bitwise the tp_size = 1 model); "local": each rank
-        draws only its shard (faster; a different random model)."""
+        draws only its shard (faster; a different random model).  seq_tokens: per-sequence token
+        capacity; the arena then holds exactly those blocks (default: max_ctx for every sequence)."""
         self.cfg, self.batch, self.max_ctx = cfg, batch, max_ctx
         self.tp_rank, self.tp_size, self.tp_group = tp_rank, tp_size, tp_group
         dev = self.device = torch.device(device)
@@ -164,13 +165,22 @@ class Decoder:
 
         # paged KV arena (kv_cache.cpp:353-370 layout): [(block*n_layer + layer)][16][hkv][D] fp16
         self.blocks_per_seq = (max_ctx + KV_BLOCK - 1) // KV_BLOCK
-        self.n_blocks = batch * self.blocks_per_seq
+        if seq_tokens is None:
+            nblk = [self.blocks_per_seq] * batch
+        else:
+            nblk = [(int(t) + KV_BLOCK - 1) // KV_BLOCK for t in seq_tokens]
+        self.n_blocks = sum(nblk)
         shape = (self.n_blocks * cfg.n_layer, KV_BLOCK, self.hkv, D)
         self.k_arena = torch.empty(shape, dtype=torch.float16, device=dev)
         self.v_arena = torch.empty(shape, dtype=torch.float16, device=dev)
         # each sequence owns a shuffled set of physical blocks
         perm = torch.randperm(self.n_blocks, generator=torch.Generator().manual_seed(seed + 1))
-        self.block_tables = perm.view(batch, self.blocks_per_seq).to(torch.int32).to(dev)
+        bt = torch.zeros((batch, self.blocks_per_seq), dtype=torch.int32)
+        o = 0
+        for i, nb in enumerate(nblk):
+            bt[i, :nb] = perm[o:o + nb].to(torch.int32)
+            o += nb
+        self.block_tables = bt.to(dev)
 
         # step buffers (static for graph capture)
         self.tokens = torch.zeros(batch, dtype=torch.long, device=dev)
@@ -215,6 +225,8 @@ class Decoder:
         return t
 
     def _mm(self, key, w: ops.QuantWeight, act, m):
+        # outputs are reused across layers (the stream orders every reuse after the last reader)
+        key = (key[0], w.n, w.k, w.qtype)
         out = self._buf(("y", key), (m, w.n))
         scr = self._buf(("qs", key), (max(1, ops.mul_mat_q_scratch_size(w.qtype, w.n, w.k, m)),),
                         torch.uint8, zero=True)
@@ -337,6 +349,6 @@ class Decoder:
     def step_bytes(self, ctx_lens) -> int:
         w = sum(wt.nbytes for L in self.layers for wt in L.values()
                 if isinstance(wt, ops.QuantWeight)) + self.output.nbytes
-        kv = int(sum(int(c) for c in ctx_lens)) * self.cfg.n_layer * 2 * self.cfg.n_head_kv * \
+        kv = int(sum(int(c) for c in ctx_lens)) * self.cfg.n_layer * 2 * self.hkv * \
             self.cfg.head_dim * 2
         return w + kv
