@@ -369,7 +369,7 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_source": f"{peak_kind} hbm_gbs",
-                         "traffic": traffic, "kernel": "gemv_tma_kernel<Q4_K,M=1>",
+                         "traffic": traffic, "kernel": "qmm_q4k_m1_kernel (Q4_K, M=1)",
                          "alg_bytes_per_step": ALG_BYTES,
                          "kernel_us_per_step": round(gemv_ms_per_step * 1e3, 3)},
             "e2e": {"value": round(ws * WEIGHT_BYTES * e2e_steps / e2e_s / 1e9, 2), "unit": UNIT,
