@@ -141,6 +141,50 @@ def cpu_reference(budget_s: float):
                       f"host threads, oracle restatement of ggml vec_dot_q4_K_q8_K"}
 
 
+def matmul_point(qtype: int, n: int, k: int, m: int, dev, reps: int = 20) -> dict:
+    """One mul_mat shape (activation quantize + matmul), CUDA-graph replays over a weight ring
+    larger than L2; weight GB/s and int8 TOPS."""
+    import torch
+
+    from densecore_b200 import ops
+    from densecore_b200.ggml_types import row_size
+    wbytes = n * row_size(qtype, k)
+    ring = max(2, -(-512 * 2**20 // wbytes))
+    g = torch.Generator(device=dev)
+    g.manual_seed(n + k + m)
+    ws = [ops.QuantWeight.from_float(torch.randn((n, k), generator=g, device=dev) * 0.02, qtype)
+          for _ in range(ring)]
+    x = torch.randn((m, k), generator=g, device=dev)
+    y = torch.empty((m, n), device=dev)
+    scr = torch.empty(ops.mul_mat_scratch_size(qtype, n, k, m), dtype=torch.uint8, device=dev)
+
+    def once():
+        for w in ws:
+            ops.mul_mat(w, x, out=y, scratch=scr)
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        once()
+    torch.cuda.current_stream().wait_stream(side)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        once()
+    for _ in range(3):
+        gr.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * ring)
+    del ws
+    torch.cuda.empty_cache()
+    return {"n": n, "k": k, "m": m, "us": round(us, 2), "weight_gbs": round(wbytes / us / 1e3, 1),
+            "int8_tops": round(2.0 * m * n * k / us / 1e6, 1)}
+
+
 def decode_bench(which: str, steps: int, dev):
     """Batched decode tokens/s of a random-init Qwen3-architecture decoder (BASELINE configs 3/4):
     KV history is seeded random fp16 (prefill is not timed), contexts from the config's seed."""
@@ -379,6 +423,10 @@ def run_ours(args):
             "gpu_launches": 4 * steps,
             "clocks": clk.summary(),
         }
+        if not args.no_sweep:
+            out["config1_q8_0"] = [matmul_point(8, 4096, 4096, m, dev) for m in (1, 8)]
+            out["config2_m_sweep"] = [matmul_point(Q4_K, n, k, m, dev) for m in (16, 64, 256)
+                                      for n, k in SHAPES]
         if not args.no_decode:
             out["decode"] = {"config3": decode_bench("3", 20, dev)}
             if not args.quick:
@@ -491,6 +539,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3/4 decode tokens/s")
     ap.add_argument("--quick", action="store_true", help="decode: config 3 only")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the config-1 / config-2 M sweep")
     ap.add_argument("--decode-70b", action="store_true",
                     help="only config 5 (Llama-3-70B arch) tensor-parallel decode over the torchrun ranks")
     ap.add_argument("--steps-70b", type=int, default=10)
