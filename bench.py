@@ -38,8 +38,9 @@ def q4k_bytes(n, k):
 
 
 WEIGHT_BYTES = sum(q4k_bytes(n, k) for n, k in SHAPES)
-# algorithmic bytes of one GEMV launch: weights + Q8_K activation (qs + d + bsums) + f32 output
-ALG_BYTES = sum(q4k_bytes(n, k) + k + (k // 256) * 4 + (k // 16) * 2 + n * 4 for n, k in SHAPES)
+# algorithmic bytes of one step (two launches of the M=1 kernel, which quantizes x itself):
+# weights + f32 activation + f32 output
+ALG_BYTES = sum(q4k_bytes(n, k) + 4 * k + 4 * n for n, k in SHAPES)
 
 
 def read_peak():
@@ -314,33 +315,22 @@ def run_ours(args):
     ys = [torch.empty((1, n), device=dev) for n, _ in SHAPES]
     scr = [torch.empty(ops.mul_mat_scratch_size(Q4_K, n, k, 1), dtype=torch.uint8, device=dev)
            for n, k in SHAPES]
-    qscr = [torch.zeros(max(1, ops.mul_mat_q_scratch_size(Q4_K, n, k, 1)), dtype=torch.uint8,
-                        device=dev) for n, k in SHAPES]
-    acts = [ops.quantize_act(x, Q8_K) for x in xs]
     torch.cuda.synchronize()
 
-    def ring_pass():          # RING steps, each = 2 x (quantize + GEMV)
+    def ring_pass():          # RING steps, each = 2 launches of the M=1 kernel (quantize fused)
         for s in range(RING):
             for j in range(2):
                 ops.mul_mat(ring[s][j], xs[j], out=ys[j], scratch=scr[j])
-
-    def gemv_pass():          # the GEMV kernels alone, same weights
-        for s in range(RING):
-            for j in range(2):
-                ops.mul_mat_q(ring[s][j], acts[j], 1, out=ys[j], scratch=qscr[j])
 
     # CUDA graphs: one ring pass per replay (launch overhead off the timed path)
     side = torch.cuda.Stream(device=dev)
     side.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(side):
         ring_pass()
-        gemv_pass()
     torch.cuda.current_stream().wait_stream(side)
-    g_step, g_gemv = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    g_step = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_step):
         ring_pass()
-    with torch.cuda.graph(g_gemv):
-        gemv_pass()
 
     reps = max(1, (args.steps + RING - 1) // RING)
     steps = reps * RING
@@ -361,17 +351,8 @@ def run_ours(args):
     if ws > 1:
         dist.barrier()
 
-    # kernel-only timing of the GEMV (the dominant kernel)
-    for _ in range(3):
-        g_gemv.replay()
-    torch.cuda.synchronize()
-    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    k0.record()
-    for _ in range(reps):
-        g_gemv.replay()
-    k1.record()
-    torch.cuda.synchronize()
-    gemv_ms_per_step = k0.elapsed_time(k1) / steps
+    # the step graph holds only the two M=1 kernel launches per step: the kernel time is the step time
+    gemv_ms_per_step = ms / steps
 
     # e2e through the host-pointer ABI (weights registered once; x / y cross PCIe every call)
     ctx = ops.HostContext(local)
@@ -413,14 +394,15 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_source": f"{peak_kind} hbm_gbs",
-                         "traffic": traffic, "kernel": "qmm_q4k_m1_kernel (Q4_K, M=1)",
+                         "traffic": traffic,
+                         "kernel": "qmm_q4k_m1_kernel<true> (Q4_K, M=1, Q8_K quantize fused)",
                          "alg_bytes_per_step": ALG_BYTES,
                          "kernel_us_per_step": round(gemv_ms_per_step * 1e3, 3)},
             "e2e": {"value": round(ws * WEIGHT_BYTES * e2e_steps / e2e_s / 1e9, 2), "unit": UNIT,
                     "h2d_bytes_per_step": sum(4 * k for _, k in SHAPES),
                     "d2h_bytes_per_step": sum(4 * n for n, _ in SHAPES),
                     "steps": e2e_steps, "api": "dcg_ctx_mul_mat (host pointers)"},
-            "gpu_launches": 4 * steps,
+            "gpu_launches": 2 * steps,
             "clocks": clk.summary(),
         }
         if not args.no_sweep:
@@ -482,10 +464,9 @@ def profile_case(args):
     m = args.profile_m
     w = ops.QuantWeight.from_float(torch.randn((n, k), device="cuda") * 0.02, qtype)
     x = torch.randn((m, k), device="cuda")
-    act = ops.quantize_act(x, Q8_K if qtype != 8 else 8)
     y = torch.empty((m, n), device="cuda")
     for _ in range(args.profile_iters):
-        ops.mul_mat_q(w, act, m, out=y)
+        ops.mul_mat(w, x, out=y)
     torch.cuda.synchronize()
     print("profile case done", qtype, n, k, m)
 

@@ -73,6 +73,10 @@ static int enqueue_mul_mat_q(int type, const void* w, int64_t n, int64_t k, cons
 
 static int enqueue_mul_mat(int type, const void* w, int64_t n, int64_t k, const float* x,
                            int64_t m, float* y, void* scratch, cudaStream_t st) {
+    if (dcg::qmm_m1_fused_supports(type, n, k, m)) {
+        DCG_CUDA(dcg::launch_qmm_m1_fused(w, n, k, x, y, st), "qmm m1");
+        return DCG_OK;
+    }
     void* qs = (uint8_t*)scratch + dcg::act_bytes(act_type_of(type), m, k);
     const int nt = dcg::qmm_supports(type) ? dcg::qmm_ticket_count(type, n, m) : 0;
     DCG_CUDA(dcg::launch_quantize_act(act_type_of(type), x, scratch, m, k, true, st, (int*)qs, nt),

@@ -21,6 +21,10 @@ cudaError_t launch_gemv(int type, const void* packed_w, int64_t n, int64_t k, co
 size_t qmm_scratch_bytes(int type, int64_t n, int64_t k, int64_t m);
 // ints at the start of the qmm scratch that must be zero when a qmm launch starts (left zero)
 int qmm_ticket_count(int type, int64_t n, int64_t m);
+// M == 1 Q4_K with the activation quantized inside the matmul kernel (no scratch)
+bool qmm_m1_fused_supports(int type, int64_t n, int64_t k, int64_t m);
+cudaError_t launch_qmm_m1_fused(const void* packed_w, int64_t n, int64_t k, const float* x, float* y,
+                                cudaStream_t st);
 cudaError_t launch_qmm(int type, const void* packed_w, int64_t n, int64_t k, const void* act,
                        int64_t m, float* y, void* scratch, cudaStream_t st);
 cudaError_t qmm_device_error(int* out, bool clear);

@@ -21,14 +21,15 @@
 // sum_j m_j * bsum32_j uses dp2a on the packed 6-bit mins and the pair-summed Q8_K block sums;
 // then y += dx * (d * isum - dmin * msum) in fp32 once per super-block.
 //
-// Split-K partials go to scratch; the last CTA of a tile (atomic ticket) adds them in split order,
-// so results are deterministic.  Tickets must be zero when a launch starts and are left zero
+// Split-K partials (M > 1) go to scratch; the last CTA of a tile (atomic ticket) adds them in split
+// order, so results are deterministic.  Tickets must be zero when a launch starts and are left zero
 // (dcg_mul_mat clears them inside its activation-quantize launch).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
 #include "kernels.h"
+#include "quant_dev.cuh"
 #include "tma.cuh"
 
 #include <algorithm>
@@ -315,38 +316,68 @@ __global__ void __launch_bounds__(QMM_THREADS, NT >= 4 ? 1 : (NT >= 2 ? 2 : 3))
 // int32 dot of row r with sub-block c in C[r][c].  Lane (gid, tig) thus ends a super-block holding
 // the dots of sub-blocks 2*tig, 2*tig+1 for rows gid and gid+8 and applies their 6-bit scales and
 // mins itself; only lanes with gid>>1 == tig feed nonzero activation bytes (others read a zero pad).
-// The 4 lanes of a row add their partial sums once at the end.
+//
+// The CTA's slice of the activation (its split's super-blocks) sits in shared memory for the whole
+// launch: either quantized to Q8_K right here from the fp32 input (QX: dcg_mul_mat's fused path,
+// the same arithmetic and bytes as the stand-alone quantize kernel) or copied from a quantized
+// activation, by all five warps, while the producer warp's first weight fill is in flight.  The
+// ring is then kept full by that producer warp.  The S split-K CTAs of a row block form one thread
+// block cluster; rank 0 adds their 64-row partials in rank order through distributed shared memory
+// (deterministic, no global partials, no tickets).
 // ------------------------------------------------------------------------------------------
 constexpr int M1_WARPS = 4;        // consumer warps; warp 4 only issues the copies
 constexpr int M1_THREADS = 160;
-constexpr int M1_KS = 1;                          // super-blocks per stage
-constexpr int M1_SROW = M1_KS * Q4_K_BYTES;        // 144 B: rows gid, gid+1 hit disjoint banks
-constexpr int M1_W_BYTES = QMM_ROWS * M1_SROW;
-constexpr int M1_STAGE = M1_W_BYTES + 384;         // weights | activation (256 B) + pair sums (16 B)
-constexpr int M1_CTAS = 6;                         // resident CTAs per SM
+constexpr int M1_SROW = Q4_K_BYTES;                // 144 B: rows gid, gid+1 hit disjoint banks
+constexpr int M1_STAGE = QMM_ROWS * M1_SROW;       // one super-block of 64 rows
+constexpr int M1_HDR = 512;                        // barriers | zero pad | 64 row partials
+constexpr int M1_XQ = QK_K + 16 + 4;               // per super-block: quants, pair sums, d
+constexpr int M1_MAX_SPS = 32;                     // activation slice: at most 32 super-blocks
+constexpr int M1_CTAS = 4;     // resident CTAs per SM (swept 2..6 x 2..7 stages on config 2)
+constexpr int M1_STAGES = 4;   // weight ring depth
+constexpr int M1_MAX_CLUSTER = 8;                  // portable cluster size bounds the splits
 
+__device__ __forceinline__ float ld_cluster_f32(const float* p, uint32_t rank) {
+    uint32_t addr;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(addr) : "r"(smem_u32(p)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+template <bool QX>
 __global__ void __launch_bounds__(M1_THREADS, M1_CTAS)
-    qmm_q4k_m1_kernel(const __grid_constant__ CUtensorMap wmap, int nb, int64_t n, ActQ a, int64_t k,
-                      float* __restrict__ y, float* __restrict__ part, int* __restrict__ tickets, int S,
-                      int sps) {
+    qmm_q4k_m1_kernel(const __grid_constant__ CUtensorMap wmap, int nb, int64_t n, ActQ a,
+                      const float* __restrict__ x, float* __restrict__ y, int sps) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = (uint64_t*)smem;
-    uint64_t* empty = full + QMM_STAGES;
-    int* flag = (int*)(smem + 96);
+    uint64_t* empty = full + M1_STAGES;
     uint8_t* zpad = smem + 128;   // 64 zero bytes: the activation words of inactive lanes
-    uint8_t* buf = smem + 256;
+    float* ypart = (float*)(smem + 256);
+    uint8_t* ring = smem + M1_HDR;
+    int8_t* xqs = (int8_t*)(ring + M1_STAGES * M1_STAGE);
+    int16_t* xbs = (int16_t*)(xqs + (size_t)sps * QK_K);
+    float* xd = (float*)(xbs + (size_t)sps * 8);
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int gid = lane >> 2, tig = lane & 3;
     const int64_t r0 = (int64_t)blockIdx.x * QMM_ROWS;
-    const int split = blockIdx.z;
-    const int sb0 = split * sps, sb1 = min(nb, sb0 + sps);
-    const int nchunks = (sb1 - sb0 + M1_KS - 1) / M1_KS;
-    const int rows_here = (int)((n - r0) < QMM_ROWS ? (n - r0) : QMM_ROWS);
+    const int sb0 = blockIdx.z * sps, sb1 = min(nb, sb0 + sps);
+    const int nchunks = sb1 - sb0;
 
     if (threadIdx.x < 16) ((uint32_t*)zpad)[threadIdx.x] = 0u;
+    if (threadIdx.x < QMM_ROWS) ypart[threadIdx.x] = 0.0f;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < QMM_STAGES; s++) {
+        for (int s = 0; s < M1_STAGES; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], M1_WARPS);
         }
@@ -354,61 +385,65 @@ __global__ void __launch_bounds__(M1_THREADS, M1_CTAS)
     }
     __syncthreads();
 
-    // Chunk c: weights (constant: may be fetched before the producing kernel finishes) and the
-    // activation slice + pair sums (after pdl_wait).
-    auto issue_w = [&](int c) {
-        const int st = c % QMM_STAGES;
-        const int sbc = sb0 + c * M1_KS;
-        const int nsb = min(M1_KS, sb1 - sbc);
-        mbar_arrive_expect_tx(&full[st], (uint32_t)M1_W_BYTES + (uint32_t)(nsb * (QK_K + 16)));
+    // producer lane: the first ring fill, then all warps stage the activation slice
+    const int pre = min(M1_STAGES, nchunks);
+    auto issue = [&](int c) {
+        const int st = c % M1_STAGES;
+        mbar_arrive_expect_tx(&full[st], (uint32_t)M1_STAGE);
         fence_proxy_async_smem();
-        tma_load_2d(buf + (size_t)st * M1_STAGE, &wmap, sbc * (Q4_K_BYTES / 4), (int)r0, &full[st]);
+        tma_load_2d(ring + (size_t)st * M1_STAGE, &wmap, (sb0 + c) * (Q4_K_BYTES / 4), (int)r0, &full[st]);
     };
-    auto issue_x = [&](int c) {
-        const int st = c % QMM_STAGES;
-        const int sbc = sb0 + c * M1_KS;
-        const int nsb = min(M1_KS, sb1 - sbc);
-        uint8_t* dst = buf + (size_t)st * M1_STAGE;
-        bulk_g2s(dst + M1_W_BYTES, a.qs + (size_t)sbc * QK_K, (uint32_t)(nsb * QK_K), &full[st]);
-        bulk_g2s(dst + M1_W_BYTES + 256, a.bs32 + (size_t)sbc * 8, (uint32_t)(nsb * 16), &full[st]);
-    };
-    const int pre = min(QMM_STAGES, nchunks);
     if (warp == M1_WARPS && lane == 0)
-        for (int c = 0; c < pre; c++) issue_w(c);
-    pdl_wait();
-    bool ok = true;
-    if (warp == M1_WARPS) {  // producer: keep the ring full, independent of the consumers' progress
-        if (lane == 0) {
-            for (int c = 0; c < pre; c++) issue_x(c);
-            for (int c = pre; c < nchunks && ok; c++) {
-                ok = mbar_wait(&empty[c % QMM_STAGES], (uint32_t)(((c / QMM_STAGES) - 1) & 1), &g_qmm_error);
-                if (ok) {
-                    issue_w(c);
-                    issue_x(c);
-                }
+        for (int c = 0; c < pre; c++) issue(c);
+    constexpr int NW = M1_WARPS + 1;
+    if (QX) {  // quantize: warp w takes super-blocks w, w + 5, ..., two at a time (loads overlap)
+        for (int s = warp; s < nchunks; s += 2 * NW) {
+            const int s2 = s + NW;
+            const bool two = s2 < nchunks;  // warp-uniform
+            const float4* p1 = (const float4*)(x + (size_t)(sb0 + s) * QK_K + lane * 8);
+            const float4* p2 = (const float4*)(x + (size_t)(sb0 + (two ? s2 : s)) * QK_K + lane * 8);
+            const float4 u0 = __ldg(p1), u1 = __ldg(p1 + 1), w0 = __ldg(p2), w1 = __ldg(p2 + 1);
+            const float v1[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+            const float v2[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+            const Q8KLane q1 = warp_q8_K(v1, lane);
+            const Q8KLane q2 = warp_q8_K(v2, lane);
+            *(uint2*)(xqs + s * QK_K + lane * 8) = make_uint2(q1.w0, q1.w1);
+            if ((lane & 3) == 0) xbs[s * 8 + (lane >> 2)] = (int16_t)q1.s32;
+            if (lane == 0) xd[s] = q1.d;
+            if (two) {
+                *(uint2*)(xqs + s2 * QK_K + lane * 8) = make_uint2(q2.w0, q2.w1);
+                if ((lane & 3) == 0) xbs[s2 * 8 + (lane >> 2)] = (int16_t)q2.s32;
+                if (lane == 0) xd[s2] = q2.d;
             }
         }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
+    } else {   // copy the slice of an already quantized activation
+        const int t = threadIdx.x;
+        for (int i = t; i < nchunks * (QK_K / 16); i += M1_THREADS)
+            ((uint4*)xqs)[i] = __ldg((const uint4*)(a.qs + (size_t)sb0 * QK_K) + i);
+        for (int i = t; i < nchunks * 8; i += M1_THREADS) xbs[i] = a.bs32[(size_t)sb0 * 8 + i];
+        for (int i = t; i < nchunks; i += M1_THREADS) xd[i] = ((const float*)a.d)[sb0 + i];
     }
+    __syncthreads();
 
-    const bool active = (gid >> 1) == tig;  // feeds column gid (sub-block gid) of every mma
-    const bool odd = gid & 1;                // ... through b1 (odd sub-block) or b0 (even)
-    float yA = 0.0f, yB = 0.0f;
-    for (int c = 0; c < nchunks && ok && warp < M1_WARPS; c++) {
-        const int sbc = sb0 + c * M1_KS;
-        const int nsb = min(M1_KS, sb1 - sbc);
-        float dxr[M1_KS];
-#pragma unroll
-        for (int s = 0; s < M1_KS; s++) dxr[s] = s < nsb ? __ldg(&((const float*)a.d)[sbc + s]) : 0.0f;
-        ok = mbar_wait(&full[c % QMM_STAGES], (uint32_t)((c / QMM_STAGES) & 1), &g_qmm_error) && ok;
-        if (!ok) break;
-        const uint8_t* stage = buf + (size_t)(c % QMM_STAGES) * M1_STAGE;
-        const uint8_t* xs = stage + M1_W_BYTES;
-        const int16_t* bss = (const int16_t*)(stage + M1_W_BYTES + 256);
+    bool ok = true;
+    if (warp == M1_WARPS) {  // producer: keep the ring full
+        if (lane == 0) {
+            for (int c = pre; c < nchunks && ok; c++) {
+                ok = mbar_wait(&empty[c % M1_STAGES], (uint32_t)(((c / M1_STAGES) - 1) & 1), &g_qmm_error);
+                if (ok) issue(c);
+            }
+        }
+    } else {
+        const bool active = (gid >> 1) == tig;  // feeds column gid (sub-block gid) of every mma
+        const bool odd = gid & 1;                // ... through b1 (odd sub-block) or b0 (even)
+        float yA = 0.0f, yB = 0.0f;
+        for (int c = 0; c < nchunks; c++) {
+            const float dx = xd[c];
+            ok = mbar_wait(&full[c % M1_STAGES], (uint32_t)((c / M1_STAGES) & 1), &g_qmm_error);
+            if (!ok) break;
+            const uint8_t* stage = ring + (size_t)(c % M1_STAGES) * M1_STAGE;
 #ifndef DCG_QMM_NOCOMPUTE
-#pragma unroll
-        for (int s = 0; s < M1_KS; s++) {
-            const uint8_t* rowA = stage + (warp * 16 + gid) * M1_SROW + s * Q4_K_BYTES;
+            const uint8_t* rowA = stage + (warp * 16 + gid) * M1_SROW;
             const uint8_t* rowB = rowA + 8 * M1_SROW;
             const uint4 hA = *(const uint4*)rowA, hB = *(const uint4*)rowB;
             // weight words: pair group tig, elements 4i..4i+3 (i = 0..7) of rows gid / gid+8
@@ -417,7 +452,7 @@ __global__ void __launch_bounds__(M1_THREADS, M1_CTAS)
             const uint32_t wa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
             const uint32_t wb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
             // activation words of sub-block gid (active lanes) or zeros
-            const uint8_t* xsrc = active ? xs + s * QK_K + 32 * gid : zpad;
+            const uint8_t* xsrc = active ? (const uint8_t*)xqs + c * QK_K + 32 * gid : zpad;
             const uint4 x0 = *(const uint4*)xsrc, x1 = *(const uint4*)(xsrc + 16);
             const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
             int acc[4] = {0, 0, 0, 0};
@@ -436,44 +471,34 @@ __global__ void __launch_bounds__(M1_THREADS, M1_CTAS)
             const uint32_t mnB = ((tig < 2 ? sB.mn03 : sB.mn47) >> sh) & 0xFFFFu;
             const int isA = (int)(scA & 0xFF) * acc[0] + (int)(scA >> 8) * acc[1];
             const int isB = (int)(scB & 0xFF) * acc[2] + (int)(scB >> 8) * acc[3];
-            const int bsp = *(const int*)(bss + s * 8 + 2 * tig);  // pair sums of sub-blocks 2tig, 2tig+1
+            const int bsp = *(const int*)(xbs + c * 8 + 2 * tig);  // pair sums of sub-blocks 2tig, 2tig+1
             const int msA = __dp2a_lo(bsp, (int)mnA, 0), msB = __dp2a_lo(bsp, (int)mnB, 0);
             const float2 dA = __half22float2(*reinterpret_cast<const __half2*>(&hA.x));
             const float2 dB = __half22float2(*reinterpret_cast<const __half2*>(&hB.x));
-            yA += dxr[s] * (dA.x * (float)isA - dA.y * (float)msA);
-            yB += dxr[s] * (dB.x * (float)isB - dB.y * (float)msB);
-        }
+            yA += dx * (dA.x * (float)isA - dA.y * (float)msA);
+            yB += dx * (dB.x * (float)isB - dB.y * (float)msB);
 #endif
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[c % QMM_STAGES]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[c % M1_STAGES]);
+        }
+        yA += __shfl_xor_sync(0xffffffffu, yA, 1);
+        yA += __shfl_xor_sync(0xffffffffu, yA, 2);
+        yB += __shfl_xor_sync(0xffffffffu, yB, 1);
+        yB += __shfl_xor_sync(0xffffffffu, yB, 2);
+        if (tig == 0) {
+            ypart[warp * 16 + gid] = yA;
+            ypart[warp * 16 + gid + 8] = yB;
+        }
     }
     pdl_trigger();
-    ok = __syncthreads_and(ok);
-    if (!ok) return;
-    yA += __shfl_xor_sync(0xffffffffu, yA, 1);
-    yA += __shfl_xor_sync(0xffffffffu, yA, 2);
-    yB += __shfl_xor_sync(0xffffffffu, yB, 1);
-    yB += __shfl_xor_sync(0xffffffffu, yB, 2);
-    const int64_t rowA = r0 + warp * 16 + gid, rowB = rowA + 8;
-    float* dst = S == 1 ? y : part + (size_t)split * n;
-    if (tig == 0 && warp < M1_WARPS) {
-        if (rowA < n) dst[rowA] = yA;
-        if (rowB < n) dst[rowB] = yB;
-    }
-    if (S == 1) return;
-    __threadfence();
-    __syncthreads();
-    int* ticket = &tickets[blockIdx.x];
-    if (threadIdx.x == 0) *flag = (atomicAdd(ticket, 1) == S - 1);
-    __syncthreads();
-    if (!*flag) return;
-    __threadfence();
-    for (int i = threadIdx.x; i < rows_here; i += blockDim.x) {
+    // every thread of every CTA of the cluster reaches both barriers, on the error path too
+    cluster_sync_all();
+    if (cluster_rank() == 0 && threadIdx.x < QMM_ROWS && r0 + threadIdx.x < n) {
         float sum = 0.0f;
-        for (int q = 0; q < S; q++) sum += __ldcg(&part[(size_t)q * n + r0 + i]);
-        y[r0 + i] = sum;
+        for (uint32_t r = 0; r < gridDim.z; r++) sum += ld_cluster_f32(ypart + threadIdx.x, r);
+        y[r0 + threadIdx.x] = sum;
     }
-    if (threadIdx.x == 0) *ticket = 0;
+    cluster_sync_all();   // keeps every CTA's partials alive until rank 0 has read them
 }
 
 // split-K count: as many splits as still fit one wave of resident CTAs (ctas_per_sm x 148 SMs),
@@ -501,7 +526,7 @@ size_t qmm_scratch_bytes(int type, int64_t n, int64_t k, int64_t m) {
     const int rb = (int)((n + QMM_ROWS - 1) / QMM_ROWS);
     const int nt = m <= 8 ? 1 : (m <= 16 ? 2 : 4);
     const int cb = (int)((m + 8 * nt - 1) / (8 * nt));
-    const int S = m == 1 ? qmm_splits(rb, nb, M1_CTAS) : qmm_splits(rb * cb, nb);
+    const int S = qmm_splits(rb * cb, nb);  // M == 1 needs none of it unless it falls back
     return align256((size_t)rb * cb * 4) + (S > 1 ? align256((size_t)S * m * n * 4) : 0);
 }
 
@@ -538,7 +563,7 @@ template <int NT>
 static cudaError_t launch_q4k_t(const uint8_t* W, int64_t n, int64_t k, const ActQ& a, int m, float* y,
                                 void* scratch, cudaStream_t st) {
     static bool attr = false;
-    const size_t smem = 128 + (size_t)QMM_STAGES * QMM_W_BYTES;
+    const size_t smem = 128 + (size_t)M1_STAGES * QMM_W_BYTES;
     if (!attr) {
         cudaError_t e = cudaFuncSetAttribute(qmm_q4k_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
@@ -561,28 +586,63 @@ static cudaError_t launch_q4k_t(const uint8_t* W, int64_t n, int64_t k, const Ac
                       part, tickets, S, sps);
 }
 
-static cudaError_t launch_q4k_m1(const uint8_t* W, int64_t n, int64_t k, const ActQ& a, float* y,
-                                 void* scratch, cudaStream_t st) {
+// M == 1 grid: row blocks x S splits (one cluster of S CTAs per row block), S <= 8 and each
+// split's activation slice <= M1_MAX_SPS super-blocks; cudaErrorNotSupported when K is too long.
+static bool m1_plan(int64_t n, int64_t k, int* rb, int* S, int* sps) {
+    const int nb = (int)(k / QK_K);
+    *rb = (int)((n + QMM_ROWS - 1) / QMM_ROWS);
+    int s = qmm_splits(*rb, nb, M1_CTAS);
+    s = std::min(s, M1_MAX_CLUSTER);
+    s = std::max(s, (nb + M1_MAX_SPS - 1) / M1_MAX_SPS);
+    if (s > M1_MAX_CLUSTER) return false;
+    *sps = (nb + s - 1) / s;
+    *S = (nb + *sps - 1) / *sps;
+    return true;
+}
+
+template <bool QX>
+static cudaError_t launch_q4k_m1(const uint8_t* W, int64_t n, int64_t k, const ActQ& a, const float* x,
+                                 float* y, cudaStream_t st) {
+    int rb, S, sps;
+    if (!m1_plan(n, k, &rb, &S, &sps)) return cudaErrorNotSupported;
     static bool attr = false;
-    const size_t smem = 256 + (size_t)QMM_STAGES * M1_STAGE;
+    const size_t smem_max = M1_HDR + (size_t)M1_STAGES * M1_STAGE + (size_t)M1_MAX_SPS * M1_XQ;
     if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(qmm_q4k_m1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(qmm_q4k_m1_kernel<QX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem_max);
         if (e != cudaSuccess) return e;
         attr = true;
     }
     const int nb = (int)(k / QK_K);
-    const int rb = (int)((n + QMM_ROWS - 1) / QMM_ROWS);
-    int S = qmm_splits(rb, nb, M1_CTAS);
-    const int sps = (nb + S - 1) / S;
-    S = (nb + sps - 1) / sps;
-    int* tickets = (int*)scratch;
-    float* part = (float*)((uint8_t*)scratch + align256((size_t)rb * 4));
     CUtensorMap wmap;
-    cudaError_t e = make_wmap(&wmap, W, n, (size_t)nb * Q4_K_BYTES, M1_KS);
+    cudaError_t e = make_wmap(&wmap, W, n, (size_t)nb * Q4_K_BYTES, 1);
     if (e != cudaSuccess) return e;
-    dim3 grid(rb, 1, S);
-    return launch_pdl(qmm_q4k_m1_kernel, grid, dim3(M1_THREADS), smem, st, wmap, nb, n, a, k, y, part,
-                      tickets, S, sps);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(rb, 1, S);
+    cfg.blockDim = dim3(M1_THREADS);
+    cfg.dynamicSmemBytes = M1_HDR + (size_t)M1_STAGES * M1_STAGE + (size_t)sps * M1_XQ;
+    cfg.stream = st;
+    // Plain stream order, not a programmatic dependent: launched early into a GPU still draining
+    // the previous grid, the clusters land unevenly and a config-2 step (two launches) measured
+    // 28.3 us against 21.1 us in stream order.
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = S;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, qmm_q4k_m1_kernel<QX>, wmap, nb, n, a, x, y, sps);
+}
+
+bool qmm_m1_fused_supports(int type, int64_t n, int64_t k, int64_t m) {
+    int rb, S, sps;
+    return type == DCG_TYPE_Q4_K && m == 1 && m1_plan(n, k, &rb, &S, &sps);
+}
+
+cudaError_t launch_qmm_m1_fused(const void* packed_w, int64_t n, int64_t k, const float* x, float* y,
+                                cudaStream_t st) {
+    return launch_q4k_m1<true>((const uint8_t*)packed_w, n, k, ActQ{}, x, y, st);
 }
 
 bool qmm_supports(int type) { return type == DCG_TYPE_Q4_K; }
@@ -592,7 +652,10 @@ cudaError_t launch_qmm(int type, const void* packed_w, int64_t n, int64_t k, con
     if (type != DCG_TYPE_Q4_K) return cudaErrorNotSupported;
     const ActQ a = act_view(DCG_TYPE_Q8_K, const_cast<void*>(act), m, k);
     const uint8_t* W = (const uint8_t*)packed_w;
-    if (m == 1) return launch_q4k_m1(W, n, k, a, y, scratch, st);
+    if (m == 1) {
+        const cudaError_t e = launch_q4k_m1<false>(W, n, k, a, nullptr, y, st);
+        if (e != cudaErrorNotSupported) return e;
+    }
     if (m <= 8) return launch_q4k_t<1>(W, n, k, a, (int)m, y, scratch, st);
     if (m <= 16) return launch_q4k_t<2>(W, n, k, a, (int)m, y, scratch, st);
     return launch_q4k_t<4>(W, n, k, a, (int)m, y, scratch, st);

@@ -82,6 +82,8 @@ MATMUL_CASES = [
     (O.Q8_0, 64, 4128, 2),        # k not a multiple of 512
     (O.Q4_K, 2048, 4096, 1),
     (O.Q4_K, 512, 14336, 1),
+    (O.Q4_K, 100, 2560, 1),       # ragged row block, 10 super-blocks
+    (O.Q4_K, 64, 69632, 1),       # 272 super-blocks: beyond the M=1 kernel's slice, falls back
     (O.Q4_K, 300, 2560, 5),       # ragged super-block count (10)
     (O.Q4_K, 256, 9728, 12),      # 38 super-blocks, m > 8
     (O.Q4_K, 128, 4096, 16),
@@ -127,6 +129,18 @@ def test_mul_mat_config2_full_size(ops):
         y_ref = O.mul_mat(O.Q4_K, wq, k, xq, 1, nthreads=8)
         y = ops.mul_mat(ops.QuantWeight.from_ggml(rows, O.Q4_K, k), _dev(x)).cpu().numpy()
         _assert_rows_close(y, wq, O.Q4_K, k, xq, O.Q8_K, y_ref)
+
+
+@pytest.mark.parametrize("n,k", [(14336, 4096), (4096, 14336), (8192, 28672), (100, 2560)])
+def test_m1_fused_quantize_equals_quantized_path(ops, n, k):
+    """dcg_mul_mat at M=1 quantizes x inside the Q4_K kernel; its output is bit-identical to
+    quantizing first (dcg_quantize_act) and running dcg_mul_mat_q on that activation."""
+    torch.manual_seed(n + k)
+    qw = ops.QuantWeight.from_float(torch.randn(n, k, device="cuda") * 0.02, O.Q4_K)
+    x = torch.randn(1, k, device="cuda")
+    y_fused = ops.mul_mat(qw, x)
+    y_q = ops.mul_mat_q(qw, ops.quantize_act(x, O.Q8_K), 1)
+    assert torch.equal(y_fused, y_q)
 
 
 def test_mul_mat_linearity_in_x(ops):
