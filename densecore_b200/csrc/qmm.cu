@@ -336,24 +336,6 @@ constexpr int M1_CTAS = 4;     // resident CTAs per SM (swept 2..6 x 2..7 stages
 constexpr int M1_STAGES = 4;   // weight ring depth
 constexpr int M1_MAX_CLUSTER = 8;                  // portable cluster size bounds the splits
 
-__device__ __forceinline__ float ld_cluster_f32(const float* p, uint32_t rank) {
-    uint32_t addr;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(addr) : "r"(smem_u32(p)), "r"(rank));
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
-}
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-
 template <bool QX>
 __global__ void __launch_bounds__(M1_THREADS, M1_CTAS)
     qmm_q4k_m1_kernel(const __grid_constant__ CUtensorMap wmap, int nb, int64_t n, ActQ a,

@@ -12,8 +12,11 @@
 //       value is (ql nibble | qh 2 bits << 4) - 32; isum += scale_s * C (int32) over the
 //       super-block, y += d_w * d_x * isum.
 // Device weight layout (common.cuh): payload rows + separate fp16 scale array.
+// Split-K: when the row x column blocks cannot fill the GPU, grid.z splits K and the splits of a
+// tile form one thread-block cluster that reduces through distributed shared memory.
 #include "common.cuh"
 #include "kernels.h"
+#include "tma.cuh"
 
 namespace dcg {
 
@@ -46,6 +49,51 @@ __device__ __forceinline__ uint32_t ldg32_stream(const void* p) {
     return r;
 }
 
+constexpr int RD_RS = 68;  // row stride of the split-K reduction tile: conflict-free lane writes
+
+// S splits (one cluster): rank 0 adds the S partial tiles parked in shared memory in rank order
+// through distributed shared memory.  Kept out of line: inlined, the cluster barriers changed the
+// main loops' schedule (240 -> 168 registers, a 2.5x slower Q8_0 loop).
+__device__ __noinline__ void rd_cluster_reduce(const float* red, float* __restrict__ y, int64_t n, int m,
+                                               int64_t r0, int c0, int ncols) {
+    cluster_sync_all();
+    if (cluster_rank() == 0) {
+        for (int idx = threadIdx.x; idx < RD_WARPS * 16 * ncols; idx += blockDim.x) {
+            const int row = idx % (RD_WARPS * 16), col = idx / (RD_WARPS * 16);
+            float sum = 0.0f;
+            for (uint32_t r = 0; r < gridDim.z; r++) sum += ld_cluster_f32(red + col * RD_RS + row, r);
+            if (c0 + col < m && r0 + row < n) y[(size_t)(c0 + col) * n + r0 + row] = sum;
+        }
+    }
+    cluster_sync_all();   // keeps every CTA's tile alive until rank 0 has read it
+}
+
+// Output of a warp's 16 rows x 8*NT columns: stored directly (one split) or parked in shared
+// memory for the cluster reduction; the result does not depend on timing either way.
+template <int NT>
+__device__ __forceinline__ void rd_store(const float (&acc)[NT][4], float* red, float* __restrict__ y,
+                                         int64_t n, int m, int64_t r0, int c0, int warp, int gid, int tig,
+                                         bool live) {
+    if (gridDim.z == 1) {
+        if (!live) return;
+#pragma unroll
+        for (int t = 0; t < NT; t++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int col = c0 + t * 8 + 2 * tig + (i & 1);
+                const int64_t row = r0 + warp * 16 + gid + (i < 2 ? 0 : 8);
+                if (col < m && row < n) y[(size_t)col * n + row] = acc[t][i];
+            }
+        return;
+    }
+#pragma unroll
+    for (int t = 0; t < NT; t++)
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            red[(t * 8 + 2 * tig + (i & 1)) * RD_RS + warp * 16 + gid + (i < 2 ? 0 : 8)] = acc[t][i];
+    rd_cluster_reduce(red, y, n, m, r0, c0, 8 * NT);
+}
+
 // ------------------------------------------------------------------------------------------
 // Q8_0.  A super-block here is 8 blocks (256 elements) so the loop shape matches Q6_K.
 // ------------------------------------------------------------------------------------------
@@ -76,13 +124,22 @@ __device__ __forceinline__ float h_at(const uint4& v, int j) {  // fp16 j (0..7)
 
 template <int NT>
 __global__ void __launch_bounds__(RD_WARPS * 32) qmm_q8_0_rd_kernel(PackedW w, int64_t n, int64_t k,
-                                                                   ActQ a, int m, float* __restrict__ y) {
+                                                                   ActQ a, int m, float* __restrict__ y,
+                                                                   int sps) {
     pdl_wait();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int gid = lane >> 2, tig = lane & 3;
     const int64_t rowA = ((int64_t)blockIdx.x * RD_WARPS + warp) * 16 + gid, rowB = rowA + 8;
     const int c0 = blockIdx.y * 8 * NT;
-    const int nsb = (int)(k / 256);
+    // this split's super-blocks [sb0, sb0 + nsb): base pointers move, the loop stays 0-based
+    // (a loop from sb0 compiled to a slower schedule)
+    const int sb0 = blockIdx.z * sps;
+    const int nsb = min((int)(k / 256) - sb0, sps);
+    w.payload += (size_t)sb0 * 256;
+    w.d += (size_t)sb0 * 8;
+    a.qs += (size_t)sb0 * 256;
+    a.d = (uint8_t*)a.d + (size_t)sb0 * 8 * sizeof(__half);
+    extern __shared__ float red[];  // 8 * NT * RD_RS floats when split
     const int nbx = (int)(k / QK8_0);
     const __half* xd = (const __half*)a.d;
     float acc[NT][4];
@@ -90,8 +147,12 @@ __global__ void __launch_bounds__(RD_WARPS * 32) qmm_q8_0_rd_kernel(PackedW w, i
     for (int t = 0; t < NT; t++)
 #pragma unroll
         for (int i = 0; i < 4; i++) acc[t][i] = 0.0f;
-    if (rowA - gid >= n) return;
+    const bool live = rowA - gid < n;
 
+    if (!live) {   // rows past n: no loads, but the warp still takes part in the split reduction
+        rd_store<NT>(acc, red, y, n, m, (int64_t)blockIdx.x * RD_WARPS * 16, c0, warp, gid, tig, false);
+        return;
+    }
     Q80Frag cur, nxt;
     q80_load(cur, w, rowA, rowB, n, 0, tig);
     for (int sb = 0; sb < nsb; sb++) {
@@ -121,14 +182,7 @@ __global__ void __launch_bounds__(RD_WARPS * 32) qmm_q8_0_rd_kernel(PackedW w, i
         if (sb + 1 < nsb) cur = nxt;
     }
     pdl_trigger();
-#pragma unroll
-    for (int t = 0; t < NT; t++)
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int col = c0 + t * 8 + 2 * tig + (i & 1);
-            const int64_t row = i < 2 ? rowA : rowB;
-            if (col < m && row < n) y[(size_t)col * n + row] = acc[t][i];
-        }
+    rd_store<NT>(acc, red, y, n, m, (int64_t)blockIdx.x * RD_WARPS * 16, c0, warp, gid, tig, live);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -180,21 +234,33 @@ __device__ __forceinline__ int sc_at(const uint4& v, int s) {  // signed int8 sc
 
 template <int NT>
 __global__ void __launch_bounds__(RD_WARPS * 32) qmm_q6k_rd_kernel(PackedW w, int64_t n, int64_t k,
-                                                                  ActQ a, int m, float* __restrict__ y) {
+                                                                  ActQ a, int m, float* __restrict__ y,
+                                                                   int sps) {
     pdl_wait();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int gid = lane >> 2, tig = lane & 3;
     const int64_t rowA = ((int64_t)blockIdx.x * RD_WARPS + warp) * 16 + gid, rowB = rowA + 8;
     const int c0 = blockIdx.y * 8 * NT;
-    const int nsb = (int)(k / QK_K);
+    const int sb0 = blockIdx.z * sps;   // base pointers move to the split, the loop stays 0-based
+    const int nsb = min((int)(k / QK_K) - sb0, sps);
+    const int nsb_all = (int)(k / QK_K);
+    w.payload += (size_t)sb0 * Q6_K_PAYLOAD;
+    w.d += sb0;
+    a.qs += (size_t)sb0 * QK_K;
+    a.d = (uint8_t*)a.d + (size_t)sb0 * sizeof(float);
+    extern __shared__ float red[];  // 8 * NT * RD_RS floats when split
     const float* xd = (const float*)a.d;
     float acc[NT][4];
 #pragma unroll
     for (int t = 0; t < NT; t++)
 #pragma unroll
         for (int i = 0; i < 4; i++) acc[t][i] = 0.0f;
-    if (rowA - gid >= n) return;
+    const bool live = rowA - gid < n;
 
+    if (!live) {   // rows past n: no loads, but the warp still takes part in the split reduction
+        rd_store<NT>(acc, red, y, n, m, (int64_t)blockIdx.x * RD_WARPS * 16, c0, warp, gid, tig, false);
+        return;
+    }
     Q6Frag cur, nxt;
     q6_load(cur, w, rowA, rowB, n, 0, tig);
     for (int sb = 0; sb < nsb; sb++) {
@@ -216,8 +282,8 @@ __global__ void __launch_bounds__(RD_WARPS * 32) qmm_q6k_rd_kernel(PackedW w, in
                 is[2] += sbb * c[2];
                 is[3] += sbb * c[3];
             }
-            const float x0 = cA < m ? xd[(size_t)cA * nsb + sb] : 0.0f;
-            const float x1 = cA + 1 < m ? xd[(size_t)(cA + 1) * nsb + sb] : 0.0f;
+            const float x0 = cA < m ? xd[(size_t)cA * nsb_all + sb] : 0.0f;
+            const float x1 = cA + 1 < m ? xd[(size_t)(cA + 1) * nsb_all + sb] : 0.0f;
             acc[t][0] += (cur.d[0] * x0) * (float)is[0];
             acc[t][1] += (cur.d[0] * x1) * (float)is[1];
             acc[t][2] += (cur.d[1] * x0) * (float)is[2];
@@ -226,23 +292,49 @@ __global__ void __launch_bounds__(RD_WARPS * 32) qmm_q6k_rd_kernel(PackedW w, in
         if (sb + 1 < nsb) cur = nxt;
     }
     pdl_trigger();
-#pragma unroll
-    for (int t = 0; t < NT; t++)
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int col = c0 + t * 8 + 2 * tig + (i & 1);
-            const int64_t row = i < 2 ? rowA : rowB;
-            if (col < m && row < n) y[(size_t)col * n + row] = acc[t][i];
-        }
+    rd_store<NT>(acc, red, y, n, m, (int64_t)blockIdx.x * RD_WARPS * 16, c0, warp, gid, tig, live);
 }
 
+// grid (row blocks, column blocks, splits): split K until one wave of resident CTAs is filled, at
+// most 8 splits (one portable cluster), keeping >= 4 super-blocks per split for Q8_0 and >= 2 for
+// Q6_K (its super-blocks cost 16 mmas; shorter splits measured slower than fewer).
 template <int TYPE, int NT>
 static cudaError_t launch_rd_t(const PackedW& w, int64_t n, int64_t k, const ActQ& a, int m, float* y,
                                cudaStream_t st) {
-    dim3 grid((unsigned)((n + RD_WARPS * 16 - 1) / (RD_WARPS * 16)), (unsigned)((m + 8 * NT - 1) / (8 * NT)));
-    if (TYPE == DCG_TYPE_Q8_0)
-        return launch_pdl(qmm_q8_0_rd_kernel<NT>, grid, dim3(RD_WARPS * 32), 0, st, w, n, k, a, m, y);
-    return launch_pdl(qmm_q6k_rd_kernel<NT>, grid, dim3(RD_WARPS * 32), 0, st, w, n, k, a, m, y);
+    const int rb = (int)((n + RD_WARPS * 16 - 1) / (RD_WARPS * 16)), cb = (m + 8 * NT - 1) / (8 * NT);
+    const int nsb = (int)(k / 256);
+    auto kern = TYPE == DCG_TYPE_Q8_0 ? qmm_q8_0_rd_kernel<NT> : qmm_q6k_rd_kernel<NT>;
+    static int resident = 0;   // CTAs per SM the kernel's registers allow
+    if (!resident) {
+        int dev = 0, sms = 0, per_sm = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, RD_WARPS * 32, 0);
+        resident = (per_sm > 0 ? per_sm : 1) * (sms > 0 ? sms : 148);
+    }
+    int S = (resident + rb * cb - 1) / (rb * cb);
+    S = S < 1 ? 1 : (S > 8 ? 8 : S);
+    const int min_sps = TYPE == DCG_TYPE_Q8_0 ? 4 : 2;   // below this a split costs more than it gains
+    S = S > nsb / min_sps ? (nsb / min_sps > 0 ? nsb / min_sps : 1) : S;
+    const int sps = (nsb + S - 1) / S;
+    S = (nsb + sps - 1) / sps;
+    const dim3 grid((unsigned)rb, (unsigned)cb, (unsigned)S);
+    if (S == 1) return launch_pdl(kern, grid, dim3(RD_WARPS * 32), 0, st, w, n, k, a, m, y, sps);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(RD_WARPS * 32);
+    cfg.dynamicSmemBytes = sizeof(float) * 8 * NT * RD_RS;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = S;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kern, w, n, k, a, m, y, sps);
 }
 
 bool qmm_rd_supports(int type, int64_t k, int64_t m) {

@@ -95,6 +95,7 @@ MATMUL_CASES = [
     (O.Q8_0, 300, 3072, 33),      # ragged n and m
     (O.Q6_K, 512, 2560, 32),      # Qwen3-4B attn_v-like, decode batch 32
     (O.Q6_K, 100, 9728, 5),
+    (O.Q8_0, 1000, 8192, 16),     # split-K over an 8-CTA cluster, ragged last row block
     (O.Q4_K, 1024, 2560, 64),
     (O.Q4_K, 256, 4096, 256),     # config-2 M=256 (reduced n)
     (O.Q4_K, 130, 14336, 17),
