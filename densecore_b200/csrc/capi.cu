@@ -195,11 +195,12 @@ int dcg_mul_mat(int type, const void* w, int64_t n, int64_t k, const float* x, i
 
 int dcg_device_error(int* code, int clear) {
     if (!code) return fail(DCG_EINVAL, "null pointer");
-    int a = 0, b = 0, c = 0;
+    int a = 0, b = 0, c = 0, d = 0;
     DCG_CUDA(dcg::gemv_device_error(&a, clear != 0), "read device error flag");
     DCG_CUDA(dcg::qmm_device_error(&b, clear != 0), "read device error flag");
     DCG_CUDA(dcg::attn_device_error(&c, clear != 0), "read device error flag");
-    *code = a ? a : (b ? b : c);
+    DCG_CUDA(dcg::qmm_tc_device_error(&d, clear != 0), "read device error flag");
+    *code = a ? a : (b ? b : (c ? c : d));
     return DCG_OK;
 }
 

@@ -120,6 +120,20 @@ __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c
 
 // 6-bit scale/min j (0..7) from the 12-byte Q4_K scale field given as three u32 words
 // (bytes 0-3, 4-7, 8-11); ggml's get_scale_min_k4 bit layout.
+// the 6-bit scales (sc) and mins (mn) of Q4_K sub-blocks 0-3 / 4-7, one per byte, from the block's
+// first 16 bytes (d, dmin, 12 packed scale bytes)
+struct Q4kScales {
+    uint32_t sc03, sc47, mn03, mn47;
+};
+__device__ __forceinline__ Q4kScales q4k_unpack(const uint4& h) {
+    Q4kScales s;
+    s.sc03 = h.y & 0x3F3F3F3Fu;
+    s.mn03 = h.z & 0x3F3F3F3Fu;
+    s.sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+    s.mn47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+    return s;
+}
+
 __device__ __forceinline__ void q4k_scale_min(uint32_t s0, uint32_t s1, uint32_t s2, int j, int& sc,
                                               int& m) {
     if (j < 4) {

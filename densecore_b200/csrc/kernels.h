@@ -27,6 +27,11 @@ cudaError_t launch_qmm_m1_fused(const void* packed_w, int64_t n, int64_t k, cons
                                 cudaStream_t st);
 cudaError_t launch_qmm(int type, const void* packed_w, int64_t n, int64_t k, const void* act,
                        int64_t m, float* y, void* scratch, cudaStream_t st);
+// tcgen05 Q4_K GEMM (qmm_tc.cu)
+bool qmm_tc_supports(int type, int64_t n, int64_t k, int64_t m);
+cudaError_t launch_qmm_tc(const void* packed_w, int64_t n, int64_t k, const void* act, int64_t m, float* y,
+                          cudaStream_t st);
+cudaError_t qmm_tc_device_error(int* out, bool clear);
 cudaError_t qmm_device_error(int* out, bool clear);
 bool qmm_supports(int type);
 

@@ -71,18 +71,6 @@ __device__ __forceinline__ int byte_of(uint32_t w, int j) {  // zero-extended by
 }
 
 // packed Q4_K 6-bit scales / mins of one block header (ggml get_scale_min_k4, 4 per word)
-struct Q4kScales {
-    uint32_t sc03, sc47, mn03, mn47;
-};
-__device__ __forceinline__ Q4kScales q4k_unpack(const uint4& h) {
-    Q4kScales s;
-    s.sc03 = h.y & 0x3F3F3F3Fu;
-    s.mn03 = h.z & 0x3F3F3F3Fu;
-    s.sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
-    s.mn47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
-    return s;
-}
-
 template <int NT>
 __global__ void __launch_bounds__(QMM_THREADS, NT >= 4 ? 1 : (NT >= 2 ? 2 : 3))
     qmm_q4k_kernel(const __grid_constant__ CUtensorMap wmap, int nb, int64_t n, ActQ a,
@@ -638,6 +626,9 @@ cudaError_t launch_qmm(int type, const void* packed_w, int64_t n, int64_t k, con
         const cudaError_t e = launch_q4k_m1<false>(W, n, k, a, nullptr, y, st);
         if (e != cudaErrorNotSupported) return e;
     }
+    // M >= 16: the tcgen05 kernel (qmm_tc.cu); measured 1.0-2.2x faster than the mma.sync kernel
+    // below on the decode shapes at M = 16, 32, 64
+    if (m >= 16 && qmm_tc_supports(type, n, k, m)) return launch_qmm_tc(packed_w, n, k, act, m, y, st);
     if (m <= 8) return launch_q4k_t<1>(W, n, k, a, (int)m, y, scratch, st);
     if (m <= 16) return launch_q4k_t<2>(W, n, k, a, (int)m, y, scratch, st);
     return launch_q4k_t<4>(W, n, k, a, (int)m, y, scratch, st);

@@ -97,6 +97,8 @@ MATMUL_CASES = [
     (O.Q6_K, 100, 9728, 5),
     (O.Q8_0, 1000, 8192, 16),     # split-K over an 8-CTA cluster, ragged last row block
     (O.Q4_K, 1024, 2560, 64),
+    (O.Q4_K, 300, 2560, 20),      # tcgen05 path: ragged row tile and column tile
+    (O.Q4_K, 640, 9728, 32),      # tcgen05 path, split-K over a cluster
     (O.Q4_K, 256, 4096, 256),     # config-2 M=256 (reduced n)
     (O.Q4_K, 130, 14336, 17),
 ]
