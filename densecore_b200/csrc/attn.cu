@@ -49,14 +49,6 @@ cudaError_t attn_device_error(int* out, bool clear) {
     return e;
 }
 
-__device__ __forceinline__ void tma_load_3d(void* dst, const void* map, int x, int y, int z, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-        "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
-        : "memory");
-}
-
 // ------------------------------------------------------------------------------------------
 // Per 16-token KV block, per consumer warp:
 //   S^T[rep][t] = Q K^T : mma m16n8k16 f16 -> f32, A = Q (NREP query heads as rows, zero-padded to

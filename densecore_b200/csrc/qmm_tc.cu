@@ -7,14 +7,15 @@
 // super-blocks (split-K across a cluster when the tiles alone cannot fill the GPU).  Per
 // super-block (K = 256):
 //   producer warp   TMA: the 128 x 144 B Q4_K weight tile, and the N x 256 B Q8_K activation tile
-//                   as 16 boxes of 16 B x N rows (the K-major no-swizzle core-matrix layout)
-//   prep warpgroup  thread r expands weight row r into two int8 planes, H = q * sh and
+//                   as one 3-D box (16 B x N rows x 16 K chunks: the K-major no-swizzle
+//                   core-matrix layout); its lanes stage the columns' dx and pair sums
+//   prep warpgroup  (warps 2-5) thread r expands weight row r into two int8 planes, H = q * sh and
 //                   L = q * sl with the 6-bit sub-block scale sc = 8 * sh + sl (q <= 15, sh, sl
 //                   <= 7: every product fits int8, four at a time in one 32-bit multiply), written
 //                   in the core-matrix layout the MMA reads
 //   MMA thread      16 x tcgen05.mma.kind::i8 (8 k-steps of 32 for each plane) into two int32
 //                   accumulators C_H, C_L in tensor memory; double-buffered across super-blocks
-//   epilogue        the same warpgroup: thread r reads row r of C_H, C_L (tcgen05.ld) and the
+//   epilogue        (warps 6-9, concurrent with the prep of the next super-block) thread r reads row r of C_H, C_L (tcgen05.ld) and the
 //                   columns' dx and pair sums (staged in shared memory by the producer warp), forms the
 //                   exact integer sum isum = 8 C_H + C_L, the min term sum_j m_j * bsum32_j (dp2a),
 //                   and accumulates y += dx * (d * isum - dmin * msum) in fp32, as ggml does
@@ -40,7 +41,8 @@ cudaError_t qmm_tc_device_error(int* out, bool clear) {
 }
 
 constexpr int TC_ROWS = 128;                     // weight rows per CTA (MMA M)
-constexpr int TC_THREADS = 192;                  // warp 0 producer, warp 1 MMA, warps 2-5 prep/epilogue
+constexpr int TC_THREADS = 576;                  // warp 0 producer, 1 MMA, 2-9 prep, 10-17 epilogue
+constexpr int TC_EPI0 = 10;                      // first epilogue warp
 constexpr int TC_WTILE = TC_ROWS * Q4_K_BYTES;   // 18432 B raw weight tile per super-block
 constexpr int TC_PLANE = TC_ROWS * QK_K;         // 32 KB: one int8 plane of a super-block
 constexpr int TC_PLANE_SBO = 16 * 128;           // plane: 8-row groups 2 KB apart, 16-B K chunks 128 B
@@ -52,9 +54,11 @@ struct TcCfg {
     static constexpr int OFF_RAW = 1024;                         // after barriers
     static constexpr int OFF_ACT = OFF_RAW + STAGES * TC_WTILE;
     static constexpr int OFF_PL = OFF_ACT + STAGES * ATILE;      // [2 buffers][H, L]
+    static constexpr int MSLOTS = STAGES + 2;                    // metadata lives until the epilogue
     static constexpr int META = N * 4 + N * 16;                  // per column: dx, 8 pair sums
     static constexpr int OFF_META = OFF_PL + 4 * TC_PLANE;
-    static constexpr int SMEM = OFF_META + STAGES * META;
+    static constexpr int OFF_ROWP = OFF_META + MSLOTS * META;    // [slot][128 rows] d | dmin, mins
+    static constexpr int SMEM = OFF_ROWP + MSLOTS * TC_ROWS * 16;
     static constexpr int TMEM_COLS = 4 * N;                      // [2 buffers][C_H, C_L] x N
 };
 
@@ -109,18 +113,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     constexpr int R = C::STAGES;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = (uint64_t*)smem;          // [R] weight + activation tiles landed (tx)
-    uint64_t* raw_empty = full + R;            // [R] 128 threads done with the weight tile and metadata
+    uint64_t* raw_empty = full + R;            // [R] 128 prep threads read the weight tile
     uint64_t* act_empty = raw_empty + R;       // [R] MMAs that read the activation tile done
     uint64_t* pl_full = act_empty + R;         // [2] planes written (128 arrivals)
     uint64_t* pl_empty = pl_full + 2;          // [2] MMAs that read the planes done
     uint64_t* acc_full = pl_empty + 2;         // [2] accumulators complete
     uint64_t* acc_empty = acc_full + 2;        // [2] 128 epilogue threads read them
-    uint64_t* mma_done = acc_empty + 2;        // [1] every MMA of the CTA retired
+    uint64_t* meta_empty = acc_empty + 2;      // [MSLOTS] epilogue done with a metadata slot
+    uint64_t* mma_done = meta_empty + C::MSLOTS; // [1] every MMA of the CTA retired
     uint32_t* tmem_slot = (uint32_t*)(mma_done + 1);
     uint8_t* raw = smem + C::OFF_RAW;
     uint8_t* act = smem + C::OFF_ACT;
     uint8_t* planes = smem + C::OFF_PL;
-    uint8_t* meta = smem + C::OFF_META;        // [R][dx: N floats | pair sums: N x 8 int16]
+    uint8_t* meta = smem + C::OFF_META;        // [MSLOTS][dx: N floats | pair sums: N x 8 int16]
+    uint4* rowp = (uint4*)(smem + C::OFF_ROWP);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t r0 = (int64_t)blockIdx.x * TC_ROWS;
@@ -131,15 +137,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < R; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&raw_empty[s], 128);
+            mbar_init(&raw_empty[s], 256);
             mbar_init(&act_empty[s], 1);
         }
         for (int b = 0; b < 2; b++) {
-            mbar_init(&pl_full[b], 128);
+            mbar_init(&pl_full[b], 256);
             mbar_init(&pl_empty[b], 1);
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 128);
+            mbar_init(&acc_empty[b], 256);
         }
+        for (int s = 0; s < C::MSLOTS; s++) mbar_init(&meta_empty[s], 256);
         mbar_init(mma_done, 1);
         fence_mbar_init();
     }
@@ -160,35 +167,56 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // ---------------- producer ----------------
         // lane 0 issues the tile copies; lane c stages column c's dx and pair sums (strided in
         // global memory) into the stage's metadata before lane 0 arrives on the full barrier
+        // column c's dx and pair sums for super-block s, loaded one super-block ahead
+        auto load_meta = [&](int s, float (&dx)[(N + 31) / 32], uint4 (&bs)[(N + 31) / 32]) {
+#pragma unroll
+            for (int i = 0; i < (N + 31) / 32; i++) {
+                const int c = lane + 32 * i, col = c0 + c;
+                dx[i] = 0.0f;
+                bs[i] = make_uint4(0, 0, 0, 0);
+                if (c < N && col < m && s < nsb) {
+                    dx[i] = __ldg(&((const float*)a.d)[(size_t)col * nb + sb0 + s]);
+                    bs[i] = __ldg((const uint4*)(a.bs32 + ((size_t)col * nb + sb0 + s) * 8));
+                }
+            }
+        };
+        float ndx[(N + 31) / 32];
+        uint4 nbs[(N + 31) / 32];
+        load_meta(0, ndx, nbs);
         for (int s = 0; s < nsb && ok; s++) {
-            const int st = s % R;
+            const int st = s % R, ms = s % C::MSLOTS;
+            float cdx[(N + 31) / 32];
+            uint4 cbs[(N + 31) / 32];
+#pragma unroll
+            for (int i = 0; i < (N + 31) / 32; i++) {
+                cdx[i] = ndx[i];
+                cbs[i] = nbs[i];
+            }
+            load_meta(s + 1, ndx, nbs);
             if (s >= R) {
                 const uint32_t par = (uint32_t)(((s / R) - 1) & 1);
                 ok = mbar_wait(&raw_empty[st], par, &g_tc_error) && mbar_wait(&act_empty[st], par, &g_tc_error);
             }
+            if (ok && s >= C::MSLOTS)
+                ok = mbar_wait(&meta_empty[ms], (uint32_t)(((s / C::MSLOTS) - 1) & 1), &g_tc_error);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
-            float* mdx = (float*)(meta + (size_t)st * C::META);
+            float* mdx = (float*)(meta + (size_t)ms * C::META);
             uint4* mbs = (uint4*)(mdx + N);
-            for (int c = lane; c < N; c += 32) {
-                const int col = c0 + c;
-                float dx = 0.0f;
-                uint4 bs = make_uint4(0, 0, 0, 0);
-                if (col < m) {
-                    dx = __ldg(&((const float*)a.d)[(size_t)col * nb + sb0 + s]);
-                    bs = __ldg((const uint4*)(a.bs32 + ((size_t)col * nb + sb0 + s) * 8));
+#pragma unroll
+            for (int i = 0; i < (N + 31) / 32; i++) {
+                const int c = lane + 32 * i;
+                if (c < N) {
+                    mdx[c] = cdx[i];
+                    mbs[c] = cbs[i];
                 }
-                mdx[c] = dx;
-                mbs[c] = bs;
             }
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive_expect_tx(&full[st], (uint32_t)(TC_WTILE + C::ATILE));
                 tma_load_2d(raw + (size_t)st * TC_WTILE, &wmap, (sb0 + s) * (Q4_K_BYTES / 4), (int)r0, &full[st]);
-                uint8_t* dst = act + (size_t)st * C::ATILE;
-#pragma unroll 4
-                for (int kc = 0; kc < 16; kc++)   // 16-B K chunk kc of N rows -> [kc][row][16 B]
-                    tma_load_2d(dst + kc * N * 16, &amap, (sb0 + s) * QK_K + kc * 16, c0, &full[st]);
+                // the activation tile in one box: [16-B K chunk][row][16 B], the core-matrix layout
+                tma_load_3d(act + (size_t)st * C::ATILE, &amap, 0, c0, (sb0 + s) * 16, &full[st]);
             }
         }
     } else if (warp == 1) {
@@ -221,53 +249,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
     }
 
-    // ---------------- prep + epilogue: thread r <-> weight row r <-> TMEM lane r ----------------
-    float yacc[N];
+    // ---- prep (warps 2-9) and epilogue (warps 10-17): thread <-> weight row <-> TMEM lane; two
+    // warps per row quarter, splitting the K chunks (prep) or the columns (epilogue) ----
+    constexpr int NH = N / 2;                       // columns per epilogue thread
+    float yacc[NH];
 #pragma unroll
-    for (int c = 0; c < N; c++) yacc[c] = 0.0f;
+    for (int c = 0; c < NH; c++) yacc[c] = 0.0f;
     const int quarter = warp & 3;                   // TMEM lanes 32*quarter .. +31 for this warp
     const int row = quarter * 32 + lane;
-    if (warp >= 2) {
-        float pd = 0.0f, pdm = 0.0f;                // previous super-block's d, dmin, packed mins
-        uint32_t pmn03 = 0, pmn47 = 0;
-        auto epilogue = [&](int e, float d, float dmin, uint32_t mn03, uint32_t mn47) -> bool {
-            const int b = e & 1;
-            // warp-uniform outcome: the TMEM loads below are .sync.aligned
-            if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[b], (uint32_t)((e >> 1) & 1), &g_tc_error))) return false;
-            tc_fence_after();
-            const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 2 * N);
-            // mins as (m0, m1), (m2, m3), ... pairs in the low bytes for dp2a
-            const int mp0 = (int)(mn03 & 0xFFu) | (int)((mn03 >> 8) & 0xFFu) << 8;
-            const int mp1 = (int)((mn03 >> 16) & 0xFFu) | (int)(mn03 >> 24) << 8;
-            const int mp2 = (int)(mn47 & 0xFFu) | (int)((mn47 >> 8) & 0xFFu) << 8;
-            const int mp3 = (int)((mn47 >> 16) & 0xFFu) | (int)(mn47 >> 24) << 8;
-#pragma unroll
-            for (int cc = 0; cc < N; cc += 16) {
-                uint32_t h[16], l[16];
-                tmem_ld16(lane_addr + cc, h);
-                tmem_ld16(lane_addr + N + cc, l);
-                tmem_wait_ld();
-                if (cc + 16 == N) {   // all reads of this buffer issued and complete
-                    tc_fence_before();
-                    mbar_arrive(&acc_empty[b]);
-                }
-                const float* mdx = (const float*)(meta + (size_t)(e % R) * C::META);
-                const uint4* mbs = (const uint4*)(mdx + N);
-#pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    const float dx = mdx[cc + j];       // 0 for columns past m
-                    const uint4 bs = mbs[cc + j];
-                    int ms = __dp2a_lo((int)bs.x, mp0, 0);
-                    ms = __dp2a_lo((int)bs.y, mp1, ms);
-                    ms = __dp2a_lo((int)bs.z, mp2, ms);
-                    ms = __dp2a_lo((int)bs.w, mp3, ms);
-                    const int isum = 8 * (int)h[j] + (int)l[j];
-                    yacc[cc + j] += dx * (d * (float)isum - dmin * (float)ms);
-                }
-            }
-            mbar_arrive(&raw_empty[e % R]);   // weight tile and metadata of super-block e released
-            return true;
-        };
+    const int half = warp < TC_EPI0 ? (warp - 2) >> 2 : (warp - TC_EPI0) >> 2;
+    if (warp >= 2 && warp < TC_EPI0) {
         for (int s = 0; s < nsb && ok; s++) {
             const int st = s % R, b = s & 1;
             ok = mbar_wait(&full[st], (uint32_t)((s / R) & 1), &g_tc_error) &&
@@ -275,17 +266,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             const uint4* src = (const uint4*)(raw + (size_t)st * TC_WTILE + (size_t)row * Q4_K_BYTES);
-            uint4 q[9];
+            uint4 q[5];   // header + the 64 nibble bytes of this half (sub-blocks 4*half .. +3)
+            q[0] = src[0];
 #pragma unroll
-            for (int i = 0; i < 9; i++) q[i] = src[i];
+            for (int i = 1; i < 5; i++) q[i] = src[half * 4 + i];
+            mbar_arrive(&raw_empty[st]);
             const Q4kScales sc = q4k_unpack(q[0]);
-            const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&q[0].x));
+            // the row's d | dmin, packed mins, for the epilogue of this super-block
+            if (half == 0) rowp[(s % C::MSLOTS) * TC_ROWS + row] = make_uint4(q[0].x, sc.mn03, sc.mn47, 0u);
             uint8_t* pH = planes + (size_t)(2 * b) * TC_PLANE + (size_t)(row >> 3) * TC_PLANE_SBO + (row & 7) * 16;
             uint8_t* pL = pH + TC_PLANE;
-            const uint32_t* qs = (const uint32_t*)&q[1];   // 128 bytes of nibbles
+            const uint32_t* qs = (const uint32_t*)&q[1];   // nibble bytes 64*half .. +63
 #pragma unroll
-            for (int kc = 0; kc < 16; kc++) {   // elements 16kc .. 16kc+15: sub-block kc/2
-                const int sbk = kc >> 1, g = sbk >> 1;
+            for (int kh = 0; kh < 8; kh++) {    // elements 16kc .. 16kc+15: sub-block kc/2
+                const int kc = half * 8 + kh;
+                const int sbk = kc >> 1, g = (kh >> 1) >> 1;
                 const uint32_t scs = ((sbk < 4 ? sc.sc03 : sc.sc47) >> (8 * (sbk & 3))) & 0x3Fu;
                 const uint32_t sh = scs >> 3, sl = scs & 7u;
                 uint4 vh, vl;
@@ -303,13 +298,48 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
             fence_proxy_async_smem();
             mbar_arrive(&pl_full[b]);
-            if (s > 0) ok = epilogue(s - 1, pd, pdm, pmn03, pmn47);
-            pd = dd.x;
-            pdm = dd.y;
-            pmn03 = sc.mn03;
-            pmn47 = sc.mn47;
         }
-        if (ok && nsb > 0) ok = epilogue(nsb - 1, pd, pdm, pmn03, pmn47);
+    } else if (warp >= TC_EPI0) {
+        for (int e = 0; e < nsb && ok; e++) {
+            const int b = e & 1, ms = e % C::MSLOTS;
+            // warp-uniform outcome: the TMEM loads below are .sync.aligned
+            ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[b], (uint32_t)((e >> 1) & 1), &g_tc_error));
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 2 * N + half * NH);
+            const uint4 rp = rowp[ms * TC_ROWS + row];
+            const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&rp.x));
+            // mins as (m0, m1), (m2, m3), ... pairs in the low bytes for dp2a
+            const int mp0 = (int)(rp.y & 0xFFu) | (int)((rp.y >> 8) & 0xFFu) << 8;
+            const int mp1 = (int)((rp.y >> 16) & 0xFFu) | (int)(rp.y >> 24) << 8;
+            const int mp2 = (int)(rp.z & 0xFFu) | (int)((rp.z >> 8) & 0xFFu) << 8;
+            const int mp3 = (int)((rp.z >> 16) & 0xFFu) | (int)(rp.z >> 24) << 8;
+            const float* mdx = (const float*)(meta + (size_t)ms * C::META) + half * NH;
+            const uint4* mbs = (const uint4*)((const float*)(meta + (size_t)ms * C::META) + N) + half * NH;
+#pragma unroll
+            for (int cc = 0; cc < NH; cc += 16) {
+                uint32_t h[16], l[16];
+                tmem_ld16(lane_addr + cc, h);
+                tmem_ld16(lane_addr + N + cc, l);
+                tmem_wait_ld();
+                if (cc + 16 == NH) {   // all reads of this buffer issued and complete
+                    tc_fence_before();
+                    mbar_arrive(&acc_empty[b]);
+                }
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const float dx = mdx[cc + j];       // 0 for columns past m
+                    const uint4 bs = mbs[cc + j];
+                    int ms = __dp2a_lo((int)bs.x, mp0, 0);
+                    ms = __dp2a_lo((int)bs.y, mp1, ms);
+                    ms = __dp2a_lo((int)bs.z, mp2, ms);
+                    ms = __dp2a_lo((int)bs.w, mp3, ms);
+                    const int isum = 8 * (int)h[j] + (int)l[j];
+                    yacc[cc + j] += dx * (dd.x * (float)isum - dd.y * (float)ms);
+                }
+            }
+            mbar_arrive(&meta_empty[ms]);   // row parameters and metadata of super-block e released
+        }
     }
 
     // ---------------- output: direct, or rank-ordered sum over the split cluster ----------------
@@ -317,14 +347,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncthreads();   // every MMA retired (mma_done) and every TMEM read done
     float* red = (float*)planes;   // [N][128] partial tile, reusing the plane buffers
     if (gridDim.z == 1) {
-        if (warp >= 2 && r0 + row < n)
+        if (warp >= TC_EPI0 && r0 + row < n)
 #pragma unroll
-            for (int c = 0; c < N; c++)
-                if (c0 + c < m) y[(size_t)(c0 + c) * n + r0 + row] = yacc[c];
+            for (int c = 0; c < NH; c++)
+                if (c0 + half * NH + c < m) y[(size_t)(c0 + half * NH + c) * n + r0 + row] = yacc[c];
     } else {
-        if (warp >= 2)
+        if (warp >= TC_EPI0)
 #pragma unroll
-            for (int c = 0; c < N; c++) red[c * TC_ROWS + row] = yacc[c];
+            for (int c = 0; c < NH; c++) red[(half * NH + c) * TC_ROWS + row] = yacc[c];
         cluster_sync_all();
         if (cluster_rank() == 0)
             for (int idx = threadIdx.x; idx < N * TC_ROWS; idx += TC_THREADS) {
@@ -361,12 +391,12 @@ static cudaError_t tc_maps(CUtensorMap* wm, CUtensorMap* am, const void* W, int6
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return cudaErrorInvalidValue;
     }
-    {
-        const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
-        const cuuint64_t strides[1] = {(cuuint64_t)k};
-        const cuuint32_t box[2] = {16u, (cuuint32_t)N};
-        const cuuint32_t estr[2] = {1, 1};
-        if (fn(am, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(qs), dims, strides, box, estr,
+    {   // Q8_K quants as [k/16 chunks][m rows][16 B]: dims (16 B, rows, chunks), strides (k, 16)
+        const cuuint64_t dims[3] = {16u, (cuuint64_t)m, (cuuint64_t)(k / 16)};
+        const cuuint64_t strides[2] = {(cuuint64_t)k, 16u};
+        const cuuint32_t box[3] = {16u, (cuuint32_t)N, 16u};
+        const cuuint32_t estr[3] = {1, 1, 1};
+        if (fn(am, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(qs), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return cudaErrorInvalidValue;
