@@ -16,19 +16,21 @@ the B200 kernels:
   (all dcgpu kernels; torch only gathers the embedding rows and takes the argmax)
 
 Each sequence attends to its own history through its own block table (per-sequence semantics; the
-reference's batched path reads seq_id[0]'s history for every sequence).  Weights are random-init
-N(0, 0.02) of the named architecture, quantized on the device by the weight encoder; norm weights
-are ones.  The step runs as one CUDA graph.
+reference's batched path reads seq_id[0]'s history for every sequence).  Weights are either
+random-init N(0, 0.02) of the named architecture, quantized on the device by the weight encoder
+(norm weights ones), or a GGUF checkpoint's (Decoder.from_gguf).  The step runs as one CUDA graph.
 """
 from __future__ import annotations
 
 import dataclasses
 import math
+import warnings
 
+import numpy as np
 import torch
 
 from . import ops
-from .ggml_types import Q4_K, Q6_K, Q8_0, Q8_K, VEC_DOT_TYPE
+from .ggml_types import F16, F32, Q4_K, Q6_K, Q8_0, Q8_K, VEC_DOT_TYPE
 
 KV_BLOCK = 16
 
@@ -89,15 +91,17 @@ class Decoder:
 
     def __init__(self, cfg: DecoderConfig, batch: int, max_ctx: int, seed: int = 0,
                  device: str | torch.device = "cuda", tp_rank: int = 0, tp_size: int = 1,
-                 tp_group=None, shard_init: str = "slice", seq_tokens=None):
+                 tp_group=None, shard_init: str = "slice", seq_tokens=None, weights: dict | None = None):
         """tp_size > 1: this process holds shard tp_rank of every weight (tp_plan) and the KV heads
         of its query-head group; two all-reduces per layer (after attn_output and ffn_down) and an
         all-gather of the logits over tp_group (NCCL).  shard_init = "slice": every rank draws the
         full random weights and keeps its slice (bitwise the tp_size = 1 model); "local": each rank
         draws only its shard (faster; a different random model).  seq_tokens: per-sequence token
-        capacity; the arena then holds exactly those blocks (default: max_ctx for every sequence)."""
+        capacity; the arena then holds exactly those blocks (default: max_ctx for every sequence).
+        weights: GGUF-named tensors (gguf_file.decoder_weights) instead of random ones; tp_size 1."""
         self.cfg, self.batch, self.max_ctx = cfg, batch, max_ctx
         self.tp_rank, self.tp_size, self.tp_group = tp_rank, tp_size, tp_group
+        self.seed = seed
         dev = self.device = torch.device(device)
         g = torch.Generator(device=dev)
         g.manual_seed(seed if shard_init == "slice" else seed * 1009 + tp_rank)
@@ -124,6 +128,15 @@ class Decoder:
         def qw(n, k, t, rows=None, cols=None):
             return ops.QuantWeight.from_float(draw(n, k, rows, cols), t)
 
+        self.ones_h = torch.ones(H, device=dev)
+        self.ones_d = torch.ones(D, device=dev) if cfg.qk_norm else None
+        if weights is not None:
+            if tp_size != 1:
+                raise NotImplementedError("GGUF weights are loaded with tp_size = 1")
+            self._load_weights(weights)
+            self._init_cache(batch, max_ctx, seq_tokens)
+            return
+
         self.layers = []
         for li in range(cfg.n_layer):
             t_q, t_k, t_v = (_wtype(cfg, li, nm) for nm in ("attn_q", "attn_k", "attn_v"))
@@ -143,7 +156,10 @@ class Decoder:
             L["ffn_gate_up"] = ops.QuantWeight.from_float(torch.cat([wg, wu]), _wtype(cfg, li, "ffn_gate"))
             del wg, wu
             L["ffn_down"] = qw(H, cfg.ffn, _wtype(cfg, li, "ffn_down"), cols=plan["down_cols"])
+            L["attn_norm"] = L["ffn_norm"] = self.ones_h
+            L["attn_q_norm"] = L["attn_k_norm"] = self.ones_d
             self.layers.append(L)
+        self.output_norm = self.ones_h
         out_t = cfg.out_type if cfg.out_type >= 0 else (Q8_0 if cfg.wtype == Q8_0 else Q6_K)
         if cfg.tied:
             # the LM head is the quantized token embedding; lookups dequantize it (all vocab rows)
@@ -160,8 +176,87 @@ class Decoder:
         else:
             self.tok_embd = (torch.randn((cfg.vocab, H), generator=g, device=dev) * 0.02).half()
             self.output = qw(cfg.vocab, H, out_t, rows=plan["vocab_rows"])
-        self.ones_h = torch.ones(H, device=dev)
-        self.ones_d = torch.ones(D, device=dev) if cfg.qk_norm else None
+        self._init_cache(batch, max_ctx, seq_tokens)
+
+    def _load_weights(self, w: dict):
+        """Weights from GGUF-named tensors: ggml rows go to the device as they are; q|k|v and
+        gate|up are stacked by concatenating rows (rows are quantized independently)."""
+        cfg, dev, H = self.cfg, self.device, self.cfg.hidden
+        supported = (Q8_0, Q4_K, Q6_K)
+
+        def to_dev(a):
+            # tensors of a memory-mapped file are read-only views: only read here (copied to the device)
+            with warnings.catch_warnings():
+                warnings.filterwarnings("ignore", message="The given NumPy array is not writable")
+                return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+        def rows(name):
+            r, t, k = w[name]
+            if t not in supported:
+                raise ValueError(f"{name}: ggml type {t} is not a supported matmul weight type")
+            return to_dev(r), t, k
+
+        def stack(names):
+            parts = [rows(n) for n in names]
+            if len({t for _, t, _ in parts}) != 1:
+                return None
+            return ops.QuantWeight.from_ggml(torch.cat([r for r, _, _ in parts]), parts[0][1], parts[0][2])
+
+        def vec(name):
+            return torch.from_numpy(np.ascontiguousarray(w[name], dtype=np.float32)).to(dev)
+
+        self.layers = []
+        for li in range(cfg.n_layer):
+            p = f"blk.{li}."
+            L = {"qkv_split": False}
+            qkv = stack([p + "attn_q.weight", p + "attn_k.weight", p + "attn_v.weight"])
+            if qkv is not None:
+                L["attn_qkv"] = qkv
+            else:
+                qk = stack([p + "attn_q.weight", p + "attn_k.weight"])
+                if qk is None:
+                    raise NotImplementedError(f"layer {li}: attn_q and attn_k of different types")
+                L.update(qkv_split=True, attn_qk=qk, attn_v=ops.QuantWeight.from_ggml(*rows(p + "attn_v.weight")))
+            L["attn_output"] = ops.QuantWeight.from_ggml(*rows(p + "attn_output.weight"))
+            gu = stack([p + "ffn_gate.weight", p + "ffn_up.weight"])
+            if gu is None:
+                raise NotImplementedError(f"layer {li}: ffn_gate and ffn_up of different types")
+            L["ffn_gate_up"] = gu
+            L["ffn_down"] = ops.QuantWeight.from_ggml(*rows(p + "ffn_down.weight"))
+            L["attn_norm"], L["ffn_norm"] = vec(p + "attn_norm.weight"), vec(p + "ffn_norm.weight")
+            L["attn_q_norm"] = vec(p + "attn_q_norm.weight") if cfg.qk_norm else None
+            L["attn_k_norm"] = vec(p + "attn_k_norm.weight") if cfg.qk_norm else None
+            self.layers.append(L)
+        self.output_norm = vec("output_norm.weight")
+        er, et, ek = w["token_embd.weight"]
+        er_dev = to_dev(er)
+        if et in supported:
+            emb = ops.QuantWeight.from_ggml(er_dev, et, ek)
+            self.tok_embd = self._dequant_rows(emb)
+        elif et in (F16, F32):
+            self.tok_embd = er_dev.view(torch.float16 if et == F16 else torch.float32).reshape(-1, ek).half()
+            emb = None
+        else:
+            raise ValueError(f"token_embd: ggml type {et} is not supported")
+        if "output.weight" in w:
+            self.output = ops.QuantWeight.from_ggml(*rows("output.weight"))
+        elif emb is not None:      # tied: the LM head is the embedding matrix itself
+            self.output = emb
+        else:                      # tied fp embedding: quantized to Q8_0 for the head matmul
+            self.output = ops.QuantWeight.from_float(self.tok_embd.float(), Q8_0)
+
+    @classmethod
+    def from_gguf(cls, path: str, batch: int, max_ctx: int, device: str | torch.device = "cuda",
+                  seq_tokens=None) -> "Decoder":
+        """A decoder holding the weights of a GGUF checkpoint (tensor names and hyper-parameter
+        keys of DenseCore's loader, core/src/model_loader.cpp:154-403)."""
+        from .gguf_file import GGUFFile, decoder_config, decoder_weights
+        g = GGUFFile(path)
+        return cls(decoder_config(g), batch, max_ctx, device=device, seq_tokens=seq_tokens,
+                   weights=decoder_weights(g))
+
+    def _init_cache(self, batch, max_ctx, seq_tokens):
+        cfg, dev, H, D = self.cfg, self.device, self.cfg.hidden, self.cfg.head_dim
 
         # paged KV arena (kv_cache.cpp:353-370 layout): [(block*n_layer + layer)][16][hkv][D] fp16
         self.blocks_per_seq = (max_ctx + KV_BLOCK - 1) // KV_BLOCK
@@ -174,7 +269,7 @@ class Decoder:
         self.k_arena = torch.empty(shape, dtype=torch.float16, device=dev)
         self.v_arena = torch.empty(shape, dtype=torch.float16, device=dev)
         # each sequence owns a shuffled set of physical blocks
-        perm = torch.randperm(self.n_blocks, generator=torch.Generator().manual_seed(seed + 1))
+        perm = torch.randperm(self.n_blocks, generator=torch.Generator().manual_seed(self.seed + 1))
         bt = torch.zeros((batch, self.blocks_per_seq), dtype=torch.int32)
         o = 0
         for i, nb in enumerate(nblk):
@@ -189,7 +284,7 @@ class Decoder:
         self.next_tokens = torch.zeros(batch, dtype=torch.long, device=dev)
         self.logits = torch.empty((batch, cfg.vocab), device=dev)
         self.logits_r = torch.empty((batch, self.vocab_r), device=dev)
-        self.gathered = torch.empty((tp_size, batch, self.vocab_r), device=dev)
+        self.gathered = torch.empty((self.tp_size, batch, self.vocab_r), device=dev)
         self._scratch = {}
         self.graph = None
 
@@ -202,6 +297,18 @@ class Decoder:
             d = b[..., :2].contiguous().view(torch.float16).float()
             q = b[..., 2:].contiguous().view(torch.int8).float()
             return (q * d).reshape(n, k).to(torch.float16)
+        if w.qtype == Q4_K:
+            # d, dmin (fp16), 12 bytes of 6-bit scales / mins, 128 bytes of nibbles per 256
+            b = rows.view(n, k // 256, 144)
+            d = b[..., 0:2].contiguous().view(torch.float16).float()
+            dmin = b[..., 2:4].contiguous().view(torch.float16).float()
+            s = b[..., 4:16].to(torch.int32)
+            sc = torch.cat([s[..., 0:4] & 63, (s[..., 8:12] & 15) | ((s[..., 0:4] >> 6) << 4)], -1).float()
+            mn = torch.cat([s[..., 4:8] & 63, (s[..., 8:12] >> 4) | ((s[..., 4:8] >> 6) << 4)], -1).float()
+            qs = b[..., 16:144].to(torch.int32).view(n, k // 256, 4, 32)
+            q = torch.stack([qs & 15, qs >> 4], 3).reshape(n, k // 256, 8, 32).float()
+            out = d[..., None] * sc[..., None] * q - dmin[..., None] * mn[..., None]
+            return out.reshape(n, k).to(torch.float16)
         # Q6_K: ql[128] qh[64] sc[16] d[2] per 256 (gguf layout)
         b = rows.view(n, k // 256, 210)
         ql, qh = b[..., :128].to(torch.int32), b[..., 128:192].to(torch.int32)
@@ -270,19 +377,19 @@ class Decoder:
         for li, L in enumerate(self.layers):
             wqk = L["attn_qk"] if L["qkv_split"] else L["attn_qkv"]
             act = self._actbuf(("attn", wqk.qtype), B, H, wqk.qtype)
-            ops.add_rmsnorm_quantize(x, self.ones_h, cfg.rms_eps, VEC_DOT_TYPE[wqk.qtype], act, delta)
+            ops.add_rmsnorm_quantize(x, L["attn_norm"], cfg.rms_eps, VEC_DOT_TYPE[wqk.qtype], act, delta)
             yqk = self._mm(("qkv", li), wqk, act, B)
             if L["qkv_split"]:
                 wv = L["attn_v"]
                 act_v = act
                 if VEC_DOT_TYPE[wv.qtype] != VEC_DOT_TYPE[wqk.qtype]:
                     act_v = self._actbuf(("attn_v", wv.qtype), B, H, wv.qtype)
-                    ops.add_rmsnorm_quantize(x, self.ones_h, cfg.rms_eps, VEC_DOT_TYPE[wv.qtype], act_v)
+                    ops.add_rmsnorm_quantize(x, L["attn_norm"], cfg.rms_eps, VEC_DOT_TYPE[wv.qtype], act_v)
                 yv, ldv = self._mm(("v", li), wv, act_v, B), kvd
             else:
                 yv, ldv = yqk[:, qd + kvd:], wqk.n
-            ops.qk_norm_rope_kv_append(yqk, wqk.n, yqk[:, qd:], wqk.n, yv, ldv, B, hq, hkv, self.ones_d,
-                                       self.ones_d, cfg.rms_eps, cfg.rope_theta, pos, q_rot,
+            ops.qk_norm_rope_kv_append(yqk, wqk.n, yqk[:, qd:], wqk.n, yv, ldv, B, hq, hkv, L["attn_q_norm"],
+                                       L["attn_k_norm"], cfg.rms_eps, cfg.rope_theta, pos, q_rot,
                                        self.k_arena, self.v_arena, cfg.n_layer, li, self.block_tables)
             ops.paged_attn_decode(q_rot, self.k_arena, self.v_arena, cfg.n_layer, li, self.block_tables,
                                   self.ctx_lens, hkv, self.max_ctx, scale, out=attn_out, scratch=attn_scr)
@@ -292,14 +399,14 @@ class Decoder:
             yo = self._allreduce(self._mm(("o", li), wo, act_o, B))
             wgu = L["ffn_gate_up"]
             act_f = self._actbuf(("ffn", wgu.qtype), B, H, wgu.qtype)
-            ops.add_rmsnorm_quantize(x, self.ones_h, cfg.rms_eps, VEC_DOT_TYPE[wgu.qtype], act_f, yo)
+            ops.add_rmsnorm_quantize(x, L["ffn_norm"], cfg.rms_eps, VEC_DOT_TYPE[wgu.qtype], act_f, yo)
             ygu = self._mm(("gu", li), wgu, act_f, B)
             wd = L["ffn_down"]
             act_d = self._actbuf(("down", wd.qtype), B, ffn, wd.qtype)
             ops.swiglu_quantize(ygu, ygu[:, ffn:], 2 * ffn, B, ffn, VEC_DOT_TYPE[wd.qtype], act_d)
             delta = self._allreduce(self._mm(("down", li), wd, act_d, B))
         act_h = self._actbuf(("head", self.output.qtype), B, H, self.output.qtype)
-        ops.add_rmsnorm_quantize(x, self.ones_h, cfg.rms_eps, VEC_DOT_TYPE[self.output.qtype], act_h, delta)
+        ops.add_rmsnorm_quantize(x, self.output_norm, cfg.rms_eps, VEC_DOT_TYPE[self.output.qtype], act_h, delta)
         if self.tp_size == 1:
             self.logits.copy_(self._mm(("head",), self.output, act_h, B))
         else:  # vocab-split LM head: gather the shards' columns

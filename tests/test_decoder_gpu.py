@@ -18,8 +18,10 @@ def tiny(wtype, q6k_alt=()):
                          vocab=512, wtype=wtype, q6k_alternate=q6k_alt)
 
 
-def reference_step(dec, tokens, ctx_lens):
+def reference_step(dec, tokens, ctx_lens, norms=None):
+    """norms: GGUF-named norm weight vectors (default: ones, the random-init decoder's)."""
     cfg = dec.cfg
+    nw = (lambda name: norms[name].astype(np.float64)) if norms else (lambda name: 1.0)
     B, D, hq, hkv = dec.batch, cfg.head_dim, cfg.n_head, cfg.n_head_kv
     ka = dec.k_arena.cpu().numpy().copy()
     va = dec.v_arena.cpu().numpy().copy()
@@ -27,8 +29,8 @@ def reference_step(dec, tokens, ctx_lens):
     pos = np.array(ctx_lens) - 1
     inv = 1.0 / (cfg.rope_theta ** (np.arange(0, D, 2, dtype=np.float64) / D))
 
-    def rms(x):
-        return x / np.sqrt((x * x).mean(-1, keepdims=True) + cfg.rms_eps)
+    def rms(x, w=1.0):
+        return x / np.sqrt((x * x).mean(-1, keepdims=True) + cfg.rms_eps) * w
 
     def rope(x):
         ang = pos[:, None].astype(np.float64) * inv[None, :]
@@ -45,21 +47,24 @@ def reference_step(dec, tokens, ctx_lens):
 
     x = dec.tok_embd.cpu().float().numpy().astype(np.float64)[tokens]
     for li in range(cfg.n_layer):
-        h = rms(x)
+        p = f"blk.{li}."
+        h = rms(x, nw(p + "attn_norm.weight"))
         q = mm(li, "attn_q", h).reshape(B, hq, D)
         k = mm(li, "attn_k", h).reshape(B, hkv, D)
         v = mm(li, "attn_v", h).reshape(B, hkv, D)
-        q, k = rope(rms(q)), rope(rms(k))
+        if cfg.qk_norm:
+            q, k = rms(q, nw(p + "attn_q_norm.weight")), rms(k, nw(p + "attn_k_norm.weight"))
+        q, k = rope(q), rope(k)
         O.kv_append(k.astype(np.float32), v.astype(np.float32), ka, va, cfg.n_layer, li, bt,
                     np.arange(B, dtype=np.int32), pos.astype(np.int32))
         att = O.paged_attn_decode(q.astype(np.float32), ka, va, cfg.n_layer, li, bt,
                                   np.array(ctx_lens, np.int32), hkv, 1.0 / math.sqrt(D), nthreads=8)
         x = x + mm(li, "attn_output", att.reshape(B, hq * D).astype(np.float64))
-        h = rms(x)
+        h = rms(x, nw(p + "ffn_norm.weight"))
         g = mm(li, "ffn_gate", h)
         u = mm(li, "ffn_up", h)
         x = x + mm(li, "ffn_down", g / (1.0 + np.exp(-g)) * u)
-    return mm(None, None, rms(x))
+    return mm(None, None, rms(x, nw("output_norm.weight")))
 
 
 @pytest.mark.parametrize("layout", ["q8_0", "q4_k_m"])
