@@ -136,10 +136,20 @@ def cpu_reference(budget_s: float):
         el = time.perf_counter() - t0
         if el >= budget_s:
             break
-    return {"value": WEIGHT_BYTES * steps / el / 1e9, "unit": UNIT, "cores": threads,
-            "kind": "port", "steps": steps, "seconds": el,
-            "sample": f"{steps} full steps (both FFN matmuls, M=1) of config 2 on {threads} "
-                      f"host threads, oracle restatement of ggml vec_dot_q4_K_q8_K"}
+    out = {"value": WEIGHT_BYTES * steps / el / 1e9, "unit": UNIT, "cores": threads,
+           "kind": "port", "steps": steps, "seconds": el,
+           "sample": f"{steps} full steps (both FFN matmuls, M=1) of config 2 on {threads} "
+                     f"host threads, oracle restatement of ggml vec_dot_q4_K_q8_K"}
+    # side datapoint: DenseCore's own INT4 decode GEMV (its custom INT4 format, group 128) on the
+    # same shapes -- the reference's best-ISA integer GEMV that is compiled here
+    r = O.ref_int4_gemv(SHAPES, 128, threads, max(1.0, budget_s / 2))
+    if r is not None:
+        out["reference_int4"] = {
+            "value": r["weight_bytes_per_pass"] * r["passes"] / r["seconds"] / 1e9, "unit": UNIT,
+            "kind": "reference", "cores": threads, "isa": r["isa"],
+            "sample": f"{r['passes']} passes over W_up and W_down (M=1) with GemvInt4 "
+                      f"(core/src/kernels/cpu_int4.cpp) in DenseCore's INT4 format, group 128"}
+    return out
 
 
 def matmul_point(qtype: int, n: int, k: int, m: int, dev, reps: int = 20) -> dict:

@@ -235,12 +235,23 @@ __global__ void __launch_bounds__((MA_CONS + 1) * 32, 2) paged_attn_mma_kernel(
         uint32_t ph0, pl0, ph1, pl1;
         split_h2(p[0], p[1], ph0, pl0);   // a0: tokens 2tig, 2tig+1
         split_h2(p[2], p[3], ph1, pl1);   // a2: tokens 8+2tig, 9+2tig
+        // slots past the context hold whatever the arena held (possibly NaN / Inf bit patterns):
+        // P is 0 there, but 0 * NaN is NaN, so their V halves are zeroed as well (B fragment:
+        // low half = the lower token of each pair)
+        const uint32_t vm01 = (tk[0] < ntok ? 0x0000FFFFu : 0u) | (tk[1] < ntok ? 0xFFFF0000u : 0u);
+        const uint32_t vm23 = (tk[2] < ntok ? 0x0000FFFFu : 0u) | (tk[3] < ntok ? 0xFFFF0000u : 0u);
 #pragma unroll
         for (int n2 = 0; n2 < 8; n2++) {
             // matrices: m0 tok 0-7 dims 16n2.., m1 tok 8-15 dims 16n2.., m2 tok 0-7 dims 16n2+8.., m3 tok 8-15 dims 16n2+8..
             const int tok = (mi & 1) * 8 + mr, ch = 2 * n2 + (mi >> 1);
             uint32_t v0, v1, v2, v3;
             ldsm_x4_t(swz(vt, tok, ch), v0, v1, v2, v3);
+            if (ntok < KVB) {   // the last, partial block of the sequence
+                v0 &= vm01;
+                v2 &= vm01;
+                v1 &= vm23;
+                v3 &= vm23;
+            }
             float c0[4] = {o[2 * n2][0], o[2 * n2][1], 0.f, 0.f};
             float c1[4] = {o[2 * n2 + 1][0], o[2 * n2 + 1][1], 0.f, 0.f};
             mma_f16(c0, ph0, 0u, ph1, 0u, v0, v1);

@@ -69,6 +69,27 @@ def ref_lib():
     return _ref
 
 
+def ref_int4_gemv(shapes, group: int, threads: int, budget_s: float) -> dict | None:
+    """Times DenseCore's own INT4 decode GEMV (core/src/kernels/cpu_int4.cpp, runtime ISA dispatch)
+    over the (n, k) shapes for about budget_s seconds; None when it was never built here."""
+    path = os.path.join(HERE, "_ref", "libref_int4.so")
+    if not os.path.exists(path):
+        return None
+    R = ctypes.CDLL(path)
+    R.ref_int4_isa.restype = ctypes.c_char_p
+    R.ref_int4_time.restype = ctypes.c_long
+    R.ref_int4_time.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                ctypes.c_int, ctypes.c_double, ctypes.c_void_p]
+    ns = (ctypes.c_int * len(shapes))(*[n for n, _ in shapes])
+    ks = (ctypes.c_int * len(shapes))(*[k for _, k in shapes])
+    sec = ctypes.c_double()
+    passes = R.ref_int4_time(ns, ks, len(shapes), group, threads, budget_s, ctypes.byref(sec))
+    # bytes per row: K/2 packed nibbles + an f32 scale and zero per group
+    wbytes = sum(n * (k // 2 + 8 * (k // group)) for n, k in shapes)
+    return {"passes": int(passes), "seconds": sec.value, "weight_bytes_per_pass": wbytes,
+            "isa": R.ref_int4_isa().decode()}
+
+
 def _p(a: np.ndarray):
     assert a.flags["C_CONTIGUOUS"]
     return a.ctypes.data_as(ctypes.c_void_p)

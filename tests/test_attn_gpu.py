@@ -105,3 +105,27 @@ def test_kv_append_bit_exact(ops):
     ops.kv_append(dev(k), dev(v), kd, vd, n_layer, 2, dev(bt), dev(seq), dev(pos))
     assert np.array_equal(kd.cpu().numpy().view(np.uint16), ka_ref.view(np.uint16))
     assert np.array_equal(vd.cpu().numpy().view(np.uint16), va_ref.view(np.uint16))
+
+
+def test_attention_ignores_slots_past_the_context(ops):
+    """Arena slots past each sequence's context (the tail of its last block) may hold anything,
+    NaN and Inf bit patterns included: the output must equal the oracle's, which reads only
+    positions 0..ctx_len-1."""
+    rng = np.random.default_rng(17)
+    ctx, hq, hkv, n_layer, layer = [1, 7, 16, 21, 40], 16, 8, 2, 0
+    ka, va, bt = make_cache(rng, ctx, hkv, n_layer)
+    for s, c in enumerate(ctx):
+        for p in range(c, ((c + 15) // 16) * 16):
+            blk = bt[s, p // 16] * n_layer + layer
+            ka[blk, p % 16] = np.nan
+            va[blk, p % 16] = np.inf if p % 2 else np.nan
+    q = rng.standard_normal((len(ctx), hq, 128)).astype(np.float32)
+    scale = 1.0 / np.sqrt(128.0)
+    ref = O.paged_attn_decode(q, ka, va, n_layer, layer, bt, np.array(ctx), hkv, scale, nthreads=8)
+    assert np.isfinite(ref).all()
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    out = ops.paged_attn_decode(dev(q), dev(ka), dev(va), n_layer, layer, dev(bt),
+                                dev(np.array(ctx, np.int32)), hkv, max(ctx)).cpu().numpy()
+    assert np.isfinite(out).all()
+    err = np.linalg.norm(out - ref, axis=-1) / (np.linalg.norm(ref, axis=-1) + 1e-30)
+    assert err.max() < ATOL_REL
