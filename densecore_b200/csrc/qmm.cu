@@ -365,6 +365,7 @@ __global__ void __launch_bounds__(M1_THREADS, M1_CTAS)
     };
     if (warp == M1_WARPS && lane == 0)
         for (int c = 0; c < pre; c++) issue(c);
+    pdl_wait();
     constexpr int NW = M1_WARPS + 1;
     if (QX) {  // quantize: warp w takes super-blocks w, w + 5, ..., two at a time (loads overlap)
         for (int s = warp; s < nchunks; s += 2 * NW) {
@@ -460,7 +461,6 @@ __global__ void __launch_bounds__(M1_THREADS, M1_CTAS)
             ypart[warp * 16 + gid + 8] = yB;
         }
     }
-    pdl_trigger();
     // every thread of every CTA of the cluster reaches both barriers, on the error path too
     cluster_sync_all();
     if (cluster_rank() == 0 && threadIdx.x < QMM_ROWS && r0 + threadIdx.x < n) {
@@ -469,6 +469,7 @@ __global__ void __launch_bounds__(M1_THREADS, M1_CTAS)
         y[r0 + threadIdx.x] = sum;
     }
     cluster_sync_all();   // keeps every CTA's partials alive until rank 0 has read them
+    pdl_trigger();
 }
 
 // split-K count: as many splits as still fit one wave of resident CTAs (ctas_per_sm x 148 SMs),
@@ -592,16 +593,19 @@ static cudaError_t launch_q4k_m1(const uint8_t* W, int64_t n, int64_t k, const A
     cfg.blockDim = dim3(M1_THREADS);
     cfg.dynamicSmemBytes = M1_HDR + (size_t)M1_STAGES * M1_STAGE + (size_t)sps * M1_XQ;
     cfg.stream = st;
-    // Plain stream order, not a programmatic dependent: launched early into a GPU still draining
-    // the previous grid, the clusters land unevenly and a config-2 step (two launches) measured
-    // 28.3 us against 21.1 us in stream order.
-    cudaLaunchAttribute at[1];
+    // A programmatic dependent whose own dependents are released only at its exit (after the
+    // cluster reduction).  Released earlier, the next grid's clusters landed in a GPU still
+    // holding this one and a config-2 step measured 28.3 us; in plain stream order 20.6 us; with
+    // the release at exit 19.5 us (the next launch overlaps this one's drain).
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = 1;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = S;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, qmm_q4k_m1_kernel<QX>, wmap, nb, n, a, x, y, sps);
 }
 

@@ -151,6 +151,7 @@ __global__ void __launch_bounds__(RD_WARPS * 32) qmm_q8_0_rd_kernel(PackedW w, i
 
     if (!live) {   // rows past n: no loads, but the warp still takes part in the split reduction
         rd_store<NT>(acc, red, y, n, m, (int64_t)blockIdx.x * RD_WARPS * 16, c0, warp, gid, tig, false);
+        pdl_trigger();
         return;
     }
     Q80Frag cur, nxt;
@@ -181,8 +182,8 @@ __global__ void __launch_bounds__(RD_WARPS * 32) qmm_q8_0_rd_kernel(PackedW w, i
         }
         if (sb + 1 < nsb) cur = nxt;
     }
-    pdl_trigger();
     rd_store<NT>(acc, red, y, n, m, (int64_t)blockIdx.x * RD_WARPS * 16, c0, warp, gid, tig, live);
+    pdl_trigger();   // after the split reduction: see the Q4_K M = 1 kernel
 }
 
 // ------------------------------------------------------------------------------------------
@@ -259,6 +260,7 @@ __global__ void __launch_bounds__(RD_WARPS * 32) qmm_q6k_rd_kernel(PackedW w, in
 
     if (!live) {   // rows past n: no loads, but the warp still takes part in the split reduction
         rd_store<NT>(acc, red, y, n, m, (int64_t)blockIdx.x * RD_WARPS * 16, c0, warp, gid, tig, false);
+        pdl_trigger();
         return;
     }
     Q6Frag cur, nxt;
@@ -291,8 +293,8 @@ __global__ void __launch_bounds__(RD_WARPS * 32) qmm_q6k_rd_kernel(PackedW w, in
         }
         if (sb + 1 < nsb) cur = nxt;
     }
-    pdl_trigger();
     rd_store<NT>(acc, red, y, n, m, (int64_t)blockIdx.x * RD_WARPS * 16, c0, warp, gid, tig, live);
+    pdl_trigger();   // after the split reduction: see the Q4_K M = 1 kernel
 }
 
 // grid (row blocks, column blocks, splits): split K until one wave of resident CTAs is filled, at

@@ -365,12 +365,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
         cluster_sync_all();
     }
-    pdl_trigger();
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::TMEM_COLS)
                      : "memory");
     }
+    pdl_trigger();   // dependents are released only after this CTA's tensor memory is free
 }
 
 // ---- host side ----
@@ -430,13 +430,15 @@ static cudaError_t launch_tc_t(const uint8_t* W, int64_t n, int64_t k, const Act
     cfg.blockDim = dim3(TC_THREADS);
     cfg.dynamicSmemBytes = C::SMEM;
     cfg.stream = st;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = 1;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = S;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, qmm_q4k_tc_kernel<N>, wm, am, nb, n, a, m, y, sps);
 }
 
