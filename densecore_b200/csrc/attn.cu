@@ -154,7 +154,7 @@ __global__ void __launch_bounds__((MA_CONS + 1) * 32, 2) paged_attn_mma_kernel(
     __syncthreads();
 
     bool ok = true;
-    if (warp == MA_CONS) {  // producer: 4 swizzled half-tiles per block
+    if (warp == MA_CONS) {  // producer: K and V tiles of each block, one box each
         if (lane == 0) {
             for (int i = 0; i < nbh && ok; i++) {
                 const int st = i % MA_STAGES;
@@ -165,10 +165,9 @@ __global__ void __launch_bounds__((MA_CONS + 1) * 32, 2) paged_attn_mma_kernel(
                 const int slot = (phys * n_layer + layer) * KVB;
                 uint8_t* dst = ring + (size_t)st * MA_STAGE;
                 mbar_arrive_expect_tx(&full[st], MA_STAGE);
-                tma_load_3d(dst, &kmap, 0, kvh, slot, &full[st]);
-                tma_load_3d(dst + MA_HALF, &kmap, 64, kvh, slot, &full[st]);
-                tma_load_3d(dst + 2 * MA_HALF, &vmap, 0, kvh, slot, &full[st]);
-                tma_load_3d(dst + 3 * MA_HALF, &vmap, 64, kvh, slot, &full[st]);
+                // one box per tile: 64 dims x 16 tokens x 2 halves -> the two swizzled half-tiles
+                tma_load_4d(dst, &kmap, 0, slot, 0, kvh, &full[st]);
+                tma_load_4d(dst + 2 * MA_HALF, &vmap, 0, slot, 0, kvh, &full[st]);
             }
         }
         ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -380,11 +379,13 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn();  // qmm.cu
 static cudaError_t make_kv_map(CUtensorMap* map, const void* arena, int hkv, int64_t n_slots) {
     auto fn = encode_fn();
     if (!fn) return cudaErrorNotSupported;
-    const cuuint64_t dims[3] = {(cuuint64_t)HD, (cuuint64_t)hkv, (cuuint64_t)n_slots};
-    const cuuint64_t strides[2] = {(cuuint64_t)HD * 2, (cuuint64_t)hkv * HD * 2};
-    const cuuint32_t box[3] = {64, 1, (cuuint32_t)KVB};
-    const cuuint32_t es[3] = {1, 1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(arena), dims, strides, box,
+    // (64 dims of a half, slot, half, kv head): one box of 64 x 16 tokens x 2 halves fills the
+    // [half][token][64] smem tile, each 128-B row swizzled
+    const cuuint64_t dims[4] = {64u, (cuuint64_t)n_slots, 2u, (cuuint64_t)hkv};
+    const cuuint64_t strides[3] = {(cuuint64_t)hkv * HD * 2, 128u, (cuuint64_t)HD * 2};
+    const cuuint32_t box[4] = {64, (cuuint32_t)KVB, 2, 1};
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(arena), dims, strides, box,
                     es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;

@@ -86,6 +86,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* map, int x, i
         : "memory");
 }
 
+// 4-D tiled tensor copy global -> shared (no multicast); x innermost
+__device__ __forceinline__ void tma_load_4d(void* dst, const void* map, int x, int y, int z, int w, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // ---- thread-block clusters (distributed shared memory) ----
 __device__ __forceinline__ float ld_cluster_f32(const float* p, uint32_t rank) {
     uint32_t addr;
