@@ -156,7 +156,6 @@ __global__ void __launch_bounds__(QMM_THREADS, NT >= 4 ? 1 : (NT >= 2 ? 2 : 3))
         ok = mbar_wait(&full[c % QMM_STAGES], (uint32_t)((c / QMM_STAGES) & 1), &g_qmm_error) && ok;
         if (!ok) break;
         const uint8_t* stage = buf + (size_t)(c % QMM_STAGES) * SB_BYTES;
-#ifndef DCG_QMM_NOCOMPUTE
         // both super-blocks of the chunk, unconditionally (ILP): one that is absent (zero-filled by
         // the tensor copy) or belongs to the next split has dx = 0 and adds nothing
 #pragma unroll
@@ -231,7 +230,6 @@ __global__ void __launch_bounds__(QMM_THREADS, NT >= 4 ? 1 : (NT >= 2 ? 2 : 3))
                 }
             }
         }
-#endif
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[c % QMM_STAGES]);
     }
@@ -413,7 +411,6 @@ __global__ void __launch_bounds__(M1_THREADS, M1_CTAS)
             ok = mbar_wait(&full[c % M1_STAGES], (uint32_t)((c / M1_STAGES) & 1), &g_qmm_error);
             if (!ok) break;
             const uint8_t* stage = ring + (size_t)(c % M1_STAGES) * M1_STAGE;
-#ifndef DCG_QMM_NOCOMPUTE
             const uint8_t* rowA = stage + (warp * 16 + gid) * M1_SROW;
             const uint8_t* rowB = rowA + 8 * M1_SROW;
             const uint4 hA = *(const uint4*)rowA, hB = *(const uint4*)rowB;
@@ -448,7 +445,6 @@ __global__ void __launch_bounds__(M1_THREADS, M1_CTAS)
             const float2 dB = __half22float2(*reinterpret_cast<const __half2*>(&hB.x));
             yA += dx * (dA.x * (float)isA - dA.y * (float)msA);
             yB += dx * (dB.x * (float)isB - dB.y * (float)msB);
-#endif
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[c % M1_STAGES]);
         }
