@@ -10,7 +10,7 @@
 // Arena element (block, layer, slot, head, dim) = ((block*n_layer + layer)*16 + slot)*hkv*D +
 // head*D + dim, fp16.
 //
-// paged_attn_mma_kernel<NREP>: one CTA (3 consumer warps + 1 producer warp, 3 CTAs per SM) per
+// paged_attn_mma_kernel<NREP>: one CTA (3 consumer warps + 1 producer warp, 2 CTAs per SM) per
 // (sequence, kv head, split of the KV blocks); consumer warp w takes blocks w, w+3, ... through
 // ring stages that hold its next two blocks while it computes one; the NREP query heads that share the kv head are served
 // together so every K/V byte is read once.  Scores and P.V run on the tensor cores with an
@@ -62,7 +62,7 @@ cudaError_t attn_device_error(int* out, bool clear) {
 // Tiles arrive by TMA with 128-byte swizzle (two 64-dim halves per tile) so every ldmatrix is
 // bank-conflict free: 16-byte chunk c of row r sits at chunk c ^ (r & 7).
 // ------------------------------------------------------------------------------------------
-constexpr int MA_CONS = 3;                 // consumer warps (+1 producer): 3 x 9 stages, 3 CTAs per SM
+constexpr int MA_CONS = 3;                 // consumer warps (+1 producer): 3 x 9 stages, 2 CTAs per SM
 constexpr int MA_STAGES = 9;                // 3 per consumer warp: its next blocks load while it computes
 constexpr int MA_HALF = KVB * 64 * 2;      // 2 KB: 16 rows x 64 dims
 constexpr int MA_STAGE = 4 * MA_HALF;      // K lo | K hi | V lo | V hi = 8 KB
