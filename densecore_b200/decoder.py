@@ -98,7 +98,7 @@ class Decoder:
         full random weights and keeps its slice (bitwise the tp_size = 1 model); "local": each rank
         draws only its shard (faster; a different random model).  seq_tokens: per-sequence token
         capacity; the arena then holds exactly those blocks (default: max_ctx for every sequence).
-        weights: GGUF-named tensors (gguf_file.decoder_weights) instead of random ones; tp_size 1."""
+        weights: GGUF-named tensors (gguf_file.decoder_weights) instead of random ones."""
         self.cfg, self.batch, self.max_ctx = cfg, batch, max_ctx
         self.tp_rank, self.tp_size, self.tp_group = tp_rank, tp_size, tp_group
         self.seed = seed
@@ -131,8 +131,6 @@ class Decoder:
         self.ones_h = torch.ones(H, device=dev)
         self.ones_d = torch.ones(D, device=dev) if cfg.qk_norm else None
         if weights is not None:
-            if tp_size != 1:
-                raise NotImplementedError("GGUF weights are loaded with tp_size = 1")
             self._load_weights(weights)
             self._init_cache(batch, max_ctx, seq_tokens)
             return
@@ -180,9 +178,29 @@ class Decoder:
 
     def _load_weights(self, w: dict):
         """Weights from GGUF-named tensors: ggml rows go to the device as they are; q|k|v and
-        gate|up are stacked by concatenating rows (rows are quantized independently)."""
-        cfg, dev, H = self.cfg, self.device, self.cfg.hidden
+        gate|up are stacked by concatenating rows (rows are quantized independently).  With
+        tp_size > 1 each rank keeps its tp_plan shard: whole rows, or whole blocks of columns."""
+        from .gguf_file import shard_cols, shard_rows
+        cfg, dev, H, plan = self.cfg, self.device, self.cfg.hidden, self.plan
         supported = (Q8_0, Q4_K, Q6_K)
+        if self.tp_size > 1:
+            w = dict(w)
+            rows_of = {"attn_q": "q_rows", "attn_k": "kv_rows", "attn_v": "kv_rows", "ffn_gate": "ffn_rows",
+                       "ffn_up": "ffn_rows"}
+            cols_of = {"attn_output": "o_cols", "ffn_down": "down_cols"}
+            for name, v in list(w.items()):
+                if not isinstance(v, tuple) or not name.startswith("blk."):
+                    continue
+                base = name.split(".")[2]
+                r, t, k = v
+                if base in rows_of:
+                    w[name] = (shard_rows(r, *plan[rows_of[base]]), t, k)
+                elif base in cols_of:
+                    sr, sk = shard_cols(r, t, k, *plan[cols_of[base]])
+                    w[name] = (sr, t, sk)
+            head = "output.weight" if "output.weight" in w else "token_embd.weight"
+            r, t, k = w[head]
+            w["output.weight"] = (shard_rows(r, *plan["vocab_rows"]), t, k)
 
         def to_dev(a):
             # tensors of a memory-mapped file are read-only views: only read here (copied to the device)
@@ -238,7 +256,7 @@ class Decoder:
             emb = None
         else:
             raise ValueError(f"token_embd: ggml type {et} is not supported")
-        if "output.weight" in w:
+        if "output.weight" in w:   # untied, or this rank's vocabulary rows of a tied head
             self.output = ops.QuantWeight.from_ggml(*rows("output.weight"))
         elif emb is not None:      # tied: the LM head is the embedding matrix itself
             self.output = emb
@@ -247,13 +265,14 @@ class Decoder:
 
     @classmethod
     def from_gguf(cls, path: str, batch: int, max_ctx: int, device: str | torch.device = "cuda",
-                  seq_tokens=None) -> "Decoder":
+                  seq_tokens=None, tp_rank: int = 0, tp_size: int = 1, tp_group=None) -> "Decoder":
         """A decoder holding the weights of a GGUF checkpoint (tensor names and hyper-parameter
-        keys of DenseCore's loader, core/src/model_loader.cpp:154-403)."""
+        keys of DenseCore's loader, core/src/model_loader.cpp:154-403); with tp_size > 1, this
+        rank's tensor-parallel shard of them."""
         from .gguf_file import GGUFFile, decoder_config, decoder_weights
         g = GGUFFile(path)
         return cls(decoder_config(g), batch, max_ctx, device=device, seq_tokens=seq_tokens,
-                   weights=decoder_weights(g))
+                   weights=decoder_weights(g), tp_rank=tp_rank, tp_size=tp_size, tp_group=tp_group)
 
     def _init_cache(self, batch, max_ctx, seq_tokens):
         cfg, dev, H, D = self.cfg, self.device, self.cfg.hidden, self.cfg.head_dim

@@ -150,6 +150,21 @@ class GGUFFile:
         return default
 
 
+def shard_rows(rows: np.ndarray, r0: int, r1: int) -> np.ndarray:
+    """Output rows [r0, r1) of a weight in ggml rows (rows are quantized independently)."""
+    return rows[r0:r1]
+
+
+def shard_cols(rows: np.ndarray, ggml_type: int, k: int, c0: int, c1: int) -> tuple[np.ndarray, int]:
+    """Input columns [c0, c1) of a weight in ggml rows, for a K-split shard.  The bounds must fall on
+    block boundaries; a block is then kept whole, so the shard equals quantizing the sliced matrix."""
+    from .ggml_types import block_size, type_size
+    bs, bb = block_size(ggml_type), type_size(ggml_type)
+    if c0 % bs or c1 % bs or not 0 <= c0 < c1 <= k:
+        raise ValueError(f"columns [{c0}, {c1}) do not fall on {bs}-value block boundaries of K={k}")
+    return np.ascontiguousarray(rows[:, c0 // bs * bb: c1 // bs * bb]), c1 - c0
+
+
 def decoder_config(g: GGUFFile):
     """DecoderConfig of a GGUF decoder checkpoint (Llama / Qwen2 / Qwen3 families)."""
     from .decoder import DecoderConfig

@@ -45,3 +45,36 @@ def test_rejects_bad_files(tmp_path):
     (tmp_path / "short.gguf").write_bytes(data[: len(data) // 2])
     with pytest.raises(ValueError, match="past the end|truncated"):
         gguf_file.GGUFFile(str(tmp_path / "short.gguf"))
+
+
+@pytest.mark.parametrize("t", [O.Q8_0, O.Q4_K, O.Q6_K])
+def test_shards_equal_quantized_slices(t):
+    """A tensor-parallel shard of file weights (whole rows, or whole blocks of columns) has the
+    bytes of the quantized slice of the matrix, so sharded ranks hold exactly the unsplit model."""
+    rng = np.random.default_rng(t)
+    n, k = 96, 1024
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    rows = O.quantize(w, t)
+    assert np.array_equal(gguf_file.shard_rows(rows, 32, 80), O.quantize(w[32:80], t))
+    sc, sk = gguf_file.shard_cols(rows, t, k, 256, 768)
+    assert sk == 512 and np.array_equal(sc, O.quantize(np.ascontiguousarray(w[:, 256:768]), t))
+    with pytest.raises(ValueError, match="block boundaries"):
+        gguf_file.shard_cols(rows, t, k, 16 if t == O.Q8_0 else 128, 768)
+
+
+def test_tp_shard_plan_on_file_weights(tmp_path):
+    """The decoder's tensor-parallel plan applied to GGUF weights: every rank's shard of every
+    linear weight is well formed and the shards tile the unsplit weight."""
+    from densecore_b200.decoder import tp_plan
+    path = str(tmp_path / "tiny.gguf")
+    write_tiny_gguf(path, qk_norm=False)
+    g = gguf_file.GGUFFile(path)
+    cfg = gguf_file.decoder_config(g)
+    w = gguf_file.decoder_weights(g)
+    plans = [tp_plan(cfg, r, 2) for r in range(2)]
+    r, t, k = w["blk.0.ffn_down.weight"]
+    parts = [gguf_file.shard_cols(r, t, k, *p["down_cols"]) for p in plans]
+    assert sum(pk for _, pk in parts) == k
+    assert np.array_equal(np.concatenate([pr for pr, _ in parts], axis=1), r)
+    r, t, k = w["blk.1.attn_q.weight"]
+    assert np.array_equal(np.concatenate([gguf_file.shard_rows(r, *p["q_rows"]) for p in plans]), r)
