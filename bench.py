@@ -9,7 +9,7 @@ on the fly, then the Q4_K GEMV).  Weights come from an 8-slot ring of distinct s
 
 Prints one JSON line (rank 0).  value = weight GB/s of the whole job; e2e = the same metric
 through the host-pointer C ABI (dcg_ctx_mul_mat: H2D of x, both kernels, D2H of y, per call).
---impl reference times the CPU implementation of the same op (the oracle restatement of ggml's
+--impl reference times the CPU implementation of the same op (the AVX2 restatement of ggml's
 vec_dot / quantize_row_q8_K, all host threads) on a bounded sample of the same workload.
 """
 from __future__ import annotations
@@ -114,9 +114,10 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
-def cpu_reference(budget_s: float):
-    """The oracle's row-sliced mul_mat (ggml vec_dot_q4_K_q8_K restated) plus quantize_row_q8_K
-    on all host threads, on the same shapes; repeats whole steps until ~budget_s elapsed."""
+def cpu_reference(budget_s: float, int4: bool = True):
+    """The oracle's row-sliced mul_mat (ggml vec_dot_q4_K_q8_K restated, AVX2 dots bit-identical
+    to the scalar ones) plus quantize_row_q8_K on all host threads, on the same shapes; repeats
+    whole steps until ~budget_s elapsed.  int4: also time DenseCore's own INT4 GEMV."""
     import numpy as np
 
     from oracle import oracle as O
@@ -131,7 +132,7 @@ def cpu_reference(budget_s: float):
     while True:
         for wq, k, x in mats:
             xq = O.quantize(x, O.Q8_K)
-            O.mul_mat(O.Q4_K, wq, k, xq, 1, nthreads=threads)
+            O.mul_mat(O.Q4_K, wq, k, xq, 1, nthreads=threads, simd=True)
         steps += 1
         el = time.perf_counter() - t0
         if el >= budget_s:
@@ -139,10 +140,11 @@ def cpu_reference(budget_s: float):
     out = {"value": WEIGHT_BYTES * steps / el / 1e9, "unit": UNIT, "cores": threads,
            "kind": "port", "steps": steps, "seconds": el,
            "sample": f"{steps} full steps (both FFN matmuls, M=1) of config 2 on {threads} "
-                     f"host threads, oracle restatement of ggml vec_dot_q4_K_q8_K"}
+                     f"host threads, AVX2 restatement of ggml vec_dot_q4_K_q8_K"
+                     f"{'' if O.simd_available() else ' (scalar: no AVX2 on this CPU)'}"}
     # side datapoint: DenseCore's own INT4 decode GEMV (its custom INT4 format, group 128) on the
     # same shapes -- the reference's best-ISA integer GEMV that is compiled here
-    r = O.ref_int4_gemv(SHAPES, 128, threads, max(1.0, budget_s / 2))
+    r = O.ref_int4_gemv(SHAPES, 128, threads, max(1.0, budget_s / 2)) if int4 else None
     if r is not None:
         out["reference_int4"] = {
             "value": r["weight_bytes_per_pass"] * r["passes"] / r["seconds"] / 1e9, "unit": UNIT,
@@ -439,9 +441,9 @@ def run_reference(args):
     per_step = []
     total = 0.0
     for _ in range(args.warmup):
-        cpu_reference(0.0)
+        cpu_reference(0.0, int4=False)
     for _ in range(args.steps):
-        r = cpu_reference(args.ref_step_seconds)
+        r = cpu_reference(args.ref_step_seconds, int4=False)
         per_step.append(r)
         total += r["seconds"]
     n_steps = sum(r["steps"] for r in per_step)
@@ -450,7 +452,11 @@ def run_reference(args):
     cb["value"] = round(value, 4)
     cb["sample"] = (f"{args.steps} timed samples of >= {args.ref_step_seconds}s, {n_steps} full steps "
                     f"of config 2 (both FFN matmuls, M=1) on {cb['cores']} host threads; ggml is "
-                    "absent, so this is the oracle restatement of vec_dot_q4_K_q8_K")
+                    "absent, so this is the AVX2 restatement of vec_dot_q4_K_q8_K (bit-identical to "
+                    "the scalar oracle)")
+    side = cpu_reference(0.0, int4=True).get("reference_int4")   # timed once, not per step
+    if side is not None:
+        cb["reference_int4"] = side
     out = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
            "ms_per_step": round(total / n_steps * 1e3, 3), "higher_is_better": True,

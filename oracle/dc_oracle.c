@@ -402,9 +402,53 @@ void dco_block_dots(int type, int n, const void* vw, const void* vx, int32_t* ou
     }
 }
 
+/* ---------------- AVX2 restatement of vec_dot_q4_K (CPU baseline) --------------------------
+ * The same integer sums and the same float operations in the same order as vec_dot_q4_K, so the
+ * result is bit-identical: per pair group g the 32 nibble bytes hold sub-block 2g (low nibbles,
+ * activation bytes 64g..64g+31) and 2g+1 (high nibbles, 64g+32..64g+63); maddubs multiplies the
+ * unsigned nibbles by the signed activation bytes into int16 pairs (|pair| <= 3810, no saturation)
+ * and madd scales them by the sub-block's 6-bit scale into int32. */
+#if defined(__x86_64__)
+#include <immintrin.h>
+__attribute__((target("avx2,fma"))) static float vec_dot_q4_K_avx2(int n, const blk_q4_K* w, const blk_q8_K* x) {
+    const __m256i m4 = _mm256_set1_epi8(0x0F);
+    float sumf = 0.0f;
+    for (int b = 0; b < n / QK_K; b++) {
+        int sc[8], mn[8];
+        for (int j = 0; j < 8; j++) unpack_q4_K_scale(w[b].scales, j, &sc[j], &mn[j]);
+        __m256i acc = _mm256_setzero_si256();
+        for (int g = 0; g < 4; g++) {
+            const __m256i q = _mm256_loadu_si256((const __m256i*)(w[b].qs + 32 * g));
+            const __m256i lo = _mm256_and_si256(q, m4);
+            const __m256i hi = _mm256_and_si256(_mm256_srli_epi16(q, 4), m4);
+            const __m256i xl = _mm256_loadu_si256((const __m256i*)(x[b].qs + 64 * g));
+            const __m256i xh = _mm256_loadu_si256((const __m256i*)(x[b].qs + 64 * g + 32));
+            const __m256i pl = _mm256_madd_epi16(_mm256_maddubs_epi16(lo, xl), _mm256_set1_epi16((short)sc[2 * g]));
+            const __m256i ph = _mm256_madd_epi16(_mm256_maddubs_epi16(hi, xh), _mm256_set1_epi16((short)sc[2 * g + 1]));
+            acc = _mm256_add_epi32(acc, _mm256_add_epi32(pl, ph));
+        }
+        __m128i t = _mm_add_epi32(_mm256_castsi256_si128(acc), _mm256_extracti128_si256(acc, 1));
+        t = _mm_add_epi32(t, _mm_shuffle_epi32(t, 0x4E));
+        t = _mm_add_epi32(t, _mm_shuffle_epi32(t, 0xB1));
+        const int32_t isum = _mm_cvtsi128_si32(t);
+        int32_t ms = 0;
+        for (int j = 0; j < 8; j++) ms += mn[j] * ((int)x[b].bsums[2 * j] + (int)x[b].bsums[2 * j + 1]);
+        const float d = dco_fp16_to_fp32(w[b].d) * x[b].d;
+        const float dmin = dco_fp16_to_fp32(w[b].dmin) * x[b].d;
+        sumf += d * (float)isum;
+        sumf -= dmin * (float)ms;
+    }
+    return sumf;
+}
+static int have_avx2(void) { return __builtin_cpu_supports("avx2"); }
+#else
+static float vec_dot_q4_K_avx2(int n, const blk_q4_K* w, const blk_q8_K* x) { return vec_dot_q4_K(n, w, x); }
+static int have_avx2(void) { return 0; }
+#endif
+
 /* ---------------- threaded row-sliced GEMV/GEMM (cb_gemv_custom, inference.cpp:896-924) ----- */
 typedef struct {
-    int type;
+    int type, simd;
     const uint8_t* w;
     size_t row_stride;
     int64_t n_rows, k, m, r0, r1;
@@ -416,14 +460,34 @@ static void* mm_worker(void* p) {
     mm_job* j = (mm_job*)p;
     const size_t xrow = dco_row_size(j->type == DCO_Q8_0 ? DCO_Q8_0 : DCO_Q8_K, j->k);
     for (int64_t r = j->r0; r < j->r1; r++)
-        for (int64_t i = 0; i < j->m; i++)
-            dco_vec_dot(j->type, (int)j->k, &j->y[i * j->n_rows + r], j->w + r * j->row_stride,
-                        j->xq + i * xrow);
+        for (int64_t i = 0; i < j->m; i++) {
+            float* dst = &j->y[i * j->n_rows + r];
+            if (j->simd)
+                *dst = vec_dot_q4_K_avx2((int)j->k, (const blk_q4_K*)(j->w + r * j->row_stride),
+                                         (const blk_q8_K*)(j->xq + i * xrow));
+            else
+                dco_vec_dot(j->type, (int)j->k, dst, j->w + r * j->row_stride, j->xq + i * xrow);
+        }
     return NULL;
 }
 
+static void mul_mat_threads(int type, int simd, const void* w, size_t row_stride, int64_t n_rows,
+                            int64_t k, const void* xq, int64_t m, float* y, int nthreads);
+
 void dco_mul_mat(int type, const void* w, size_t row_stride, int64_t n_rows, int64_t k,
                  const void* xq, int64_t m, float* y, int nthreads) {
+    mul_mat_threads(type, 0, w, row_stride, n_rows, k, xq, m, y, nthreads);
+}
+
+int dco_mul_mat_simd(int type, const void* w, size_t row_stride, int64_t n_rows, int64_t k,
+                     const void* xq, int64_t m, float* y, int nthreads) {
+    const int simd = type == DCO_Q4_K && have_avx2();
+    mul_mat_threads(type, simd, w, row_stride, n_rows, k, xq, m, y, nthreads);
+    return simd;
+}
+
+static void mul_mat_threads(int type, int simd, const void* w, size_t row_stride, int64_t n_rows,
+                            int64_t k, const void* xq, int64_t m, float* y, int nthreads) {
     if (nthreads < 1) nthreads = 1;
     if (nthreads > 256) nthreads = 256;
     pthread_t th[256];
@@ -433,7 +497,7 @@ void dco_mul_mat(int type, const void* w, size_t row_stride, int64_t n_rows, int
         int64_t r0 = t * per, r1 = r0 + per;
         if (r1 > n_rows) r1 = n_rows;
         if (r0 > n_rows) r0 = n_rows;
-        jobs[t] = (mm_job){type, (const uint8_t*)w, row_stride, n_rows, k, m, r0, r1,
+        jobs[t] = (mm_job){type, simd, (const uint8_t*)w, row_stride, n_rows, k, m, r0, r1,
                            (const uint8_t*)xq, y};
         if (t > 0) pthread_create(&th[t], NULL, mm_worker, &jobs[t]);
     }

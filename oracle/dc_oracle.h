@@ -55,6 +55,11 @@ void dco_block_dots(int type, int n, const void* w, const void* xq, int32_t* out
 void dco_mul_mat(int type, const void* w, size_t row_stride, int64_t n_rows, int64_t k,
                  const void* xq, int64_t m, float* y, int nthreads);
 
+/* The same with the AVX2 restatement of the Q4_K dot (bit-identical results; the CPU baseline's
+ * compute).  Returns 1 when the AVX2 path ran, 0 when it fell back to the scalar dots. */
+int dco_mul_mat_simd(int type, const void* w, size_t row_stride, int64_t n_rows, int64_t k,
+                     const void* xq, int64_t m, float* y, int nthreads);
+
 /* fp16 paged-KV decode attention, one query token per sequence.
  * q [n_seqs][hq][d] f32; k_arena/v_arena fp16 laid out [(block*n_layer+layer)][16][hkv][d];
  * block_tables [n_seqs][max_blocks_per_seq]; ctx_lens[n_seqs]; out [n_seqs][hq][d]. */

@@ -47,6 +47,8 @@ def lib():
         L.dco_vec_dot.argtypes = [i32, i32, vp, vp, vp]
         L.dco_block_dots.argtypes = [i32, i32, vp, vp, vp, vp]
         L.dco_mul_mat.argtypes = [i32, vp, ctypes.c_size_t, i64, i64, vp, i64, vp, i32]
+        L.dco_mul_mat_simd.argtypes = [i32, vp, ctypes.c_size_t, i64, i64, vp, i64, vp, i32]
+        L.dco_mul_mat_simd.restype = i32
         L.dco_paged_attn_decode.argtypes = [vp, vp, vp, i32, i32, vp, i32, vp, i32, i32, i32, i32,
                                             f, vp, i32]
         L.dco_kv_append.argtypes = [vp, vp, vp, vp, i32, i32, vp, i32, vp, vp, i32, i32, i32]
@@ -138,15 +140,22 @@ def block_dots(wtype: int, k: int, w_row: np.ndarray, xq_row: np.ndarray):
     return (a, b) if wtype == Q4_K else a
 
 
-def mul_mat(wtype: int, w: np.ndarray, k: int, xq: np.ndarray, m: int, nthreads: int = 1):
-    """y[m, n_rows] = W . xq (row-sliced over nthreads, like cb_gemv_custom)."""
+def mul_mat(wtype: int, w: np.ndarray, k: int, xq: np.ndarray, m: int, nthreads: int = 1,
+            simd: bool = False):
+    """y[m, n_rows] = W . xq (row-sliced over nthreads, like cb_gemv_custom).  simd: Q4_K dots
+    by the AVX2 restatement (bit-identical; the CPU baseline's compute)."""
     w = np.ascontiguousarray(w, dtype=np.uint8)
     rs = row_size(wtype, k)
     n_rows = w.size // rs
     y = np.zeros((m, n_rows), dtype=np.float32)
-    lib().dco_mul_mat(wtype, _p(w), rs, n_rows, k, _p(np.ascontiguousarray(xq)), m, _p(y),
-                      nthreads)
+    fn = lib().dco_mul_mat_simd if simd else lib().dco_mul_mat
+    fn(wtype, _p(w), rs, n_rows, k, _p(np.ascontiguousarray(xq)), m, _p(y), nthreads)
     return y
+
+
+def simd_available() -> bool:
+    """Whether mul_mat(..., simd=True) runs the AVX2 Q4_K dots on this CPU."""
+    return bool(lib().dco_mul_mat_simd(Q4_K, None, 144, 0, 256, None, 0, None, 1))
 
 
 def paged_attn_decode(q, k_arena, v_arena, n_layer, layer, block_tables, ctx_lens, hkv,
