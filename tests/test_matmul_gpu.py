@@ -167,11 +167,21 @@ def test_host_context_roundtrip(ops):
     wq = O.quantize(w, O.Q4_K)
     ctx = ops.HostContext(0)
     h = ctx.register(wq, O.Q4_K, k)
-    for m in (1, 4):
+    # repeated calls per (weight, m), each with new inputs
+    for m in (1, 4, 1, 4, 1, 4, 16):
         x = rng.standard_normal((m, k)).astype(np.float32)
         y = ctx.mul_mat(h, x)
         xq = O.quantize(x, O.Q8_K)
         _assert_rows_close(y, wq, O.Q4_K, k, xq, O.Q8_K, O.mul_mat(O.Q4_K, wq, k, xq, m, 8))
+    # a second, larger weight grows the context's buffers; the first still works
+    w2 = O.quantize((rng.standard_normal((256, 14336)) * 0.02).astype(np.float32), O.Q4_K)
+    h2 = ctx.register(w2, O.Q4_K, 14336)
+    for _ in range(3):
+        for hh, ww, kk in ((h2, w2, 14336), (h, wq, k)):
+            x = rng.standard_normal((1, kk)).astype(np.float32)
+            xq = O.quantize(x, O.Q8_K)
+            _assert_rows_close(ctx.mul_mat(hh, x), ww, O.Q4_K, kk, xq, O.Q8_K,
+                               O.mul_mat(O.Q4_K, ww, kk, xq, 1, 8))
     ctx.close()
 
 
