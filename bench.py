@@ -15,6 +15,7 @@ vec_dot / quantize_row_q8_K, all host threads) on a bounded sample of the same w
 from __future__ import annotations
 
 import argparse
+import datetime
 import dataclasses
 import json
 import os
@@ -251,7 +252,7 @@ def decode_70b(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if ws > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
     batch, steps = 128, args.steps_70b
     ctx = np.random.default_rng(5).integers(1024, 4097, batch)
     cfg = D.LLAMA3_70B if args.layers_70b <= 0 else dataclasses.replace(D.LLAMA3_70B, n_layer=args.layers_70b)
@@ -310,7 +311,7 @@ def run_ours(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if ws > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
 
     # ---- resident data: RING slots x (W_up, W_down), GPU-encoded from seeded N(0, 0.02) ----
     gen = torch.Generator(device=dev)

@@ -21,6 +21,7 @@ vp, i32, i64, sz, f32 = (ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c
 # argtypes / restype of every exported symbol (kept in sync with include/dcgpu.h by a test)
 SIGNATURES = {
     "dcg_version": (i32, []),
+    "dcg_set_programmatic_launch": (i32, [i32]),
     "dcg_strerror": (ctypes.c_char_p, [i32]),
     "dcg_last_error": (ctypes.c_char_p, []),
     "dcg_device_error": (i32, [ctypes.POINTER(i32), i32]),

@@ -397,14 +397,9 @@ static cudaError_t launch_attn_mma(dim3 grid, cudaStream_t st, const CUtensorMap
                                    const float* q, int n_layer, int layer, const int* bt, int mbs,
                                    const int* ctx, int hq, int hkv, float sl2, int bps, int splits,
                                    float* po, float* pml, float* direct) {
-    static bool attr = false;
     const size_t dyn = 2048 + (size_t)MA_STAGES * MA_STAGE;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(paged_attn_mma_kernel<NR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)dyn);
-        if (e != cudaSuccess) return e;
-        attr = true;
-    }
+    cudaError_t e = DCG_SMEM_ATTR((paged_attn_mma_kernel<NR>), dyn);
+    if (e != cudaSuccess) return e;
     return launch_pdl(paged_attn_mma_kernel<NR>, grid, dim3((MA_CONS + 1) * 32), dyn, st, km, vm, q, n_layer,
                       layer, bt, mbs, ctx, hq, hkv, sl2, bps, splits, po, pml, direct);
 }

@@ -88,6 +88,10 @@ extern "C" {
 
 int dcg_version(void) { return 100; }
 
+int dcg_set_programmatic_launch(int enable) {
+    return dcg::pdl_flag().exchange(enable ? 1 : 0) ? 1 : 0;
+}
+
 const char* dcg_strerror(int code) {
     switch (code) {
         case DCG_OK: return "ok";

@@ -18,6 +18,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
 #include <utility>
 
 #define DCG_TYPE_F32 0
@@ -156,21 +158,89 @@ __device__ __forceinline__ void q4k_scale_min(uint32_t s0, uint32_t s1, uint32_t
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-// launch with the programmatic-stream-serialization attribute (kernel may overlap its predecessor)
+// Process-wide switch for programmatic dependent launch (dcg_set_programmatic_launch).  When off,
+// every launch is plainly stream-ordered: a kernel starts only after its predecessor in the stream
+// has completed, whatever that predecessor is (a collective or another library's kernel included).
+inline std::atomic<int>& pdl_flag() {
+    static std::atomic<int> flag{1};
+    return flag;
+}
+
+// Launch with optional thread-block cluster (cluster_z CTAs along z; 1 = no cluster) and, when the
+// switch above is on, the programmatic-stream-serialization attribute (the kernel may start while
+// its predecessor drains; it reads the predecessor's outputs only after pdl_wait).
 template <typename... KArgs, typename... Args>
-inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                              cudaStream_t st, Args&&... args) {
+inline cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t st, unsigned cluster_z, Args&&... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (cluster_z > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 1;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = cluster_z;
+        na++;
+    }
+    if (pdl_flag().load(std::memory_order_relaxed)) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = na;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args&&... args) {
+    return launch_ex(kernel, grid, block, smem, st, 1u, std::forward<Args>(args)...);
+}
+
+// ---- per-device one-time setup ----
+// Kernel attributes (cudaFuncSetAttribute) and device properties are per device; a process may drive
+// several GPUs from several threads.  per_device_once runs `fn` once for the calling thread's current
+// device and returns its (cached) result.
+constexpr int MAX_DEVICES = 64;
+struct PerDevice {
+    std::once_flag once[MAX_DEVICES];
+    cudaError_t err[MAX_DEVICES] = {};
+};
+template <class F>
+inline cudaError_t per_device_once(PerDevice& pd, F&& fn) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= MAX_DEVICES) return cudaErrorInvalidDevice;
+    std::call_once(pd.once[dev], [&] { pd.err[dev] = fn(); });
+    return pd.err[dev];
+}
+// dynamic shared memory opt-in of `kernel` on the current device (once per device)
+#define DCG_SMEM_ATTR(kernel, bytes)                                                               \
+    ([&]() -> cudaError_t {                                                                        \
+        static ::dcg::PerDevice pd_;                                                               \
+        return ::dcg::per_device_once(pd_, [&] {                                                   \
+            return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(bytes)); \
+        });                                                                                        \
+    }())
+// streaming multiprocessors of the current device (cached per device)
+inline int num_sms() {
+    static int sms[MAX_DEVICES] = {};
+    static PerDevice pd;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) return 148;
+    per_device_once(pd, [&] {
+        int v = 0;
+        cudaError_t e = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        sms[dev] = v > 0 ? v : 148;
+        return e;
+    });
+    return sms[dev];
 }
 
 }  // namespace dcg

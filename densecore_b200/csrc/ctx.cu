@@ -125,7 +125,11 @@ int dcg_ctx_weight_register(dcg_ctx* c, int type, const void* host_rows, size_t 
     DeviceGuard g(c->device);
     std::lock_guard<std::mutex> lk(c->mu);
     if (c->by_host.count(host_rows)) {
-        *out = c->by_host[host_rows];
+        dcg_weight* old = c->by_host[host_rows];
+        if (old->type != type || old->n != n || old->k != k)
+            return ctx_fail(DCG_EINVAL, "host pointer already registered as a different weight (type/n/k); "
+                                        "release it first");
+        *out = old;
         return DCG_OK;
     }
     void* raw = nullptr;

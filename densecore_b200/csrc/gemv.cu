@@ -535,29 +535,17 @@ __global__ void __launch_bounds__(256, (UW <= 4 ? XR_CTAS : 2)) gemv_tma_xr_kern
 template <int TYPE, int M, int UW>
 static cudaError_t launch_xr(const PackedW& w, int64_t n, int64_t k, const ActQ& a, int m0, float* y,
                              int TR, int grid, cudaStream_t st) {
-    static bool attr_set = false;
     const size_t smem = 64 + ((2 * 8 * M * 4 + 127) & ~127) + (size_t)XR_STAGES * XR_TILE;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_tma_xr_kernel<TYPE, M, UW>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    cudaError_t e = DCG_SMEM_ATTR((gemv_tma_xr_kernel<TYPE, M, UW>), smem);
+    if (e != cudaSuccess) return e;
     return launch_pdl(gemv_tma_xr_kernel<TYPE, M, UW>, dim3((unsigned)grid), dim3(256), smem, st, w, n, k, a,
                       m0, y, TR);
 }
-
-static int g_num_sms = 0;
 
 // returns cudaErrorNotSupported when the shape needs more than 8 units per warp
 template <int TYPE, int M>
 static cudaError_t launch_gemv_xr_t(const PackedW& w, int64_t n, int64_t k, const ActQ& a, int m0,
                                     float* y, cudaStream_t st) {
-    if (!g_num_sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    }
     constexpr int PER = UnitInfo<TYPE>::BLOCKS;
     int TR = 1;
     while (TR * 2 * (int64_t)w.row_bytes <= XR_TILE && TR < 64) TR *= 2;
@@ -565,7 +553,7 @@ static cudaError_t launch_gemv_xr_t(const PackedW& w, int64_t n, int64_t k, cons
     const int upr = (w.nb + PER - 1) / PER;
     const int uw = (upr + wpr - 1) / wpr;
     const int64_t n_tiles = (n + TR - 1) / TR;
-    const int grid = (int)std::min<int64_t>(n_tiles, (int64_t)g_num_sms * XR_CTAS);
+    const int grid = (int)std::min<int64_t>(n_tiles, (int64_t)num_sms() * XR_CTAS);
     if (uw <= 1) return launch_xr<TYPE, M, 1>(w, n, k, a, m0, y, TR, grid, st);
     if (uw <= 2) return launch_xr<TYPE, M, 2>(w, n, k, a, m0, y, TR, grid, st);
     if (uw <= 4) return launch_xr<TYPE, M, 4>(w, n, k, a, m0, y, TR, grid, st);
@@ -578,22 +566,13 @@ static cudaError_t launch_gemv_xr_t(const PackedW& w, int64_t n, int64_t k, cons
 template <int TYPE, int M>
 static cudaError_t launch_gemv_tma_t(const PackedW& w, int64_t n, int64_t k, const ActQ& a, int m0,
                                      float* y, cudaStream_t st) {
-    static int num_sms = 0;
-    static bool attr_set = false;
     const size_t smem = 64 + ((2 * 8 * M * 4 + 127) & ~127) + (size_t)TMA_STAGES * TMA_TILE;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_tma_kernel<TYPE, M>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
-        attr_set = true;
-    }
+    cudaError_t e = DCG_SMEM_ATTR((gemv_tma_kernel<TYPE, M>), smem);
+    if (e != cudaSuccess) return e;
     int TR = 1;
     while (TR * 2 * (int64_t)w.row_bytes <= TMA_TILE && TR < 64) TR *= 2;
     const int64_t n_tiles = (n + TR - 1) / TR;
-    const int64_t grid = std::min<int64_t>(n_tiles, (int64_t)num_sms * 2);
+    const int64_t grid = std::min<int64_t>(n_tiles, (int64_t)num_sms() * 2);
     return launch_pdl(gemv_tma_kernel<TYPE, M>, dim3((unsigned)grid), dim3(256), smem, st, w, n, k, a, m0, y,
                       TR);
 }

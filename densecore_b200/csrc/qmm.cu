@@ -529,14 +529,9 @@ static cudaError_t make_wmap(CUtensorMap* map, const void* W, int64_t n, size_t 
 template <int NT>
 static cudaError_t launch_q4k_t(const uint8_t* W, int64_t n, int64_t k, const ActQ& a, int m, float* y,
                                 void* scratch, cudaStream_t st) {
-    static bool attr = false;
     const size_t smem = 128 + (size_t)M1_STAGES * QMM_W_BYTES;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(qmm_q4k_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
-        if (e != cudaSuccess) return e;
-        attr = true;
-    }
+    cudaError_t e = DCG_SMEM_ATTR((qmm_q4k_kernel<NT>), smem);
+    if (e != cudaSuccess) return e;
     const int nb = (int)(k / QK_K);
     const int rb = (int)((n + QMM_ROWS - 1) / QMM_ROWS);
     const int cb = (m + 8 * NT - 1) / (8 * NT);
@@ -546,7 +541,7 @@ static cudaError_t launch_q4k_t(const uint8_t* W, int64_t n, int64_t k, const Ac
     int* tickets = (int*)scratch;
     float* part = (float*)((uint8_t*)scratch + align256((size_t)rb * cb * 4));
     CUtensorMap wmap;
-    cudaError_t e = make_wmap(&wmap, W, n, (size_t)nb * Q4_K_BYTES);
+    e = make_wmap(&wmap, W, n, (size_t)nb * Q4_K_BYTES);
     if (e != cudaSuccess) return e;
     dim3 grid(cb, rb, S);
     return launch_pdl(qmm_q4k_kernel<NT>, grid, dim3(QMM_THREADS), smem, st, wmap, nb, n, a, k, m, y,
@@ -572,37 +567,20 @@ static cudaError_t launch_q4k_m1(const uint8_t* W, int64_t n, int64_t k, const A
                                  float* y, cudaStream_t st) {
     int rb, S, sps;
     if (!m1_plan(n, k, &rb, &S, &sps)) return cudaErrorNotSupported;
-    static bool attr = false;
     const size_t smem_max = M1_HDR + (size_t)M1_STAGES * M1_STAGE + (size_t)M1_MAX_SPS * M1_XQ;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(qmm_q4k_m1_kernel<QX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem_max);
-        if (e != cudaSuccess) return e;
-        attr = true;
-    }
+    cudaError_t e = DCG_SMEM_ATTR((qmm_q4k_m1_kernel<QX>), smem_max);
+    if (e != cudaSuccess) return e;
     const int nb = (int)(k / QK_K);
     CUtensorMap wmap;
-    cudaError_t e = make_wmap(&wmap, W, n, (size_t)nb * Q4_K_BYTES, 1);
+    e = make_wmap(&wmap, W, n, (size_t)nb * Q4_K_BYTES, 1);
     if (e != cudaSuccess) return e;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(rb, 1, S);
-    cfg.blockDim = dim3(M1_THREADS);
-    cfg.dynamicSmemBytes = M1_HDR + (size_t)M1_STAGES * M1_STAGE + (size_t)sps * M1_XQ;
-    cfg.stream = st;
     // A programmatic dependent whose own dependents are released only at its exit (after the
     // cluster reduction).  Released earlier, the next grid's clusters landed in a GPU still
     // holding this one and a config-2 step measured 28.3 us; in plain stream order 20.6 us; with
     // the release at exit 19.5 us (the next launch overlaps this one's drain).
-    cudaLaunchAttribute at[2];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 1;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = S;
-    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, qmm_q4k_m1_kernel<QX>, wmap, nb, n, a, x, y, sps);
+    const size_t smem = M1_HDR + (size_t)M1_STAGES * M1_STAGE + (size_t)sps * M1_XQ;
+    return launch_ex(qmm_q4k_m1_kernel<QX>, dim3(rb, 1, S), dim3(M1_THREADS), smem, st, (unsigned)S,
+                     wmap, nb, n, a, x, y, sps);
 }
 
 bool qmm_m1_fused_supports(int type, int64_t n, int64_t k, int64_t m) {

@@ -306,14 +306,19 @@ static cudaError_t launch_rd_t(const PackedW& w, int64_t n, int64_t k, const Act
     const int rb = (int)((n + RD_WARPS * 16 - 1) / (RD_WARPS * 16)), cb = (m + 8 * NT - 1) / (8 * NT);
     const int nsb = (int)(k / 256);
     auto kern = TYPE == DCG_TYPE_Q8_0 ? qmm_q8_0_rd_kernel<NT> : qmm_q6k_rd_kernel<NT>;
-    static int resident = 0;   // CTAs per SM the kernel's registers allow
-    if (!resident) {
-        int dev = 0, sms = 0, per_sm = 0;
+    static int per_sm[MAX_DEVICES] = {};   // CTAs per SM the kernel's registers allow, per device
+    static PerDevice pd;
+    cudaError_t e = per_device_once(pd, [&] {
+        int dev = 0, v = 0;
         cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, RD_WARPS * 32, 0);
-        resident = (per_sm > 0 ? per_sm : 1) * (sms > 0 ? sms : 148);
-    }
+        cudaError_t r = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kern, RD_WARPS * 32, 0);
+        per_sm[dev] = v > 0 ? v : 1;
+        return r;
+    });
+    if (e != cudaSuccess) return e;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int resident = per_sm[dev] * num_sms();
     int S = (resident + rb * cb - 1) / (rb * cb);
     S = S < 1 ? 1 : (S > 8 ? 8 : S);
     const int min_sps = TYPE == DCG_TYPE_Q8_0 ? 4 : 2;   // below this a split costs more than it gains
@@ -321,22 +326,8 @@ static cudaError_t launch_rd_t(const PackedW& w, int64_t n, int64_t k, const Act
     const int sps = (nsb + S - 1) / S;
     S = (nsb + sps - 1) / sps;
     const dim3 grid((unsigned)rb, (unsigned)cb, (unsigned)S);
-    if (S == 1) return launch_pdl(kern, grid, dim3(RD_WARPS * 32), 0, st, w, n, k, a, m, y, sps);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = dim3(RD_WARPS * 32);
-    cfg.dynamicSmemBytes = sizeof(float) * 8 * NT * RD_RS;
-    cfg.stream = st;
-    cudaLaunchAttribute at[2];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 1;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = S;
-    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, kern, w, n, k, a, m, y, sps);
+    const size_t smem = S == 1 ? 0 : sizeof(float) * 8 * NT * RD_RS;
+    return launch_ex(kern, grid, dim3(RD_WARPS * 32), smem, st, (unsigned)S, w, n, k, a, m, y, sps);
 }
 
 bool qmm_rd_supports(int type, int64_t k, int64_t m) {

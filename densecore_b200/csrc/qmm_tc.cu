@@ -408,14 +408,10 @@ template <int N>
 static cudaError_t launch_tc_t(const uint8_t* W, int64_t n, int64_t k, const ActQ& a, int m, float* y,
                                cudaStream_t st) {
     using C = TcCfg<N>;
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(qmm_q4k_tc_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-        if (e != cudaSuccess) return e;
-        attr = true;
-    }
+    cudaError_t e = DCG_SMEM_ATTR((qmm_q4k_tc_kernel<N>), C::SMEM);
+    if (e != cudaSuccess) return e;
     CUtensorMap wm, am;
-    cudaError_t e = tc_maps(&wm, &am, W, n, k, a.qs, m, N);
+    e = tc_maps(&wm, &am, W, n, k, a.qs, m, N);
     if (e != cudaSuccess) return e;
     const int nb = (int)(k / QK_K);
     const int rt = (int)((n + TC_ROWS - 1) / TC_ROWS), ct = (m + N - 1) / N;
@@ -425,21 +421,8 @@ static cudaError_t launch_tc_t(const uint8_t* W, int64_t n, int64_t k, const Act
     S = S > nb / 2 ? (nb / 2 > 0 ? nb / 2 : 1) : S;     // >= 2 super-blocks per split
     const int sps = (nb + S - 1) / S;
     S = (nb + sps - 1) / sps;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)rt, (unsigned)ct, (unsigned)S);
-    cfg.blockDim = dim3(TC_THREADS);
-    cfg.dynamicSmemBytes = C::SMEM;
-    cfg.stream = st;
-    cudaLaunchAttribute at[2];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 1;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = S;
-    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, qmm_q4k_tc_kernel<N>, wm, am, nb, n, a, m, y, sps);
+    return launch_ex(qmm_q4k_tc_kernel<N>, dim3((unsigned)rt, (unsigned)ct, (unsigned)S), dim3(TC_THREADS),
+                     (size_t)C::SMEM, st, (unsigned)S, wm, am, nb, n, a, m, y, sps);
 }
 
 bool qmm_tc_supports(int type, int64_t n, int64_t k, int64_t m) {

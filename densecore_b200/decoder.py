@@ -375,6 +375,20 @@ class Decoder:
         return w.to_ggml().cpu().numpy()[a:b], w.qtype, w.k
 
     def step(self):
+        """One decode token for every sequence (see _step).  With tensor parallelism the step's
+        kernels are launched in plain stream order (no programmatic dependent launch): NCCL's
+        collective kernels sit between them in the same stream, and a kernel that overlaps its
+        predecessor's drain is only safe next to this library's own kernels."""
+        if self.tp_size == 1:
+            return self._step()
+        lib = ops._lib.load()
+        prev = lib.dcg_set_programmatic_launch(0)
+        try:
+            return self._step()
+        finally:
+            lib.dcg_set_programmatic_launch(prev)
+
+    def _step(self):
         """One decode token for every sequence: reads self.tokens / self.ctx_lens, writes
         self.next_tokens and self.logits, appends K/V at position ctx_len-1.  Per layer: fused
         add+RMSNorm+quantize, stacked QKV matmul, fused QK-norm+RoPE+KV append, paged attention,

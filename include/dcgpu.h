@@ -42,6 +42,15 @@ extern "C" {
 #define DCG_KV_BLOCK_SIZE 16 /* tokens per KV block (core/include/kv_cache.h:17) */
 
 int dcg_version(void);
+
+/* Programmatic dependent launch (on by default): each kernel of this library may start its
+ * prologue while the previous kernel in the stream drains, and reads that kernel's outputs only
+ * after it has completed.  enable = 0 makes every later launch plainly stream-ordered, for streams
+ * (or captured graphs) where this library's kernels sit next to kernels of another library, such
+ * as NCCL collectives of a tensor-parallel step.  Process-wide; returns the previous setting.
+ * Launches already captured into a graph keep the setting they were captured with.  No counterpart
+ * in the reference (its operators run on CPU threads). */
+int dcg_set_programmatic_launch(int enable);
 const char* dcg_strerror(int code);
 const char* dcg_last_error(void);
 
@@ -114,9 +123,11 @@ int dcg_mul_mat_q(int type, const void* w, int64_t n, int64_t k, const void* act
  * allocation after start-up, a step that must not synchronize on cudaMalloc).  No counterpart in
  * the reference.  The quantized activation lives in a fixed 1 MiB device array owned by the
  * library (held on every GPU that loads it until exit); calls needing more than that
- * (dcg_act_size of the vec_dot_type) fail with DCG_EINVAL.  All calls share the array: calls that
- * overlap on the GPU race, so keep them on one stream.  The first call on each device resolves the
- * array's address; make it before any stream capture.  Allocates nothing. */
+ * (dcg_act_size of the vec_dot_type > 1 MiB: m*k above about 986,000 for Q8_0 weights or 871,000
+ * for Q4_K / Q6_K weights, e.g. m <= 68 / 60 at k = 14336) fail with DCG_EINVAL.  w must be
+ * 256-byte, x 16-byte and y 4-byte aligned (DCG_EINVAL otherwise).  All calls share the array:
+ * calls that overlap on the GPU race, so keep them on one stream.  The first call on each device
+ * resolves the array's address; make it before any stream capture.  Allocates nothing. */
 int dcg_mul_mat_noalloc(int type, const void* w, int64_t n, int64_t k, const float* x, int64_t m,
                         float* y, void* stream);
 
@@ -191,7 +202,10 @@ int dcg_ctx_create(int device, dcg_ctx** out);
 int dcg_ctx_destroy(dcg_ctx* ctx);
 
 /* Upload one ggml weight tensor (n rows of k, ggml row stride) and keep it resident.  The host
- * pointer is the key dcg_ctx_find_weight looks up (the weight_tensor->data of cb_gemv_custom). */
+ * pointer is the key dcg_ctx_find_weight looks up (the weight_tensor->data of cb_gemv_custom).
+ * Registering a pointer again returns the resident copy when type, n and k match, and DCG_EINVAL
+ * when they differ.  The device copy is not refreshed from host memory: release a weight before
+ * its host buffer is freed or rewritten. */
 int dcg_ctx_weight_register(dcg_ctx* ctx, int type, const void* host_rows, size_t row_stride,
                             int64_t n, int64_t k, dcg_weight** out);
 int dcg_ctx_weight_release(dcg_ctx* ctx, dcg_weight* w);

@@ -7,7 +7,7 @@ import torch
 
 from oracle import oracle as O
 from tests.gguf_fixture import write_tiny_gguf
-from tests.test_decoder_gpu import reference_step
+from chained_ref import reference_step
 
 pytestmark = pytest.mark.gpu
 

@@ -1,8 +1,17 @@
-"""Tensor-parallel decode on 2 GPUs (NCCL): every rank's logits from the TP=2 shards equal the TP=1
+"""Tensor-parallel decode on 2 GPUs (NCCL).  Every rank's logits from the TP=2 shards equal the TP=1
 model's (same seed: shards are bitwise slices of the unsplit quantized weights) within 2e-3, eager
-and through a captured CUDA graph.  Skipped with fewer than 2 GPUs."""
+and through a captured CUDA graph; at the Llama-3-70B widths (hidden 8192, 64/8 heads, FFN 28672,
+vocab 128256, Q4_K, two layers, batch 16: the tcgen05 matmul and 256-aligned K splits of the
+benchmarked configuration) rank 0 also checks the TP=2 logits against the chained CPU oracle.
+
+The ranks are child processes with a short process-group timeout: a rank that fails reports its
+traceback through the queue, and a collective left waiting by a failed peer ends with an error
+instead of holding the test.  Skipped with fewer than 2 GPUs."""
+import datetime
 import os
 import socket
+import sys
+import traceback
 
 import numpy as np
 import pytest
@@ -10,6 +19,8 @@ import torch
 import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
 
 
 def _free_port():
@@ -20,30 +31,48 @@ def _free_port():
     return port
 
 
-def _worker(rank, size, port, q):
-    import torch.distributed as dist
-
-    from densecore_b200.decoder import Decoder, DecoderConfig
+def _config(name):
+    from densecore_b200.decoder import LLAMA3_70B, DecoderConfig
     from densecore_b200.ggml_types import Q4_K
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    torch.cuda.set_device(rank)
-    dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=size, device_id=dev)
-    try:
+    if name == "tiny":
         cfg = DecoderConfig("tiny-llama", n_layer=2, hidden=512, n_head=8, n_head_kv=4, head_dim=128, ffn=1024,
                             vocab=1024, rope_theta=5e5, rms_eps=1e-5, wtype=Q4_K, qk_norm=False, tied=False,
                             out_type=Q4_K)
-        ref = Decoder(cfg, batch=3, max_ctx=64, seed=7, device=dev)
-        sh = Decoder(cfg, batch=3, max_ctx=64, seed=7, device=dev, tp_rank=rank, tp_size=size,
+        return cfg, 3, [9, 30, 47], 64
+    import dataclasses
+    cfg = dataclasses.replace(LLAMA3_70B, n_layer=2)
+    ctx = [int(c) for c in np.random.default_rng(5).integers(64, 300, 16)]
+    return cfg, 16, ctx, 320
+
+
+def _worker(rank, size, port, name, q):
+    import torch.distributed as dist
+    sys.path.insert(0, HERE)
+    try:
+        from densecore_b200.decoder import Decoder
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=size, device_id=dev,
+                                timeout=datetime.timedelta(seconds=120))
+        cfg, batch, ctx_l, max_ctx = _config(name)
+        ref = Decoder(cfg, batch=batch, max_ctx=max_ctx, seed=7, device=dev)
+        sh = Decoder(cfg, batch=batch, max_ctx=max_ctx, seed=7, device=dev, tp_rank=rank, tp_size=size,
                      tp_group=dist.group.WORLD)
         ref.fill_kv_random(3)
         h0, h1 = rank * sh.hkv, (rank + 1) * sh.hkv
         sh.k_arena.copy_(ref.k_arena[:, :, h0:h1])
         sh.v_arena.copy_(ref.v_arena[:, :, h0:h1])
         assert torch.equal(sh.block_tables, ref.block_tables)
-        toks = torch.tensor([5, 700, 1023], device=dev)
-        ctx = torch.tensor([9, 30, 47], dtype=torch.int32, device=dev)
+        toks = torch.from_numpy(np.random.default_rng(8).integers(0, cfg.vocab, batch)).to(dev)
+        ctx = torch.tensor(ctx_l, dtype=torch.int32, device=dev)
+        oracle_err = None
+        if name != "tiny" and rank == 0:
+            from chained_ref import reference_step
+            ref.tokens.copy_(toks)
+            ref.ctx_lens.copy_(ctx)
+            oracle_logits = reference_step(ref, toks.cpu().numpy(), ctx_l)
         results = []
         for mode in ("eager", "graph"):
             for d in (ref, sh):
@@ -58,23 +87,35 @@ def _worker(rank, size, port, q):
             a, b = ref.logits.double().cpu().numpy(), sh.logits.double().cpu().numpy()
             err = float((np.linalg.norm(a - b, axis=-1) / np.linalg.norm(a, axis=-1)).max())
             results.append((mode, err, bool(torch.equal(ref.next_tokens, sh.next_tokens))))
-        q.put((rank, results))
-    finally:
+            if mode == "graph" and name != "tiny" and rank == 0:
+                oe = np.linalg.norm(b - oracle_logits, axis=-1) / np.linalg.norm(oracle_logits, axis=-1)
+                oracle_err = (float(oe.max()), bool(np.array_equal(b.argmax(-1), oracle_logits.argmax(-1))))
+        q.put((rank, "ok", results, oracle_err))
         dist.destroy_process_group()
+    except BaseException:
+        q.put((rank, "error", traceback.format_exc(), None))
 
 
-def test_tp2_decode_matches_tp1():
+@pytest.mark.parametrize("name", ["tiny", "llama3_70b_2layers"])
+def test_tp2_decode_matches_tp1(name):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, name, q), daemon=True) for r in range(2)]
     for p in procs:
         p.start()
-    res = [q.get(timeout=300) for _ in range(2)]
-    for p in procs:
-        p.join(timeout=60)
-    for rank, results in res:
+    try:
+        res = [q.get(timeout=400) for _ in range(2)]
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    for rank, status, results, oracle_err in res:
+        assert status == "ok", f"rank {rank} failed:\n{results}"
         for mode, err, same in results:
             assert err < 2e-3 and same, (rank, mode, err, same)
+        if oracle_err is not None:
+            assert oracle_err[0] < 2e-3 and oracle_err[1], oracle_err

@@ -16,7 +16,9 @@ pytestmark = pytest.mark.gpu
 RTOL = 1e-5
 
 
-@pytest.mark.parametrize("wt,n,k,m", [(12, 4096, 14336, 1), (8, 1024, 4096, 8), (14, 512, 2560, 3)])
+# m = 20 runs three 8-row chunks; m = 60 at k = 14336 is the largest Q8_K activation that fits
+@pytest.mark.parametrize("wt,n,k,m", [(12, 4096, 14336, 1), (8, 1024, 4096, 8), (14, 512, 2560, 3),
+                                      (12, 768, 4096, 20), (12, 256, 14336, 60)])
 def test_noalloc_matches_mul_mat_twice(wt, n, k, m):
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
@@ -39,6 +41,23 @@ def test_noalloc_matches_mul_mat_twice(wt, n, k, m):
         err = (y.double() - y_ref.double()).abs()
         assert torch.isfinite(y).all()
         assert bool((err <= RTOL * bound).all()), float((err / bound).max())
+
+
+def test_noalloc_limit_is_exact():
+    """m = 60 fits the fixed buffer at k = 14336 for a Q4_K weight (Q8_K activation); m = 61 does not."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from densecore_b200 import _lib
+    L = _lib.load()
+    k, n = 14336, 256
+    assert L.dcg_act_size(15, 60, k) <= 1 << 20 < L.dcg_act_size(15, 61, k)
+    w = torch.zeros(L.dcg_packed_weight_size(12, n, k), dtype=torch.uint8, device="cuda")
+    x = torch.zeros(61, k, device="cuda")
+    y = torch.zeros(61, n, device="cuda")
+    assert L.dcg_mul_mat_noalloc(12, w.data_ptr(), n, k, x.data_ptr(), 60, y.data_ptr(), None) == 0
+    rc = L.dcg_mul_mat_noalloc(12, w.data_ptr(), n, k, x.data_ptr(), 61, y.data_ptr(), None)
+    assert rc == -1 and b"no-allocation buffer" in L.dcg_last_error()
+    torch.cuda.synchronize()
 
 
 def test_noalloc_rejects_oversize():
