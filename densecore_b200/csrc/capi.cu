@@ -49,13 +49,24 @@ void set_error(const std::string& m) { g_last_error = m; }
 // ------------------------------------------------------------------------------------------
 // internal: enqueue quantize + GEMV chunks (no checks beyond shapes; scratch already sized)
 // ------------------------------------------------------------------------------------------
-// scratch of dcg_mul_mat: [quantized activation | qmm tickets + split-K partials]
+// scratch of dcg_mul_mat: [quantized activation | matmul tickets + split-K partials]
+// (the matmul part: the tcgen05 kernel for m >= 2 Q4_K / Q6_K, the Q4_K M = 1 kernel's fallback)
+static bool use_tc(int type, int64_t n, int64_t k, int64_t m) { return dcg::qmm_tc_supports(type, n, k, m); }
 static size_t qmm_part(int type, int64_t n, int64_t k, int64_t m) {
+    if (use_tc(type, n, k, m)) return dcg::qmm_tc_scratch_bytes(type, n, k, m);
     return dcg::qmm_supports(type) ? dcg::qmm_scratch_bytes(type, n, k, m) : 0;
+}
+static int qmm_tickets(int type, int64_t n, int64_t k, int64_t m) {
+    if (use_tc(type, n, k, m)) return dcg::qmm_tc_ticket_count(type, n, k, m);
+    return dcg::qmm_supports(type) ? dcg::qmm_ticket_count(type, n, m) : 0;
 }
 
 static int enqueue_mul_mat_q(int type, const void* w, int64_t n, int64_t k, const void* act, int64_t m,
                              float* y, void* qscratch, cudaStream_t st) {
+    if (use_tc(type, n, k, m)) {
+        DCG_CUDA(dcg::launch_qmm_tc(type, w, n, k, act, m, y, qscratch, st), "qmm_tc");
+        return DCG_OK;
+    }
     if (dcg::qmm_supports(type)) {
         DCG_CUDA(dcg::launch_qmm(type, w, n, k, act, m, y, qscratch, st), "qmm");
         return DCG_OK;
@@ -78,7 +89,7 @@ static int enqueue_mul_mat(int type, const void* w, int64_t n, int64_t k, const 
         return DCG_OK;
     }
     void* qs = (uint8_t*)scratch + dcg::act_bytes(act_type_of(type), m, k);
-    const int nt = dcg::qmm_supports(type) ? dcg::qmm_ticket_count(type, n, m) : 0;
+    const int nt = qmm_tickets(type, n, k, m);
     DCG_CUDA(dcg::launch_quantize_act(act_type_of(type), x, scratch, m, k, true, st, (int*)qs, nt),
              "quantize");
     return enqueue_mul_mat_q(type, w, n, k, scratch, m, y, qs, st);

@@ -27,10 +27,13 @@ cudaError_t launch_qmm_m1_fused(const void* packed_w, int64_t n, int64_t k, cons
                                 cudaStream_t st);
 cudaError_t launch_qmm(int type, const void* packed_w, int64_t n, int64_t k, const void* act,
                        int64_t m, float* y, void* scratch, cudaStream_t st);
-// tcgen05 Q4_K GEMM (qmm_tc.cu)
+// tcgen05 Q4_K / Q6_K GEMM for m >= 2 (qmm_tc.cu); scratch: tickets (zero at launch, left zero)
+// followed by the stream-K partial tiles
 bool qmm_tc_supports(int type, int64_t n, int64_t k, int64_t m);
-cudaError_t launch_qmm_tc(const void* packed_w, int64_t n, int64_t k, const void* act, int64_t m, float* y,
-                          cudaStream_t st);
+size_t qmm_tc_scratch_bytes(int type, int64_t n, int64_t k, int64_t m);
+int qmm_tc_ticket_count(int type, int64_t n, int64_t k, int64_t m);
+cudaError_t launch_qmm_tc(int type, const void* packed_w, int64_t n, int64_t k, const void* act, int64_t m,
+                          float* y, void* scratch, cudaStream_t st);
 cudaError_t qmm_tc_device_error(int* out, bool clear);
 cudaError_t qmm_device_error(int* out, bool clear);
 bool qmm_supports(int type);

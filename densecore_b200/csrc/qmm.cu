@@ -604,9 +604,6 @@ cudaError_t launch_qmm(int type, const void* packed_w, int64_t n, int64_t k, con
         const cudaError_t e = launch_q4k_m1<false>(W, n, k, a, nullptr, y, st);
         if (e != cudaErrorNotSupported) return e;
     }
-    // M >= 16: the tcgen05 kernel (qmm_tc.cu); measured 1.0-2.2x faster than the mma.sync kernel
-    // below on the decode shapes at M = 16, 32, 64
-    if (m >= 16 && qmm_tc_supports(type, n, k, m)) return launch_qmm_tc(packed_w, n, k, act, m, y, st);
     if (m <= 8) return launch_q4k_t<1>(W, n, k, a, (int)m, y, scratch, st);
     if (m <= 16) return launch_q4k_t<2>(W, n, k, a, (int)m, y, scratch, st);
     return launch_q4k_t<4>(W, n, k, a, (int)m, y, scratch, st);

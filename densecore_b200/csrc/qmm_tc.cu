@@ -1,27 +1,37 @@
-// qmm_tc.cu -- Q4_K weight x Q8_K activation matmul on the 5th-generation tensor cores
-// (tcgen05.mma kind::i8, accumulators in tensor memory), for batched decode (column tiles of
-// N = 32 activation rows).  Replaces ggml_mul_mat's vec_dot_q4_K_q8_K row loop for these shapes
-// (core/src/inference.cpp:1063, :1794-1797; the dot product of simd_ops.cpp:82-93).
+// qmm_tc.cu -- Q4_K / Q6_K weight x Q8_K activation matmul on the 5th-generation tensor cores
+// (tcgen05.mma kind::i8, int32 accumulators in tensor memory) for every M >= 2: batched decode and
+// prefill.  Replaces ggml_mul_mat's vec_dot_q4_K_q8_K / vec_dot_q6_K_q8_K row loops for these
+// shapes (core/src/inference.cpp:1063, :1794-1797, :1817; the dot products of simd_ops.cpp:82-93).
 //
-// One CTA owns 128 weight rows (the MMA's M) x N activation rows (the MMA's N) over a range of K
-// super-blocks (split-K across a cluster when the tiles alone cannot fill the GPU).  Per
-// super-block (K = 256):
-//   producer warp   TMA: the 128 x 144 B Q4_K weight tile, and the N x 256 B Q8_K activation tile
-//                   as one 3-D box (16 B x N rows x 16 K chunks: the K-major no-swizzle
-//                   core-matrix layout); its lanes stage the columns' dx and pair sums
-//   prep warpgroup  (warps 2-5) thread r expands weight row r into two int8 planes, H = q * sh and
-//                   L = q * sl with the 6-bit sub-block scale sc = 8 * sh + sl (q <= 15, sh, sl
-//                   <= 7: every product fits int8, four at a time in one 32-bit multiply), written
-//                   in the core-matrix layout the MMA reads
-//   MMA thread      16 x tcgen05.mma.kind::i8 (8 k-steps of 32 for each plane) into two int32
-//                   accumulators C_H, C_L in tensor memory; double-buffered across super-blocks
-//   epilogue        (warps 6-9, concurrent with the prep of the next super-block) thread r reads row r of C_H, C_L (tcgen05.ld) and the
-//                   columns' dx and pair sums (staged in shared memory by the producer warp), forms the
-//                   exact integer sum isum = 8 C_H + C_L, the min term sum_j m_j * bsum32_j (dp2a),
-//                   and accumulates y += dx * (d * isum - dmin * msum) in fp32, as ggml does
-// Every wait is bounded (device error flag), and tensor memory is always freed before exit.
+// Work decomposition (stream-K).  A unit is one 128-row weight tile x one N-column activation tile
+// x one K super-block (256).  The units are ordered tile by tile (column tiles of a row tile next
+// to each other, so their shared weights come from L2) and split into G contiguous ranges, one per
+// CTA (G <= number of SMs, one CTA per SM): every SM streams the same number of weight bytes,
+// whatever the tile count, and its pipeline never drains between tiles.  A tile whose units span
+// several CTAs is finished by the last of them to arrive (atomic ticket): each writes its partial
+// tile to scratch, and the last sums all partials in CTA order, so results are deterministic.
+//
+// Per unit (super-block), warp-specialised:
+//   warp 0      TMA: the 128-row weight tile (Q4_K 144 B, Q6_K 208 B per row) into a WS-deep ring
+//   warp 1      TMA: the N x 256 B Q8_K activation tile as one 3-D box in the K-major no-swizzle
+//               core-matrix layout the MMA reads, into an AS-deep ring; its lanes stage the
+//               columns' scales dx (and the Q4_K min-term pair sums) in a metadata ring
+//   warp 2      one thread issues per K half 4 k-steps x 2 planes of M128 x N x K32 MMAs into
+//               C_H, C_L (double-buffered across units) and releases stages with tcgen05.commit
+//   warps 4-11  thread (row r, half h) first expands K half h of weight row r of unit i into two
+//               int8 planes H, L with q * scale = SHIFT * H + L exactly, in the core-matrix layout:
+//                 Q4_K  sc = 8 sh + sl (sh, sl <= 7): H = q sh, L = q sl (q <= 15), SHIFT = 8
+//                 Q6_K  p = (u - 32) sc (u the unsigned 6-bit quant, sc the signed 8-bit sub-block
+//                       scale): H = p >> 7, L = p & 127, SHIFT = 128 (the -32 offset is folded in)
+//               then, while unit i's MMAs run, drains unit i-1's accumulators for half h of the
+//               columns (tcgen05.ld), forms isum = SHIFT C_H + C_L and accumulates
+//                 Q4_K  y += dx (d isum - dmin sum_j m_j bsum32_j)      (ggml's order)
+//                 Q6_K  y += dx d isum
+// Every wait is bounded (device error flag); tensor memory is always freed before exit.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+
+#include <type_traits>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -40,26 +50,45 @@ cudaError_t qmm_tc_device_error(int* out, bool clear) {
     return e;
 }
 
-constexpr int TC_ROWS = 128;                     // weight rows per CTA (MMA M)
-constexpr int TC_THREADS = 576;                  // warp 0 producer, 1 MMA, 2-9 prep, 10-17 epilogue
-constexpr int TC_EPI0 = 10;                      // first epilogue warp
-constexpr int TC_WTILE = TC_ROWS * Q4_K_BYTES;   // 18432 B raw weight tile per super-block
-constexpr int TC_PLANE = TC_ROWS * QK_K;         // 32 KB: one int8 plane of a super-block
-constexpr int TC_PLANE_SBO = 16 * 128;           // plane: 8-row groups 2 KB apart, 16-B K chunks 128 B
+constexpr int TC_ROWS = 128;      // weight rows per tile (the MMA's M)
+constexpr int TC_THREADS = 384;   // 12 warps: 0 weight TMA, 1 activation TMA, 2 MMA, 3 spare, 4-11 prep + epilogue
+constexpr int TC_WORK0 = 4;
+constexpr int TC_HPLANE = TC_ROWS * 128;   // one int8 plane of a K half: 16 KB
+constexpr int TC_HSBO = 8 * 128;           // plane: 8-row groups 1 KB apart, 16-B K chunks 128 B apart
+constexpr int TC_MS = 4;                   // metadata slots (dx, pair sums, row scales)
+constexpr int TC_SMEM_MAX = 232448;        // 227 KB opt-in
 
-template <int N>
+template <int TYPE>
+struct TcW;
+template <>
+struct TcW<DCG_TYPE_Q4_K> {
+    static constexpr int ROWB = Q4_K_BYTES;     // bytes per row per super-block in the device layout
+    static constexpr int SHIFT = 8;
+};
+template <>
+struct TcW<DCG_TYPE_Q6_K> {
+    static constexpr int ROWB = Q6_K_PAYLOAD;   // ql | qh | scales (fp16 d is a separate array)
+    static constexpr int SHIFT = 128;
+};
+
+template <int TYPE, int N>
 struct TcCfg {
-    static constexpr int STAGES = N <= 32 ? 3 : 2;
-    static constexpr int ATILE = N * QK_K;                       // activation tile per super-block
-    static constexpr int OFF_RAW = 1024;                         // after barriers
-    static constexpr int OFF_ACT = OFF_RAW + STAGES * TC_WTILE;
-    static constexpr int OFF_PL = OFF_ACT + STAGES * ATILE;      // [2 buffers][H, L]
-    static constexpr int MSLOTS = STAGES + 2;                    // metadata lives until the epilogue
-    static constexpr int META = N * 4 + N * 16;                  // per column: dx, 8 pair sums
-    static constexpr int OFF_META = OFF_PL + 4 * TC_PLANE;
-    static constexpr int OFF_ROWP = OFF_META + MSLOTS * META;    // [slot][128 rows] d | dmin, mins
-    static constexpr int SMEM = OFF_ROWP + MSLOTS * TC_ROWS * 16;
-    static constexpr int TMEM_COLS = 4 * N;                      // [2 buffers][C_H, C_L] x N
+    static constexpr int WT = TC_ROWS * TcW<TYPE>::ROWB;          // weight tile per unit
+    static constexpr int AT = N * QK_K;                            // activation tile per unit
+    static constexpr int AS = N >= 128 ? 2 : (N >= 64 ? 3 : 4);    // activation ring
+    static constexpr int META = N * 4 + N * 16;                    // per column: dx, 8 pair sums
+    static constexpr int OFF_BAR = 0;                              // barriers, flag, TMEM slot
+    static constexpr int OFF_PL = 1024;                            // planes [K half][H, L]
+    static constexpr int OFF_ACT = OFF_PL + 4 * TC_HPLANE;
+    static constexpr int OFF_META = OFF_ACT + AS * AT;
+    static constexpr int OFF_ROWP = OFF_META + TC_MS * META;       // [slot][128 rows] 16 B
+    static constexpr int OFF_RAW = OFF_ROWP + TC_MS * TC_ROWS * 16;
+    static constexpr int WS_FIT = (TC_SMEM_MAX - OFF_RAW) / WT;
+    static constexpr int WS = WS_FIT > 8 ? 8 : WS_FIT;             // weight ring
+    static constexpr int SMEM = OFF_RAW + WS * WT;
+    static constexpr int TMEM_COLS = 4 * N;                        // [2 buffers][C_H, C_L] x N
+    static_assert(WS >= 2, "weight ring too shallow");
+    static_assert(SMEM <= TC_SMEM_MAX, "shared memory");
 };
 
 // ---- tcgen05 plumbing ----
@@ -102,55 +131,146 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
         : "r"(taddr)
         : "memory");
 }
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr)
+                 : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// exact int -> float for |v| < 2^22 with two full-rate ops (the float magic-number method: v added
+// to the mantissa of 1.5 * 2^23, whose unit in the last place is 1, then the bias subtracted); the
+// conversion instruction runs at a fraction of that rate
+__device__ __forceinline__ float i2f_exact22(int v) { return __int_as_float(0x4B400000 + v) - 12582912.0f; }
+
+__device__ __forceinline__ void work_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// stream-K ranges: CTA c owns units [begin(c), begin(c+1)); owner(u) is the CTA whose range holds u
+__host__ __device__ __forceinline__ int64_t sk_begin(int64_t c, int64_t T, int64_t G) { return c * T / G; }
+__device__ __forceinline__ int64_t sk_owner(int64_t u, int64_t T, int64_t G) { return ((u + 1) * G - 1) / T; }
+
+// ---- prep: one weight row of one super-block (in shared memory) -> the two planes of K half h ----
+// Q4_K K half h (sub-blocks 4h .. 4h+3): chunk kc (16 elements) of sub-block kc/2
+template <int TYPE, typename std::enable_if<TYPE == DCG_TYPE_Q4_K, int>::type = 0>
+__device__ __forceinline__ void prep_half(const uint8_t* row, int h, uint8_t* pH, uint8_t* pL) {
+    const Q4kScales sc = q4k_unpack(*(const uint4*)row);
+    uint32_t qs[16];   // nibble bytes 64h .. 64h+63
+#pragma unroll
+    for (int q = 0; q < 4; q++) *(uint4*)&qs[4 * q] = ((const uint4*)(row + 16 + 64 * h))[q];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int sbk = 4 * h + (j >> 1);                       // sub-block
+        const uint32_t scs = ((sbk < 4 ? sc.sc03 : sc.sc47) >> (8 * (sbk & 3))) & 0x3Fu;
+        const uint32_t sh = scs >> 3, sl = scs & 7u;
+        const int g = (j >> 2);                                 // 32-byte group within the half
+        uint4 vh, vl;
+        uint32_t* ph = (uint32_t*)&vh;
+        uint32_t* pl = (uint32_t*)&vl;
+#pragma unroll
+        for (int w = 0; w < 4; w++) {
+            const uint32_t word = qs[g * 8 + (j & 1) * 4 + w];
+            const uint32_t nib = (sbk & 1) ? (word >> 4) & 0x0F0F0F0Fu : word & 0x0F0F0F0Fu;
+            ph[w] = nib * sh;
+            pl[w] = nib * sl;
+        }
+        *(uint4*)(pH + j * 128) = vh;
+        *(uint4*)(pL + j * 128) = vl;
+    }
+}
+
+// Q6_K K half h: chunk j (elements 128h + 16j .. +15) = sub-block 8h + j, group grp = j/2,
+// l-range 16 (j & 1) .. +15; u = low nibble of ql[64h + 32 (grp & 1) + l] (shifted by 4 (grp >> 1))
+// | 2 bits of qh[32h + l] (shifted by 2 grp) << 4.  p = (u - 32) sc is formed two elements per
+// 32-bit word (16-bit lanes, biased by 32768 so no lane borrows): V = (u0 | u1 << 16) sc + K with
+// K = (32768 - 32 sc) in both lanes; then L = V & 127 and H = (V >> 7) & 255 per lane.
+template <int TYPE, typename std::enable_if<TYPE == DCG_TYPE_Q6_K, int>::type = 0>
+__device__ __forceinline__ void prep_half(const uint8_t* row, int h, uint8_t* pH, uint8_t* pL) {
+    const uint32_t* w32 = (const uint32_t*)row;
+    const uint2 scv = *(const uint2*)(row + 192 + 8 * h);
+    const uint32_t scw[2] = {scv.x, scv.y};   // scales 8h .. 8h+7
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int grp = j >> 1, l0 = 16 * (j & 1);
+        const int sc = (int)(int8_t)((scw[j >> 2] >> (8 * (j & 3))) & 0xFF);
+        const uint32_t kk = (uint32_t)(32768 - 32 * sc) * 0x10001u;
+        uint4 vh, vl;
+        uint32_t* ph = (uint32_t*)&vh;
+        uint32_t* pl = (uint32_t*)&vl;
+#pragma unroll
+        for (int w = 0; w < 4; w++) {
+            const uint32_t ql = w32[(64 * h + 32 * (grp & 1) + l0) / 4 + w];
+            const uint32_t qh = w32[(128 + 32 * h + l0) / 4 + w];
+            const uint32_t u = ((ql >> (4 * (grp >> 1))) & 0x0F0F0F0Fu) | (((qh >> (2 * grp)) & 0x03030303u) << 4);
+            const uint32_t v01 = __byte_perm(u, 0u, 0x4140u) * (uint32_t)sc + kk;
+            const uint32_t v23 = __byte_perm(u, 0u, 0x4342u) * (uint32_t)sc + kk;
+            pl[w] = __byte_perm(v01 & 0x007F007Fu, v23 & 0x007F007Fu, 0x6420u);
+            ph[w] = __byte_perm((v01 >> 7) & 0x00FF00FFu, (v23 >> 7) & 0x00FF00FFu, 0x6420u);
+        }
+        *(uint4*)(pH + j * 128) = vh;
+        *(uint4*)(pL + j * 128) = vl;
+    }
+}
+
 // ---- the kernel ----
-template <int N>
+template <int TYPE, int N>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    qmm_q4k_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
-                      int nb, int64_t n, ActQ a, int m, float* __restrict__ y, int sps) {
-    using C = TcCfg<N>;
-    constexpr int R = C::STAGES;
+    qmm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
+                  const __half* __restrict__ wd, int nb, int64_t n, ActQ a, int m, float* __restrict__ y,
+                  int ct_tiles, int64_t T, float* __restrict__ part, int* __restrict__ tickets) {
+    using C = TcCfg<TYPE, N>;
+    constexpr int WS = C::WS, AS = C::AS, MS = TC_MS;
+    constexpr bool Q4 = TYPE == DCG_TYPE_Q4_K;
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint64_t* full = (uint64_t*)smem;          // [R] weight + activation tiles landed (tx)
-    uint64_t* raw_empty = full + R;            // [R] 128 prep threads read the weight tile
-    uint64_t* act_empty = raw_empty + R;       // [R] MMAs that read the activation tile done
-    uint64_t* pl_full = act_empty + R;         // [2] planes written (128 arrivals)
-    uint64_t* pl_empty = pl_full + 2;          // [2] MMAs that read the planes done
+    uint64_t* w_full = (uint64_t*)smem;        // [WS] weight tile landed (tx)
+    uint64_t* w_empty = w_full + WS;           // [WS] 8 prep warps read it
+    uint64_t* a_full = w_empty + WS;           // [AS] activation tile landed (tx)
+    uint64_t* a_empty = a_full + AS;           // [AS] MMAs that read it done
+    uint64_t* pl_full = a_empty + AS;          // [2] K-half planes written (128 prep threads)
+    uint64_t* pl_empty = pl_full + 2;          // [2] MMAs that read them done
     uint64_t* acc_full = pl_empty + 2;         // [2] accumulators complete
-    uint64_t* acc_empty = acc_full + 2;        // [2] 128 epilogue threads read them
-    uint64_t* meta_empty = acc_empty + 2;      // [MSLOTS] epilogue done with a metadata slot
-    uint64_t* mma_done = meta_empty + C::MSLOTS; // [1] every MMA of the CTA retired
+    uint64_t* acc_empty = acc_full + 2;        // [2] 8 epilogue warps read them
+    uint64_t* meta_full = acc_empty + 2;       // [MS] column metadata staged (32 producer lanes)
+    uint64_t* row_full = meta_full + MS;       // [MS] row scales staged (128 prep threads)
+    uint64_t* meta_empty = row_full + MS;      // [MS] 8 epilogue warps done with the slot
+    uint64_t* mma_done = meta_empty + MS;      // [1] every MMA retired
     uint32_t* tmem_slot = (uint32_t*)(mma_done + 1);
-    uint8_t* raw = smem + C::OFF_RAW;
-    uint8_t* act = smem + C::OFF_ACT;
+    int* last_flag = (int*)(tmem_slot + 1);
     uint8_t* planes = smem + C::OFF_PL;
-    uint8_t* meta = smem + C::OFF_META;        // [MSLOTS][dx: N floats | pair sums: N x 8 int16]
+    uint8_t* act = smem + C::OFF_ACT;
+    uint8_t* meta = smem + C::OFF_META;        // [MS][dx: N floats | pair sums: N x 8 int16]
     uint4* rowp = (uint4*)(smem + C::OFF_ROWP);
+    uint8_t* raw = smem + C::OFF_RAW;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t r0 = (int64_t)blockIdx.x * TC_ROWS;
-    const int c0 = blockIdx.y * N;
-    const int sb0 = blockIdx.z * sps, sb1 = min(nb, sb0 + sps);
-    const int nsb = sb1 - sb0;
+    const int64_t G = gridDim.x, bid = blockIdx.x;
+    const int64_t u0 = sk_begin(bid, T, G), u1 = sk_begin(bid + 1, T, G);
+    const int nu = (int)(u1 - u0);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < R; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&raw_empty[s], 256);
-            mbar_init(&act_empty[s], 1);
+        for (int s = 0; s < WS; s++) {
+            mbar_init(&w_full[s], 1);
+            mbar_init(&w_empty[s], 8);
+        }
+        for (int s = 0; s < AS; s++) {
+            mbar_init(&a_full[s], 1);
+            mbar_init(&a_empty[s], 1);
         }
         for (int b = 0; b < 2; b++) {
-            mbar_init(&pl_full[b], 256);
+            mbar_init(&pl_full[b], 128);
             mbar_init(&pl_empty[b], 1);
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 256);
+            mbar_init(&acc_empty[b], 8);
         }
-        for (int s = 0; s < C::MSLOTS; s++) mbar_init(&meta_empty[s], 256);
+        for (int s = 0; s < MS; s++) {
+            mbar_init(&meta_full[s], 32);
+            mbar_init(&row_full[s], 128);
+            mbar_init(&meta_empty[s], 8);
+        }
         mbar_init(mma_done, 1);
         fence_mbar_init();
     }
-    if (warp == 1) {
+    if (warp == 2) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"((uint32_t)C::TMEM_COLS)
                      : "memory");
@@ -160,212 +280,260 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    pdl_wait();
 
     bool ok = true;
     if (warp == 0) {
-        // ---------------- producer ----------------
-        // lane 0 issues the tile copies; lane c stages column c's dx and pair sums (strided in
-        // global memory) into the stage's metadata before lane 0 arrives on the full barrier
-        // column c's dx and pair sums for super-block s, loaded one super-block ahead
-        auto load_meta = [&](int s, float (&dx)[(N + 31) / 32], uint4 (&bs)[(N + 31) / 32]) {
-#pragma unroll
-            for (int i = 0; i < (N + 31) / 32; i++) {
-                const int c = lane + 32 * i, col = c0 + c;
-                dx[i] = 0.0f;
-                bs[i] = make_uint4(0, 0, 0, 0);
-                if (c < N && col < m && s < nsb) {
-                    dx[i] = __ldg(&((const float*)a.d)[(size_t)col * nb + sb0 + s]);
-                    bs[i] = __ldg((const uint4*)(a.bs32 + ((size_t)col * nb + sb0 + s) * 8));
-                }
+        // ---------------- weight producer (constant data: may run ahead of pdl_wait) ----------------
+        if (lane == 0) {
+            for (int i = 0; i < nu && ok; i++) {
+                const int64_t u = u0 + i, tile = u / nb;
+                const int s = (int)(u % nb), st = i % WS;
+                const int rt = (int)(tile / ct_tiles);
+                if (i >= WS) ok = mbar_wait(&w_empty[st], (uint32_t)(((i / WS) - 1) & 1), &g_tc_error);
+                if (!ok) break;
+                mbar_arrive_expect_tx(&w_full[st], (uint32_t)C::WT);
+                tma_load_2d(raw + (size_t)st * C::WT, &wmap, s * (TcW<TYPE>::ROWB / 4), rt * TC_ROWS, &w_full[st]);
             }
-        };
-        float ndx[(N + 31) / 32];
-        uint4 nbs[(N + 31) / 32];
-        load_meta(0, ndx, nbs);
-        for (int s = 0; s < nsb && ok; s++) {
-            const int st = s % R, ms = s % C::MSLOTS;
-            float cdx[(N + 31) / 32];
-            uint4 cbs[(N + 31) / 32];
-#pragma unroll
-            for (int i = 0; i < (N + 31) / 32; i++) {
-                cdx[i] = ndx[i];
-                cbs[i] = nbs[i];
-            }
-            load_meta(s + 1, ndx, nbs);
-            if (s >= R) {
-                const uint32_t par = (uint32_t)(((s / R) - 1) & 1);
-                ok = mbar_wait(&raw_empty[st], par, &g_tc_error) && mbar_wait(&act_empty[st], par, &g_tc_error);
-            }
-            if (ok && s >= C::MSLOTS)
-                ok = mbar_wait(&meta_empty[ms], (uint32_t)(((s / C::MSLOTS) - 1) & 1), &g_tc_error);
+        }
+        pdl_wait();
+    } else if (warp == 1) {
+        // ---------------- activation producer + column metadata ----------------
+        pdl_wait();
+        for (int i = 0; i < nu && ok; i++) {
+            const int64_t u = u0 + i, tile = u / nb;
+            const int s = (int)(u % nb), st = i % AS, ms = i % MS;
+            const int c0 = (int)(tile % ct_tiles) * N;
+            if (i >= AS) ok = mbar_wait(&a_empty[st], (uint32_t)(((i / AS) - 1) & 1), &g_tc_error);
+            if (ok && i >= MS) ok = mbar_wait(&meta_empty[ms], (uint32_t)(((i / MS) - 1) & 1), &g_tc_error);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             float* mdx = (float*)(meta + (size_t)ms * C::META);
             uint4* mbs = (uint4*)(mdx + N);
-#pragma unroll
-            for (int i = 0; i < (N + 31) / 32; i++) {
-                const int c = lane + 32 * i;
-                if (c < N) {
-                    mdx[c] = cdx[i];
-                    mbs[c] = cbs[i];
+            for (int c = lane; c < N; c += 32) {
+                const int col = c0 + c;
+                float dx = 0.0f;
+                uint4 bs = make_uint4(0, 0, 0, 0);
+                if (col < m) {
+                    dx = __ldg(&((const float*)a.d)[(size_t)col * nb + s]);
+                    if (Q4) bs = __ldg((const uint4*)(a.bs32 + ((size_t)col * nb + s) * 8));
                 }
+                mdx[c] = dx;
+                if (Q4) mbs[c] = bs;
             }
-            __syncwarp();
+            mbar_arrive(&meta_full[ms]);
             if (lane == 0) {
-                mbar_arrive_expect_tx(&full[st], (uint32_t)(TC_WTILE + C::ATILE));
-                tma_load_2d(raw + (size_t)st * TC_WTILE, &wmap, (sb0 + s) * (Q4_K_BYTES / 4), (int)r0, &full[st]);
-                // the activation tile in one box: [16-B K chunk][row][16 B], the core-matrix layout
-                tma_load_3d(act + (size_t)st * C::ATILE, &amap, 0, c0, (sb0 + s) * 16, &full[st]);
+                mbar_arrive_expect_tx(&a_full[st], (uint32_t)C::AT);
+                tma_load_3d(act + (size_t)st * C::AT, &amap, 0, c0, s * 16, &a_full[st]);
             }
         }
-    } else if (warp == 1) {
+    } else if (warp == 2) {
         // ---------------- MMA issue ----------------
+        pdl_wait();
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_i8<N>();
-            for (int s = 0; s < nsb && ok; s++) {
-                const int st = s % R, b = s & 1;
-                ok = mbar_wait(&full[st], (uint32_t)((s / R) & 1), &g_tc_error) &&
-                     mbar_wait(&pl_full[b], (uint32_t)((s >> 1) & 1), &g_tc_error) &&
-                     (s < 2 || mbar_wait(&acc_empty[b], (uint32_t)(((s >> 1) - 1) & 1), &g_tc_error));
-                if (!ok) break;
-                tc_fence_after();
-                const uint32_t pH = smem_u32(planes + (size_t)(2 * b) * TC_PLANE);
-                const uint32_t pL = pH + TC_PLANE;
-                const uint32_t pa = smem_u32(act + (size_t)st * C::ATILE);
+            for (int i = 0; i < nu && ok; i++) {
+                const int st = i % AS, b = i & 1;
+                ok = mbar_wait(&a_full[st], (uint32_t)((i / AS) & 1), &g_tc_error) &&
+                     (i < 2 || mbar_wait(&acc_empty[b], (uint32_t)(((i >> 1) - 1) & 1), &g_tc_error));
+                const uint32_t pa = smem_u32(act + (size_t)st * C::AT);
                 const uint32_t dH = tmem + (uint32_t)(b * 2 * N), dL = dH + N;
 #pragma unroll
-                for (int j = 0; j < 8; j++) {   // k-step j: K chunks 2j, 2j+1
-                    const uint64_t bd = umma_desc(pa + j * 2 * N * 16, N * 16, 128);
-                    mma_i8(dH, umma_desc(pH + j * 256, 128, TC_PLANE_SBO), bd, idesc, j > 0);
-                    mma_i8(dL, umma_desc(pL + j * 256, 128, TC_PLANE_SBO), bd, idesc, j > 0);
+                for (int h = 0; h < 2; h++) {
+                    ok = ok && mbar_wait(&pl_full[h], (uint32_t)(i & 1), &g_tc_error);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t pH = smem_u32(planes + (size_t)(2 * h) * TC_HPLANE), pL = pH + TC_HPLANE;
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {   // k-step: K chunks 8h + 2j, 8h + 2j + 1
+                        const uint64_t bd = umma_desc(pa + (h * 4 + j) * 2 * N * 16, N * 16, 128);
+                        const uint32_t accum = (h | j) ? 1u : 0u;
+                        mma_i8(dH, umma_desc(pH + j * 256, 128, TC_HSBO), bd, idesc, accum);
+                        mma_i8(dL, umma_desc(pL + j * 256, 128, TC_HSBO), bd, idesc, accum);
+                    }
+                    tc_commit(&pl_empty[h]);
                 }
-                tc_commit(&pl_empty[b]);
-                tc_commit(&act_empty[st]);
+                if (!ok) break;
+                tc_commit(&a_empty[st]);
                 tc_commit(&acc_full[b]);
             }
             tc_commit(mma_done);
             mbar_wait(mma_done, 0, &g_tc_error);
         }
-    }
-
-    // ---- prep (warps 2-9) and epilogue (warps 10-17): thread <-> weight row <-> TMEM lane; two
-    // warps per row quarter, splitting the K chunks (prep) or the columns (epilogue) ----
-    constexpr int NH = N / 2;                       // columns per epilogue thread
-    float yacc[NH];
-#pragma unroll
-    for (int c = 0; c < NH; c++) yacc[c] = 0.0f;
-    const int quarter = warp & 3;                   // TMEM lanes 32*quarter .. +31 for this warp
-    const int row = quarter * 32 + lane;
-    const int half = warp < TC_EPI0 ? (warp - 2) >> 2 : (warp - TC_EPI0) >> 2;
-    if (warp >= 2 && warp < TC_EPI0) {
-        for (int s = 0; s < nsb && ok; s++) {
-            const int st = s % R, b = s & 1;
-            ok = mbar_wait(&full[st], (uint32_t)((s / R) & 1), &g_tc_error) &&
-                 (s < 2 || mbar_wait(&pl_empty[b], (uint32_t)(((s >> 1) - 1) & 1), &g_tc_error));
-            ok = __all_sync(0xffffffffu, ok);
-            if (!ok) break;
-            const uint4* src = (const uint4*)(raw + (size_t)st * TC_WTILE + (size_t)row * Q4_K_BYTES);
-            uint4 q[5];   // header + the 64 nibble bytes of this half (sub-blocks 4*half .. +3)
-            q[0] = src[0];
-#pragma unroll
-            for (int i = 1; i < 5; i++) q[i] = src[half * 4 + i];
-            mbar_arrive(&raw_empty[st]);
-            const Q4kScales sc = q4k_unpack(q[0]);
-            // the row's d | dmin, packed mins, for the epilogue of this super-block
-            if (half == 0) rowp[(s % C::MSLOTS) * TC_ROWS + row] = make_uint4(q[0].x, sc.mn03, sc.mn47, 0u);
-            uint8_t* pH = planes + (size_t)(2 * b) * TC_PLANE + (size_t)(row >> 3) * TC_PLANE_SBO + (row & 7) * 16;
-            uint8_t* pL = pH + TC_PLANE;
-            const uint32_t* qs = (const uint32_t*)&q[1];   // nibble bytes 64*half .. +63
-#pragma unroll
-            for (int kh = 0; kh < 8; kh++) {    // elements 16kc .. 16kc+15: sub-block kc/2
-                const int kc = half * 8 + kh;
-                const int sbk = kc >> 1, g = (kh >> 1) >> 1;
-                const uint32_t scs = ((sbk < 4 ? sc.sc03 : sc.sc47) >> (8 * (sbk & 3))) & 0x3Fu;
-                const uint32_t sh = scs >> 3, sl = scs & 7u;
-                uint4 vh, vl;
-                uint32_t* ph = (uint32_t*)&vh;
-                uint32_t* pl = (uint32_t*)&vl;
-#pragma unroll
-                for (int w = 0; w < 4; w++) {
-                    const uint32_t word = qs[g * 8 + (kc & 1) * 4 + w];
-                    const uint32_t nib = (sbk & 1) ? (word >> 4) & 0x0F0F0F0Fu : word & 0x0F0F0F0Fu;
-                    ph[w] = nib * sh;
-                    pl[w] = nib * sl;
-                }
-                *(uint4*)(pH + kc * 128) = vh;
-                *(uint4*)(pL + kc * 128) = vl;
-            }
-            fence_proxy_async_smem();
-            mbar_arrive(&pl_full[b]);
-        }
-    } else if (warp >= TC_EPI0) {
-        for (int e = 0; e < nsb && ok; e++) {
-            const int b = e & 1, ms = e % C::MSLOTS;
-            // warp-uniform outcome: the TMEM loads below are .sync.aligned
-            ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[b], (uint32_t)((e >> 1) & 1), &g_tc_error));
-            if (!ok) break;
-            tc_fence_after();
-            const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 2 * N + half * NH);
-            const uint4 rp = rowp[ms * TC_ROWS + row];
-            const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&rp.x));
-            // mins as (m0, m1), (m2, m3), ... pairs in the low bytes for dp2a
-            const int mp0 = (int)(rp.y & 0xFFu) | (int)((rp.y >> 8) & 0xFFu) << 8;
-            const int mp1 = (int)((rp.y >> 16) & 0xFFu) | (int)(rp.y >> 24) << 8;
-            const int mp2 = (int)(rp.z & 0xFFu) | (int)((rp.z >> 8) & 0xFFu) << 8;
-            const int mp3 = (int)((rp.z >> 16) & 0xFFu) | (int)(rp.z >> 24) << 8;
-            const float* mdx = (const float*)(meta + (size_t)ms * C::META) + half * NH;
-            const uint4* mbs = (const uint4*)((const float*)(meta + (size_t)ms * C::META) + N) + half * NH;
-#pragma unroll
-            for (int cc = 0; cc < NH; cc += 16) {
-                uint32_t h[16], l[16];
-                tmem_ld16(lane_addr + cc, h);
-                tmem_ld16(lane_addr + N + cc, l);
-                tmem_wait_ld();
-                if (cc + 16 == NH) {   // all reads of this buffer issued and complete
-                    tc_fence_before();
-                    mbar_arrive(&acc_empty[b]);
-                }
-#pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    const float dx = mdx[cc + j];       // 0 for columns past m
-                    const uint4 bs = mbs[cc + j];
-                    int ms = __dp2a_lo((int)bs.x, mp0, 0);
-                    ms = __dp2a_lo((int)bs.y, mp1, ms);
-                    ms = __dp2a_lo((int)bs.z, mp2, ms);
-                    ms = __dp2a_lo((int)bs.w, mp3, ms);
-                    const int isum = 8 * (int)h[j] + (int)l[j];
-                    yacc[cc + j] += dx * (dd.x * (float)isum - dd.y * (float)ms);
+    } else if (warp >= TC_WORK0) {
+        // ---------------- prep + epilogue: thread <-> (weight row, half) ----------------
+        // Iteration i expands unit i's weights (this thread's K half of its row) and then drains
+        // unit i-1's accumulators (this thread's half of the columns): unit i's MMAs run while
+        // unit i-1 is drained.
+        constexpr int NH = N / 2;
+        const int quarter = warp & 3, half = (warp - TC_WORK0) >> 2;
+        const int row = quarter * 32 + lane;
+        const int et = threadIdx.x - TC_WORK0 * 32;   // 0..255
+        pdl_wait();   // y, the partials and the tickets may be in use by the previous kernel
+        float dnext = 0.0f;
+        auto load_d = [&](int i) -> float {   // Q6_K: the row's fp16 d of unit i (0 past the rows)
+            if (Q4 || i >= nu) return 0.0f;
+            const int64_t u = u0 + i, tile = u / nb;
+            const int64_t r = (tile / ct_tiles) * TC_ROWS + row;
+            return r < n ? __half2float(wd[r * nb + (u % nb)]) : 0.0f;
+        };
+        if (!Q4 && half == 0) dnext = load_d(0);
+        float yacc[NH];
+        int seg_s0 = 0;
+        for (int i = 0; i <= nu; i++) {
+            // ---- prep of unit i ----
+            if (i < nu && ok) {
+                const int st = i % WS, ms = i % MS;
+                ok = mbar_wait(&w_full[st], (uint32_t)((i / WS) & 1), &g_tc_error);
+                if (ok && half == 0 && i >= MS)
+                    ok = mbar_wait(&meta_empty[ms], (uint32_t)(((i / MS) - 1) & 1), &g_tc_error);
+                if (ok && i >= 1) ok = mbar_wait(&pl_empty[half], (uint32_t)((i - 1) & 1), &g_tc_error);
+                ok = __all_sync(0xffffffffu, ok);
+                if (ok) {
+                    const uint8_t* src = raw + (size_t)st * C::WT + (size_t)row * TcW<TYPE>::ROWB;
+                    if (half == 0) {   // the row's scales of this unit, for the epilogue
+                        if (Q4) {
+                            const uint4 hdr = *(const uint4*)src;
+                            const Q4kScales sc = q4k_unpack(hdr);
+                            rowp[ms * TC_ROWS + row] = make_uint4(hdr.x, sc.mn03, sc.mn47, 0u);
+                        } else {
+                            rowp[ms * TC_ROWS + row] = make_uint4(__float_as_uint(dnext), 0u, 0u, 0u);
+                            dnext = load_d(i + 1);
+                        }
+                        mbar_arrive(&row_full[ms]);
+                    }
+                    uint8_t* pH = planes + (size_t)(2 * half) * TC_HPLANE + (size_t)(row >> 3) * TC_HSBO + (row & 7) * 16;
+                    prep_half<TYPE>(src, half, pH, pH + TC_HPLANE);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&w_empty[st]);
+                    fence_proxy_async_smem();
+                    mbar_arrive(&pl_full[half]);
                 }
             }
-            mbar_arrive(&meta_empty[ms]);   // row parameters and metadata of super-block e released
+            if (i == 0) continue;
+            // ---- epilogue of unit e = i - 1 ----
+            const int e = i - 1;
+            const int64_t u = u0 + e, tile = u / nb;
+            const int s = (int)(u % nb), b = e & 1, ms = e % MS;
+            if (e == 0 || s == 0) {
+                seg_s0 = s;
+#pragma unroll
+                for (int c = 0; c < NH; c++) yacc[c] = 0.0f;
+            }
+            if (ok) {
+                ok = mbar_wait(&acc_full[b], (uint32_t)((e >> 1) & 1), &g_tc_error) &&
+                     mbar_wait(&meta_full[ms], (uint32_t)((e / MS) & 1), &g_tc_error) &&
+                     mbar_wait(&row_full[ms], (uint32_t)((e / MS) & 1), &g_tc_error);
+                ok = __all_sync(0xffffffffu, ok);   // warp-uniform: the TMEM loads are .sync.aligned
+            }
+            if (ok) {
+                tc_fence_after();
+                const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 2 * N + half * NH);
+                const uint4 rp = rowp[ms * TC_ROWS + row];
+                const float* mdx = (const float*)(meta + (size_t)ms * C::META) + half * NH;
+                const uint4* mbs = (const uint4*)((const float*)(meta + (size_t)ms * C::META) + N) + half * NH;
+                float2 dd = make_float2(__uint_as_float(rp.x), 0.0f);
+                int mp0 = 0, mp1 = 0, mp2 = 0, mp3 = 0;
+                if (Q4) {
+                    dd = __half22float2(*reinterpret_cast<const __half2*>(&rp.x));
+                    // mins as (m0, m1), (m2, m3), ... pairs in the low bytes for dp2a
+                    mp0 = (int)(rp.y & 0xFFu) | (int)((rp.y >> 8) & 0xFFu) << 8;
+                    mp1 = (int)((rp.y >> 16) & 0xFFu) | (int)(rp.y >> 24) << 8;
+                    mp2 = (int)(rp.z & 0xFFu) | (int)((rp.z >> 8) & 0xFFu) << 8;
+                    mp3 = (int)((rp.z >> 16) & 0xFFu) | (int)(rp.z >> 24) << 8;
+                }
+                constexpr int CH = NH < 16 ? NH : 16;
+#pragma unroll
+                for (int cc = 0; cc < NH; cc += CH) {
+                    uint32_t hv[16], lv[16];
+                    if (CH == 16) {
+                        tmem_ld16(lane_addr + cc, hv);
+                        tmem_ld16(lane_addr + N + cc, lv);
+                    } else {
+                        tmem_ld8(lane_addr + cc, hv);
+                        tmem_ld8(lane_addr + N + cc, lv);
+                    }
+                    tmem_wait_ld();
+                    if (cc + CH == NH) {   // every read of this buffer issued and complete
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&acc_empty[b]);
+                    }
+#pragma unroll
+                    for (int j = 0; j < CH; j++) {
+                        const float dx = mdx[cc + j];   // 0 for columns past m
+                        // isum = SHIFT C_H + C_L as one correctly rounded fp32 value (what
+                        // (float)isum gives), from exact conversions of |C_H|, |C_L| < 2^22
+                        const float fsum = fmaf(i2f_exact22((int)hv[j]), (float)TcW<TYPE>::SHIFT,
+                                                i2f_exact22((int)lv[j]));
+                        if (Q4) {
+                            const uint4 bs = mbs[cc + j];
+                            int msum = __dp2a_lo((int)bs.x, mp0, 0);
+                            msum = __dp2a_lo((int)bs.y, mp1, msum);
+                            msum = __dp2a_lo((int)bs.z, mp2, msum);
+                            msum = __dp2a_lo((int)bs.w, mp3, msum);
+                            yacc[cc + j] += dx * (dd.x * fsum - dd.y * i2f_exact22(msum));
+                        } else {
+                            yacc[cc + j] += dx * (dd.x * fsum);
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&meta_empty[ms]);
+            }
+            // ---- end of a tile segment: direct store, or partial + ticket (last arriver sums) ----
+            if (e == nu - 1 || s == nb - 1) {
+                const int64_t rt = tile / ct_tiles;
+                const int ct = (int)(tile % ct_tiles);
+                const int64_t r = rt * TC_ROWS + row;
+                const int cbase = ct * N + half * NH;
+                if (seg_s0 == 0 && s == nb - 1) {
+                    if (ok && r < n)
+#pragma unroll
+                        for (int c = 0; c < NH; c++)
+                            if (cbase + c < m) y[(size_t)(cbase + c) * n + r] = yacc[c];
+                } else {
+                    const int64_t t0 = tile * nb;
+                    const int slot = sk_begin(bid, T, G) > t0 ? 0 : 1;
+                    float* P = part + (size_t)(bid * 2 + slot) * N * TC_ROWS;
+#pragma unroll
+                    for (int c = 0; c < NH; c++) P[(half * NH + c) * TC_ROWS + row] = yacc[c];
+                    __threadfence();
+                    work_bar();
+                    const int64_t cf = sk_owner(t0, T, G), cl = sk_owner(t0 + nb - 1, T, G);
+                    if (et == 0) {
+                        const int old = atomicAdd(&tickets[tile], 1);
+                        const int last = old == (int)(cl - cf);
+                        if (last) tickets[tile] = 0;   // every contributor has arrived: ready for the next call
+                        *last_flag = last;
+                    }
+                    work_bar();
+                    const int last = *last_flag;
+                    if (last) {
+                        __threadfence();
+                        // the partials in CTA order (this CTA's own one re-read from scratch too)
+#pragma unroll
+                        for (int c = 0; c < NH; c++) yacc[c] = 0.0f;
+                        for (int64_t q = cf; q <= cl; q++) {
+                            const int sq = sk_begin(q, T, G) > t0 ? 0 : 1;
+                            const float* Q = part + (size_t)(q * 2 + sq) * N * TC_ROWS;
+#pragma unroll
+                            for (int c = 0; c < NH; c++) yacc[c] += __ldcg(&Q[(half * NH + c) * TC_ROWS + row]);
+                        }
+                        if (ok && r < n)
+#pragma unroll
+                            for (int c = 0; c < NH; c++)
+                                if (cbase + c < m) y[(size_t)(cbase + c) * n + r] = yacc[c];
+                    }
+                    work_bar();   // last_flag is reused by the next segment
+                }
+            }
         }
     }
 
-    // ---------------- output: direct, or rank-ordered sum over the split cluster ----------------
+    // ---------------- teardown ----------------
     tc_fence_before();
     __syncthreads();   // every MMA retired (mma_done) and every TMEM read done
-    float* red = (float*)planes;   // [N][128] partial tile, reusing the plane buffers
-    if (gridDim.z == 1) {
-        if (warp >= TC_EPI0 && r0 + row < n)
-#pragma unroll
-            for (int c = 0; c < NH; c++)
-                if (c0 + half * NH + c < m) y[(size_t)(c0 + half * NH + c) * n + r0 + row] = yacc[c];
-    } else {
-        if (warp >= TC_EPI0)
-#pragma unroll
-            for (int c = 0; c < NH; c++) red[(half * NH + c) * TC_ROWS + row] = yacc[c];
-        cluster_sync_all();
-        if (cluster_rank() == 0)
-            for (int idx = threadIdx.x; idx < N * TC_ROWS; idx += TC_THREADS) {
-                const int rr = idx % TC_ROWS, c = idx / TC_ROWS;
-                float sum = 0.0f;
-                for (uint32_t q = 0; q < gridDim.z; q++) sum += ld_cluster_f32(red + idx, q);
-                if (c0 + c < m && r0 + rr < n) y[(size_t)(c0 + c) * n + r0 + rr] = sum;
-            }
-        cluster_sync_all();
-    }
-    if (warp == 1) {
+    if (warp == 2) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::TMEM_COLS)
                      : "memory");
@@ -376,15 +544,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 // ---- host side ----
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn();  // qmm.cu
 
-static cudaError_t tc_maps(CUtensorMap* wm, CUtensorMap* am, const void* W, int64_t n, int64_t k, const void* qs,
-                           int64_t m, int N) {
+static cudaError_t tc_maps(CUtensorMap* wm, CUtensorMap* am, int type, const void* W, int64_t n, int64_t k,
+                           const void* qs, int64_t m, int N) {
     auto fn = encode_fn();
     if (!fn) return cudaErrorNotSupported;
-    const size_t row_bytes = (size_t)(k / QK_K) * Q4_K_BYTES;
+    const int rowb = type == DCG_TYPE_Q4_K ? Q4_K_BYTES : Q6_K_PAYLOAD;
+    const size_t row_bytes = (size_t)(k / QK_K) * rowb;
     {
         const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 4), (cuuint64_t)n};
         const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
-        const cuuint32_t box[2] = {(cuuint32_t)(Q4_K_BYTES / 4), (cuuint32_t)TC_ROWS};
+        const cuuint32_t box[2] = {(cuuint32_t)(rowb / 4), (cuuint32_t)TC_ROWS};
         const cuuint32_t estr[2] = {1, 1};
         if (fn(wm, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(W), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -404,35 +573,74 @@ static cudaError_t tc_maps(CUtensorMap* wm, CUtensorMap* am, const void* W, int6
     return cudaSuccess;
 }
 
-template <int N>
-static cudaError_t launch_tc_t(const uint8_t* W, int64_t n, int64_t k, const ActQ& a, int m, float* y,
-                               cudaStream_t st) {
-    using C = TcCfg<N>;
-    cudaError_t e = DCG_SMEM_ATTR((qmm_q4k_tc_kernel<N>), C::SMEM);
+// column tile for m activation rows: the smallest of 16 / 32 / 64 / 128 that holds them (128 beyond)
+static int tc_n(int64_t m) { return m <= 16 ? 16 : (m <= 32 ? 32 : (m <= 64 ? 64 : 128)); }
+
+struct TcPlan {
+    int N, ct;
+    int64_t rt, T, G;
+};
+static TcPlan tc_plan(int64_t n, int64_t k, int64_t m) {
+    TcPlan p;
+    p.N = tc_n(m);
+    p.ct = (int)((m + p.N - 1) / p.N);
+    p.rt = (n + TC_ROWS - 1) / TC_ROWS;
+    p.T = p.rt * p.ct * (k / QK_K);
+    const int64_t sms = num_sms();
+    p.G = p.T < sms ? p.T : sms;
+    return p;
+}
+
+size_t qmm_tc_scratch_bytes(int type, int64_t n, int64_t k, int64_t m) {
+    (void)type;
+    const TcPlan p = tc_plan(n, k, m);
+    return align256((size_t)p.rt * p.ct * 4) + (size_t)p.G * 2 * p.N * TC_ROWS * 4;
+}
+int qmm_tc_ticket_count(int type, int64_t n, int64_t k, int64_t m) {
+    (void)type;
+    const TcPlan p = tc_plan(n, k, m);
+    return (int)(p.rt * p.ct);
+}
+
+template <int TYPE, int N>
+static cudaError_t launch_tc_t(const void* W, const __half* wd, int64_t n, int64_t k, const ActQ& a, int m,
+                               float* y, void* scratch, const TcPlan& p, cudaStream_t st) {
+    using C = TcCfg<TYPE, N>;
+    cudaError_t e = DCG_SMEM_ATTR((qmm_tc_kernel<TYPE, N>), C::SMEM);
     if (e != cudaSuccess) return e;
     CUtensorMap wm, am;
-    e = tc_maps(&wm, &am, W, n, k, a.qs, m, N);
+    e = tc_maps(&wm, &am, TYPE, W, n, k, a.qs, m, N);
     if (e != cudaSuccess) return e;
-    const int nb = (int)(k / QK_K);
-    const int rt = (int)((n + TC_ROWS - 1) / TC_ROWS), ct = (m + N - 1) / N;
-    int S = 148 / (rt * ct);                             // one CTA per SM: at most one wave
-    S = S < 1 ? 1 : S;
-    S = S > 8 ? 8 : S;
-    S = S > nb / 2 ? (nb / 2 > 0 ? nb / 2 : 1) : S;     // >= 2 super-blocks per split
-    const int sps = (nb + S - 1) / S;
-    S = (nb + sps - 1) / sps;
-    return launch_ex(qmm_q4k_tc_kernel<N>, dim3((unsigned)rt, (unsigned)ct, (unsigned)S), dim3(TC_THREADS),
-                     (size_t)C::SMEM, st, (unsigned)S, wm, am, nb, n, a, m, y, sps);
+    int* tickets = (int*)scratch;
+    float* part = (float*)((uint8_t*)scratch + align256((size_t)p.rt * p.ct * 4));
+    return launch_pdl(qmm_tc_kernel<TYPE, N>, dim3((unsigned)p.G), dim3(TC_THREADS), (size_t)C::SMEM, st, wm, am,
+                      wd, (int)(k / QK_K), n, a, m, y, p.ct, p.T, part, tickets);
 }
 
 bool qmm_tc_supports(int type, int64_t n, int64_t k, int64_t m) {
-    return type == DCG_TYPE_Q4_K && m >= 2 && k % QK_K == 0 && n > 0;
+    return (type == DCG_TYPE_Q4_K || type == DCG_TYPE_Q6_K) && m >= 2 && k % QK_K == 0 && n > 0;
 }
 
-cudaError_t launch_qmm_tc(const void* packed_w, int64_t n, int64_t k, const void* act, int64_t m, float* y,
-                          cudaStream_t st) {
+cudaError_t launch_qmm_tc(int type, const void* packed_w, int64_t n, int64_t k, const void* act, int64_t m,
+                          float* y, void* scratch, cudaStream_t st) {
     const ActQ a = act_view(DCG_TYPE_Q8_K, const_cast<void*>(act), m, k);
-    return launch_tc_t<32>((const uint8_t*)packed_w, n, k, a, (int)m, y, st);
+    const TcPlan p = tc_plan(n, k, m);
+    const int mi = (int)m;
+    if (type == DCG_TYPE_Q4_K) {
+        switch (p.N) {
+            case 16: return launch_tc_t<DCG_TYPE_Q4_K, 16>(packed_w, nullptr, n, k, a, mi, y, scratch, p, st);
+            case 32: return launch_tc_t<DCG_TYPE_Q4_K, 32>(packed_w, nullptr, n, k, a, mi, y, scratch, p, st);
+            case 64: return launch_tc_t<DCG_TYPE_Q4_K, 64>(packed_w, nullptr, n, k, a, mi, y, scratch, p, st);
+            default: return launch_tc_t<DCG_TYPE_Q4_K, 128>(packed_w, nullptr, n, k, a, mi, y, scratch, p, st);
+        }
+    }
+    const PackedW w = packed_view(DCG_TYPE_Q6_K, packed_w, n, k);
+    switch (p.N) {
+        case 16: return launch_tc_t<DCG_TYPE_Q6_K, 16>(packed_w, w.d, n, k, a, mi, y, scratch, p, st);
+        case 32: return launch_tc_t<DCG_TYPE_Q6_K, 32>(packed_w, w.d, n, k, a, mi, y, scratch, p, st);
+        case 64: return launch_tc_t<DCG_TYPE_Q6_K, 64>(packed_w, w.d, n, k, a, mi, y, scratch, p, st);
+        default: return launch_tc_t<DCG_TYPE_Q6_K, 128>(packed_w, w.d, n, k, a, mi, y, scratch, p, st);
+    }
 }
 
 }  // namespace dcg

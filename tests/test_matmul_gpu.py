@@ -101,6 +101,16 @@ MATMUL_CASES = [
     (O.Q4_K, 640, 9728, 32),      # tcgen05 path, split-K over a cluster
     (O.Q4_K, 256, 4096, 256),     # config-2 M=256 (reduced n)
     (O.Q4_K, 130, 14336, 17),
+    # tcgen05 stream-K kernel: every column tile width, ragged tiles, tiles split over many CTAs
+    (O.Q4_K, 128, 14336, 16),     # one row tile, 56 units over 56 CTAs: every unit a partial
+    (O.Q4_K, 200, 2560, 2),       # N = 16 tile, 2 live columns
+    (O.Q4_K, 384, 4096, 100),     # N = 128 tile, ragged columns
+    (O.Q4_K, 256, 2560, 300),     # three N = 128 column tiles
+    (O.Q4_K, 256, 2560, 2048),    # prefill-sized M (16 column tiles)
+    (O.Q6_K, 128, 14336, 16),
+    (O.Q6_K, 384, 4096, 100),
+    (O.Q6_K, 300, 9728, 64),
+    (O.Q6_K, 256, 2560, 2048),
 ]
 
 
@@ -132,6 +142,41 @@ def test_mul_mat_config2_full_size(ops):
         y_ref = O.mul_mat(O.Q4_K, wq, k, xq, 1, nthreads=8)
         y = ops.mul_mat(ops.QuantWeight.from_ggml(rows, O.Q4_K, k), _dev(x)).cpu().numpy()
         _assert_rows_close(y, wq, O.Q4_K, k, xq, O.Q8_K, y_ref)
+
+
+@pytest.mark.parametrize("m", [16, 64, 256])
+def test_mul_mat_config2_full_size_batched(ops, m):
+    """Config 2 at the benchmarked batch sizes (full 14336x4096 and 4096x14336 Q4_K weights): the
+    tcgen05 stream-K kernel against the oracle, row by row; a second call on the same scratch gives
+    bit-identical results (deterministic partial sums, tickets left at zero)."""
+    rng = np.random.default_rng(100 + m)
+    for n, k in ((14336, 4096), (4096, 14336)):
+        wq = O.quantize((rng.standard_normal((n, k)) * 0.02).astype(np.float32), O.Q4_K)
+        x = rng.standard_normal((m, k)).astype(np.float32)
+        xq = O.quantize(x, O.Q8_K)
+        y_ref = O.mul_mat(O.Q4_K, wq, k, xq, m, nthreads=16, simd=True)
+        qw = ops.QuantWeight.from_ggml(_dev(wq), O.Q4_K, k)
+        scr = torch.zeros(ops.mul_mat_scratch_size(O.Q4_K, n, k, m), dtype=torch.uint8, device="cuda")
+        xd = _dev(x)
+        y1 = ops.mul_mat(qw, xd, scratch=scr).cpu().numpy()
+        y2 = ops.mul_mat(qw, xd, scratch=scr).cpu().numpy()
+        assert np.array_equal(y1, y2)
+        _assert_rows_close(y1, wq, O.Q4_K, k, xq, O.Q8_K, y_ref)
+
+
+@pytest.mark.parametrize("wt", [O.Q4_K, O.Q6_K])
+def test_mul_mat_q_scratch_reuse(ops, wt):
+    """dcg_mul_mat_q leaves its zero-filled scratch ready for the next call: many calls on one
+    scratch (different weights and batch sizes sharing it) equal fresh-scratch results."""
+    torch.manual_seed(wt)
+    shapes = [(512, 4096, 64), (128, 14336, 16), (1024, 2560, 32), (512, 4096, 64)]
+    need = max(ops.mul_mat_q_scratch_size(wt, n, k, m) for n, k, m in shapes)
+    shared = torch.zeros(need, dtype=torch.uint8, device="cuda")
+    for n, k, m in shapes:
+        qw = ops.QuantWeight.from_float(torch.randn(n, k, device="cuda") * 0.02, wt)
+        act = ops.quantize_act(torch.randn(m, k, device="cuda"), O.Q8_K)
+        fresh = torch.zeros(ops.mul_mat_q_scratch_size(wt, n, k, m), dtype=torch.uint8, device="cuda")
+        assert torch.equal(ops.mul_mat_q(qw, act, m, scratch=shared), ops.mul_mat_q(qw, act, m, scratch=fresh))
 
 
 @pytest.mark.parametrize("n,k", [(14336, 4096), (4096, 14336), (8192, 28672), (100, 2560)])
