@@ -54,10 +54,12 @@ void set_error(const std::string& m) { g_last_error = m; }
 static bool use_tc(int type, int64_t n, int64_t k, int64_t m) { return dcg::qmm_tc_supports(type, n, k, m); }
 static size_t qmm_part(int type, int64_t n, int64_t k, int64_t m) {
     if (use_tc(type, n, k, m)) return dcg::qmm_tc_scratch_bytes(type, n, k, m);
+    if (dcg::qmm_q8tc_supports(type, n, k, m)) return dcg::qmm_q8tc_scratch_bytes(n, k, m);
     return dcg::qmm_supports(type) ? dcg::qmm_scratch_bytes(type, n, k, m) : 0;
 }
 static int qmm_tickets(int type, int64_t n, int64_t k, int64_t m) {
     if (use_tc(type, n, k, m)) return dcg::qmm_tc_ticket_count(type, n, k, m);
+    if (dcg::qmm_q8tc_supports(type, n, k, m)) return dcg::qmm_q8tc_ticket_count(n, k, m);
     return dcg::qmm_supports(type) ? dcg::qmm_ticket_count(type, n, m) : 0;
 }
 
@@ -65,6 +67,10 @@ static int enqueue_mul_mat_q(int type, const void* w, int64_t n, int64_t k, cons
                              float* y, void* qscratch, cudaStream_t st) {
     if (use_tc(type, n, k, m)) {
         DCG_CUDA(dcg::launch_qmm_tc(type, w, n, k, act, m, y, qscratch, st), "qmm_tc");
+        return DCG_OK;
+    }
+    if (dcg::qmm_q8tc_supports(type, n, k, m)) {
+        DCG_CUDA(dcg::launch_qmm_q8tc(w, n, k, act, m, y, qscratch, st), "qmm_q8tc");
         return DCG_OK;
     }
     if (dcg::qmm_supports(type)) {
@@ -210,12 +216,13 @@ int dcg_mul_mat(int type, const void* w, int64_t n, int64_t k, const float* x, i
 
 int dcg_device_error(int* code, int clear) {
     if (!code) return fail(DCG_EINVAL, "null pointer");
-    int a = 0, b = 0, c = 0, d = 0;
+    int a = 0, b = 0, c = 0, d = 0, f = 0;
+    DCG_CUDA(dcg::qmm_q8tc_device_error(&f, clear != 0), "read device error flag");
     DCG_CUDA(dcg::gemv_device_error(&a, clear != 0), "read device error flag");
     DCG_CUDA(dcg::qmm_device_error(&b, clear != 0), "read device error flag");
     DCG_CUDA(dcg::attn_device_error(&c, clear != 0), "read device error flag");
     DCG_CUDA(dcg::qmm_tc_device_error(&d, clear != 0), "read device error flag");
-    *code = a ? a : (b ? b : (c ? c : d));
+    *code = a ? a : (b ? b : (c ? c : (d ? d : f)));
     return DCG_OK;
 }
 

@@ -38,6 +38,14 @@ cudaError_t qmm_tc_device_error(int* out, bool clear);
 cudaError_t qmm_device_error(int* out, bool clear);
 bool qmm_supports(int type);
 
+// tcgen05 Q8_0 GEMM for m >= 2, k % 256 == 0 (qmm_q8tc.cu); scratch as for qmm_tc
+bool qmm_q8tc_supports(int type, int64_t n, int64_t k, int64_t m);
+size_t qmm_q8tc_scratch_bytes(int64_t n, int64_t k, int64_t m);
+int qmm_q8tc_ticket_count(int64_t n, int64_t k, int64_t m);
+cudaError_t launch_qmm_q8tc(const void* packed_w, int64_t n, int64_t k, const void* act, int64_t m, float* y,
+                            void* scratch, cudaStream_t st);
+cudaError_t qmm_q8tc_device_error(int* out, bool clear);
+
 // register-direct tensor-core matmul for Q8_0 / Q6_K (qmm_rd.cu), M >= 2, k % 256 == 0
 bool qmm_rd_supports(int type, int64_t k, int64_t m);
 cudaError_t launch_qmm_rd(int type, const void* packed_w, int64_t n, int64_t k, const void* act,

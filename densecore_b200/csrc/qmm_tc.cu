@@ -35,6 +35,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tcgen05.cuh"
 #include "tma.cuh"
 
 namespace dcg {
@@ -91,64 +92,8 @@ struct TcCfg {
     static_assert(SMEM <= TC_SMEM_MAX, "shared memory");
 };
 
-// ---- tcgen05 plumbing ----
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-    // K-major, no swizzle: start >> 4, leading (K-direction) byte offset >> 4, stride (8-row
-    // group) byte offset >> 4, version 1 (bits 46-47), base offset 0, layout type 0
-    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | ((uint64_t)1 << 46);
-}
-
-template <int N>
-__host__ __device__ constexpr uint32_t idesc_i8() {
-    // D s32 (bits 4-5 = 2), A and B signed 8-bit (bits 7-9, 10-12 = 1), both K-major,
-    // N >> 3 at bits 17-22, M >> 4 at bits 24-28
-    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(TC_ROWS >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                       uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-        ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-        : "memory");
-}
-
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-        : "r"(taddr)
-        : "memory");
-}
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[16]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
-                 : "r"(taddr)
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// exact int -> float for |v| < 2^22 with two full-rate ops (the float magic-number method: v added
-// to the mantissa of 1.5 * 2^23, whose unit in the last place is 1, then the bias subtracted); the
-// conversion instruction runs at a fraction of that rate
-__device__ __forceinline__ float i2f_exact22(int v) { return __int_as_float(0x4B400000 + v) - 12582912.0f; }
-
+// named barrier of the 8 prep / epilogue warps
 __device__ __forceinline__ void work_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-
-// stream-K ranges: CTA c owns units [begin(c), begin(c+1)); owner(u) is the CTA whose range holds u
-__host__ __device__ __forceinline__ int64_t sk_begin(int64_t c, int64_t T, int64_t G) { return c * T / G; }
-__device__ __forceinline__ int64_t sk_owner(int64_t u, int64_t T, int64_t G) { return ((u + 1) * G - 1) / T; }
 
 // ---- prep: one weight row of one super-block (in shared memory) -> the two planes of K half h ----
 // Q4_K K half h (sub-blocks 4h .. 4h+3): chunk kc (16 elements) of sub-block kc/2
@@ -330,7 +275,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // ---------------- MMA issue ----------------
         pdl_wait();
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_i8<N>();
+            constexpr uint32_t idesc = idesc_i8<TC_ROWS, N>();
             for (int i = 0; i < nu && ok; i++) {
                 const int st = i % AS, b = i & 1;
                 ok = mbar_wait(&a_full[st], (uint32_t)((i / AS) & 1), &g_tc_error) &&
