@@ -3,6 +3,7 @@
 #include <string>
 #include <unordered_map>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include "../../include/dcgpu.h"
@@ -63,8 +64,22 @@ static int qmm_tickets(int type, int64_t n, int64_t k, int64_t m) {
     return dcg::qmm_supports(type) ? dcg::qmm_ticket_count(type, n, m) : 0;
 }
 
+// M = 1 kernel choice: the streaming mat-vec (gemv_m1.cu) unless DCG_M1_KERNEL=legacy selects the
+// earlier per-type kernels (kept for side-by-side measurement)
+static bool use_m1s(int type, int64_t n, int64_t k, int64_t m) {
+    static const bool legacy = [] {
+        const char* e = getenv("DCG_M1_KERNEL");
+        return e && strcmp(e, "legacy") == 0;
+    }();
+    return m == 1 && !legacy && dcg::m1s_supports(type, n, k);
+}
+
 static int enqueue_mul_mat_q(int type, const void* w, int64_t n, int64_t k, const void* act, int64_t m,
                              float* y, void* qscratch, cudaStream_t st) {
+    if (use_m1s(type, n, k, m)) {
+        DCG_CUDA(dcg::launch_m1s(type, w, n, k, nullptr, act, y, st), "gemv_m1");
+        return DCG_OK;
+    }
     if (use_tc(type, n, k, m)) {
         DCG_CUDA(dcg::launch_qmm_tc(type, w, n, k, act, m, y, qscratch, st), "qmm_tc");
         return DCG_OK;
@@ -90,6 +105,10 @@ static int enqueue_mul_mat_q(int type, const void* w, int64_t n, int64_t k, cons
 
 static int enqueue_mul_mat(int type, const void* w, int64_t n, int64_t k, const float* x,
                            int64_t m, float* y, void* scratch, cudaStream_t st) {
+    if (use_m1s(type, n, k, m)) {
+        DCG_CUDA(dcg::launch_m1s(type, w, n, k, x, nullptr, y, st), "gemv_m1");
+        return DCG_OK;
+    }
     if (dcg::qmm_m1_fused_supports(type, n, k, m)) {
         DCG_CUDA(dcg::launch_qmm_m1_fused(w, n, k, x, y, st), "qmm m1");
         return DCG_OK;
@@ -216,13 +235,14 @@ int dcg_mul_mat(int type, const void* w, int64_t n, int64_t k, const float* x, i
 
 int dcg_device_error(int* code, int clear) {
     if (!code) return fail(DCG_EINVAL, "null pointer");
-    int a = 0, b = 0, c = 0, d = 0, f = 0;
+    int a = 0, b = 0, c = 0, d = 0, f = 0, g = 0;
     DCG_CUDA(dcg::qmm_q8tc_device_error(&f, clear != 0), "read device error flag");
+    DCG_CUDA(dcg::m1s_device_error(&g, clear != 0), "read device error flag");
     DCG_CUDA(dcg::gemv_device_error(&a, clear != 0), "read device error flag");
     DCG_CUDA(dcg::qmm_device_error(&b, clear != 0), "read device error flag");
     DCG_CUDA(dcg::attn_device_error(&c, clear != 0), "read device error flag");
     DCG_CUDA(dcg::qmm_tc_device_error(&d, clear != 0), "read device error flag");
-    *code = a ? a : (b ? b : (c ? c : (d ? d : f)));
+    *code = a ? a : (b ? b : (c ? c : (d ? d : (f ? f : g))));
     return DCG_OK;
 }
 

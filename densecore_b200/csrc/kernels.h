@@ -46,6 +46,13 @@ cudaError_t launch_qmm_q8tc(const void* packed_w, int64_t n, int64_t k, const vo
                             void* scratch, cudaStream_t st);
 cudaError_t qmm_q8tc_device_error(int* out, bool clear);
 
+// M = 1 streaming mat-vec for Q4_K / Q6_K / Q8_0 (gemv_m1.cu): x = fp32 row quantized in the kernel,
+// or x = null and act = the SoA quantized activation; no scratch
+bool m1s_supports(int type, int64_t n, int64_t k);
+cudaError_t launch_m1s(int type, const void* packed_w, int64_t n, int64_t k, const float* x, const void* act,
+                       float* y, cudaStream_t st);
+cudaError_t m1s_device_error(int* out, bool clear);
+
 // register-direct tensor-core matmul for Q8_0 / Q6_K (qmm_rd.cu), M >= 2, k % 256 == 0
 bool qmm_rd_supports(int type, int64_t k, int64_t m);
 cudaError_t launch_qmm_rd(int type, const void* packed_w, int64_t n, int64_t k, const void* act,
