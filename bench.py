@@ -9,8 +9,9 @@ on the fly, then the Q4_K GEMV).  Weights come from an 8-slot ring of distinct s
 
 Prints one JSON line (rank 0).  value = weight GB/s of the whole job; e2e = the same metric
 through the host-pointer C ABI (dcg_ctx_mul_mat: H2D of x, both kernels, D2H of y, per call).
---impl reference times the CPU implementation of the same op (the AVX2 restatement of ggml's
-vec_dot / quantize_row_q8_K, all host threads) on a bounded sample of the same workload.
+--impl reference times the CPU implementation of the same op (the AVX-512 VNNI restatement of
+ggml's vec_dot_q4_K_q8_K where the host has it, else AVX2; quantize_row_q8_K; all host threads)
+on a bounded sample of the same workload.
 """
 from __future__ import annotations
 
@@ -116,7 +117,7 @@ class ClockSampler:
 
 
 def cpu_reference(budget_s: float, int4: bool = True):
-    """The oracle's row-sliced mul_mat (ggml vec_dot_q4_K_q8_K restated, AVX2 dots bit-identical
+    """The oracle's row-sliced mul_mat (ggml vec_dot_q4_K_q8_K restated, AVX-512 VNNI or AVX2 dots bit-identical
     to the scalar ones) plus quantize_row_q8_K on all host threads, on the same shapes; repeats
     whole steps until ~budget_s elapsed.  int4: also time DenseCore's own INT4 GEMV."""
     import numpy as np
@@ -138,11 +139,12 @@ def cpu_reference(budget_s: float, int4: bool = True):
         el = time.perf_counter() - t0
         if el >= budget_s:
             break
+    isa = O.simd_isa()
     out = {"value": WEIGHT_BYTES * steps / el / 1e9, "unit": UNIT, "cores": threads,
-           "kind": "port", "steps": steps, "seconds": el,
+           "kind": "port", "steps": steps, "seconds": el, "isa": isa,
            "sample": f"{steps} full steps (both FFN matmuls, M=1) of config 2 on {threads} "
-                     f"host threads, AVX2 restatement of ggml vec_dot_q4_K_q8_K"
-                     f"{'' if O.simd_available() else ' (scalar: no AVX2 on this CPU)'}"}
+                     f"host threads, {isa} restatement of ggml vec_dot_q4_K_q8_K (runtime-selected "
+                     "best ISA, bit-identical to the scalar oracle)"}
     # side datapoint: DenseCore's own INT4 decode GEMV (its custom INT4 format, group 128) on the
     # same shapes -- the reference's best-ISA integer GEMV that is compiled here
     r = O.ref_int4_gemv(SHAPES, 128, threads, max(1.0, budget_s / 2)) if int4 else None
@@ -453,8 +455,8 @@ def run_reference(args):
     cb["value"] = round(value, 4)
     cb["sample"] = (f"{args.steps} timed samples of >= {args.ref_step_seconds}s, {n_steps} full steps "
                     f"of config 2 (both FFN matmuls, M=1) on {cb['cores']} host threads; ggml is "
-                    "absent, so this is the AVX2 restatement of vec_dot_q4_K_q8_K (bit-identical to "
-                    "the scalar oracle)")
+                    f"absent, so this is the {cb['isa']} restatement of vec_dot_q4_K_q8_K (the best "
+                    "ISA the host has, selected at run time; bit-identical to the scalar oracle)")
     side = cpu_reference(0.0, int4=True).get("reference_int4")   # timed once, not per step
     if side is not None:
         cb["reference_int4"] = side

@@ -441,9 +441,53 @@ __attribute__((target("avx2,fma"))) static float vec_dot_q4_K_avx2(int n, const 
     return sumf;
 }
 static int have_avx2(void) { return __builtin_cpu_supports("avx2"); }
+
+/* ---------------- AVX-512 VNNI restatement of vec_dot_q4_K (the CPU baseline where the host has
+ * it; the vpdpbusd pattern of the reference's own best-ISA integer GEMV,
+ * core/src/kernels/cpu_int4.cpp:279-410) ----------------------------------------------------
+ * Per pair group g one 64-byte vector holds the low nibbles (sub-block 2g) then the high nibbles
+ * (sub-block 2g+1), matching activation bytes 64g..64g+63; vpdpbusd forms unsigned x signed byte
+ * products summed by fours into 16 int32 lanes (lanes 0-7: sub-block 2g, 8-15: 2g+1), which are
+ * scaled by the two 6-bit sub-block scales (vpmulld) and accumulated.  The integer sum, the min
+ * term and the float operations are those of vec_dot_q4_K, in the same order: bit-identical. */
+__attribute__((target("avx512f,avx512bw,avx512vnni,fma"))) static float vec_dot_q4_K_vnni(int n, const blk_q4_K* w,
+                                                                                           const blk_q8_K* x) {
+    const __m256i m4 = _mm256_set1_epi8(0x0F);
+    float sumf = 0.0f;
+    for (int b = 0; b < n / QK_K; b++) {
+        int sc[8], mn[8];
+        for (int j = 0; j < 8; j++) unpack_q4_K_scale(w[b].scales, j, &sc[j], &mn[j]);
+        __m512i acc = _mm512_setzero_si512();
+        for (int g = 0; g < 4; g++) {
+            const __m256i q = _mm256_loadu_si256((const __m256i*)(w[b].qs + 32 * g));
+            const __m256i lo = _mm256_and_si256(q, m4);
+            const __m256i hi = _mm256_and_si256(_mm256_srli_epi16(q, 4), m4);
+            const __m512i qq = _mm512_inserti64x4(_mm512_castsi256_si512(lo), hi, 1);
+            const __m512i xx = _mm512_loadu_si512((const void*)(x[b].qs + 64 * g));
+            const __m512i dot = _mm512_dpbusd_epi32(_mm512_setzero_si512(), qq, xx);
+            const __m512i scv = _mm512_inserti64x4(_mm512_castsi256_si512(_mm256_set1_epi32(sc[2 * g])),
+                                                   _mm256_set1_epi32(sc[2 * g + 1]), 1);
+            acc = _mm512_add_epi32(acc, _mm512_mullo_epi32(dot, scv));
+        }
+        const int32_t isum = _mm512_reduce_add_epi32(acc);
+        int32_t ms = 0;
+        for (int j = 0; j < 8; j++) ms += mn[j] * ((int)x[b].bsums[2 * j] + (int)x[b].bsums[2 * j + 1]);
+        const float d = dco_fp16_to_fp32(w[b].d) * x[b].d;
+        const float dmin = dco_fp16_to_fp32(w[b].dmin) * x[b].d;
+        sumf += d * (float)isum;
+        sumf -= dmin * (float)ms;
+    }
+    return sumf;
+}
+static int have_vnni(void) {
+    return __builtin_cpu_supports("avx512f") && __builtin_cpu_supports("avx512bw") &&
+           __builtin_cpu_supports("avx512vnni");
+}
 #else
 static float vec_dot_q4_K_avx2(int n, const blk_q4_K* w, const blk_q8_K* x) { return vec_dot_q4_K(n, w, x); }
+static float vec_dot_q4_K_vnni(int n, const blk_q4_K* w, const blk_q8_K* x) { return vec_dot_q4_K(n, w, x); }
 static int have_avx2(void) { return 0; }
+static int have_vnni(void) { return 0; }
 #endif
 
 /* ---------------- threaded row-sliced GEMV/GEMM (cb_gemv_custom, inference.cpp:896-924) ----- */
@@ -462,7 +506,10 @@ static void* mm_worker(void* p) {
     for (int64_t r = j->r0; r < j->r1; r++)
         for (int64_t i = 0; i < j->m; i++) {
             float* dst = &j->y[i * j->n_rows + r];
-            if (j->simd)
+            if (j->simd == DCO_ISA_VNNI)
+                *dst = vec_dot_q4_K_vnni((int)j->k, (const blk_q4_K*)(j->w + r * j->row_stride),
+                                         (const blk_q8_K*)(j->xq + i * xrow));
+            else if (j->simd == DCO_ISA_AVX2)
                 *dst = vec_dot_q4_K_avx2((int)j->k, (const blk_q4_K*)(j->w + r * j->row_stride),
                                          (const blk_q8_K*)(j->xq + i * xrow));
             else
@@ -479,11 +526,15 @@ void dco_mul_mat(int type, const void* w, size_t row_stride, int64_t n_rows, int
     mul_mat_threads(type, 0, w, row_stride, n_rows, k, xq, m, y, nthreads);
 }
 
+int dco_simd_isa(void) { return have_vnni() ? DCO_ISA_VNNI : (have_avx2() ? DCO_ISA_AVX2 : 0); }
+
 int dco_mul_mat_simd(int type, const void* w, size_t row_stride, int64_t n_rows, int64_t k,
-                     const void* xq, int64_t m, float* y, int nthreads) {
-    const int simd = type == DCO_Q4_K && have_avx2();
-    mul_mat_threads(type, simd, w, row_stride, n_rows, k, xq, m, y, nthreads);
-    return simd;
+                     const void* xq, int64_t m, float* y, int nthreads, int isa) {
+    const int best = dco_simd_isa();
+    int use = isa == 0 ? best : isa;
+    if (type != DCO_Q4_K || (use == DCO_ISA_VNNI && !have_vnni()) || (use == DCO_ISA_AVX2 && !have_avx2())) use = 0;
+    mul_mat_threads(type, use, w, row_stride, n_rows, k, xq, m, y, nthreads);
+    return use;
 }
 
 static void mul_mat_threads(int type, int simd, const void* w, size_t row_stride, int64_t n_rows,

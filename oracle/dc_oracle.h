@@ -55,10 +55,14 @@ void dco_block_dots(int type, int n, const void* w, const void* xq, int32_t* out
 void dco_mul_mat(int type, const void* w, size_t row_stride, int64_t n_rows, int64_t k,
                  const void* xq, int64_t m, float* y, int nthreads);
 
-/* The same with the AVX2 restatement of the Q4_K dot (bit-identical results; the CPU baseline's
- * compute).  Returns 1 when the AVX2 path ran, 0 when it fell back to the scalar dots. */
+/* The same with a SIMD restatement of the Q4_K dot (bit-identical results; the CPU baseline's
+ * compute): isa = DCO_ISA_VNNI (AVX-512 VNNI vpdpbusd), DCO_ISA_AVX2 (maddubs), or 0 for the best
+ * the host supports.  Returns the ISA that ran (0: the scalar dots). */
+#define DCO_ISA_AVX2 1
+#define DCO_ISA_VNNI 2
+int dco_simd_isa(void);
 int dco_mul_mat_simd(int type, const void* w, size_t row_stride, int64_t n_rows, int64_t k,
-                     const void* xq, int64_t m, float* y, int nthreads);
+                     const void* xq, int64_t m, float* y, int nthreads, int isa);
 
 /* fp16 paged-KV decode attention, one query token per sequence.
  * q [n_seqs][hq][d] f32; k_arena/v_arena fp16 laid out [(block*n_layer+layer)][16][hkv][d];

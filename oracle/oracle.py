@@ -47,8 +47,9 @@ def lib():
         L.dco_vec_dot.argtypes = [i32, i32, vp, vp, vp]
         L.dco_block_dots.argtypes = [i32, i32, vp, vp, vp, vp]
         L.dco_mul_mat.argtypes = [i32, vp, ctypes.c_size_t, i64, i64, vp, i64, vp, i32]
-        L.dco_mul_mat_simd.argtypes = [i32, vp, ctypes.c_size_t, i64, i64, vp, i64, vp, i32]
+        L.dco_mul_mat_simd.argtypes = [i32, vp, ctypes.c_size_t, i64, i64, vp, i64, vp, i32, i32]
         L.dco_mul_mat_simd.restype = i32
+        L.dco_simd_isa.restype = i32
         L.dco_paged_attn_decode.argtypes = [vp, vp, vp, i32, i32, vp, i32, vp, i32, i32, i32, i32,
                                             f, vp, i32]
         L.dco_kv_append.argtypes = [vp, vp, vp, vp, i32, i32, vp, i32, vp, vp, i32, i32, i32]
@@ -140,22 +141,35 @@ def block_dots(wtype: int, k: int, w_row: np.ndarray, xq_row: np.ndarray):
     return (a, b) if wtype == Q4_K else a
 
 
+ISA_NAMES = {0: "scalar", 1: "avx2", 2: "avx512vnni"}
+
+
 def mul_mat(wtype: int, w: np.ndarray, k: int, xq: np.ndarray, m: int, nthreads: int = 1,
-            simd: bool = False):
-    """y[m, n_rows] = W . xq (row-sliced over nthreads, like cb_gemv_custom).  simd: Q4_K dots
-    by the AVX2 restatement (bit-identical; the CPU baseline's compute)."""
+            simd=False):
+    """y[m, n_rows] = W . xq (row-sliced over nthreads, like cb_gemv_custom).  simd: Q4_K dots by
+    a SIMD restatement (bit-identical; the CPU baseline's compute): True = the best the host has
+    (AVX-512 VNNI, else AVX2), or "avx2" / "avx512vnni"."""
     w = np.ascontiguousarray(w, dtype=np.uint8)
     rs = row_size(wtype, k)
     n_rows = w.size // rs
     y = np.zeros((m, n_rows), dtype=np.float32)
-    fn = lib().dco_mul_mat_simd if simd else lib().dco_mul_mat
-    fn(wtype, _p(w), rs, n_rows, k, _p(np.ascontiguousarray(xq)), m, _p(y), nthreads)
+    args = (wtype, _p(w), rs, n_rows, k, _p(np.ascontiguousarray(xq)), m, _p(y), nthreads)
+    if simd:
+        isa = {True: 0, "avx2": 1, "avx512vnni": 2}[simd]
+        lib().dco_mul_mat_simd(*args, isa)
+    else:
+        lib().dco_mul_mat(*args)
     return y
 
 
+def simd_isa() -> str:
+    """The ISA mul_mat(..., simd=True) uses for Q4_K dots on this CPU: avx512vnni, avx2 or scalar."""
+    return ISA_NAMES[int(lib().dco_simd_isa())]
+
+
 def simd_available() -> bool:
-    """Whether mul_mat(..., simd=True) runs the AVX2 Q4_K dots on this CPU."""
-    return bool(lib().dco_mul_mat_simd(Q4_K, None, 144, 0, 256, None, 0, None, 1))
+    """Whether mul_mat(..., simd=True) runs SIMD Q4_K dots on this CPU."""
+    return simd_isa() != "scalar"
 
 
 def paged_attn_decode(q, k_arena, v_arena, n_layer, layer, block_tables, ctx_lens, hkv,

@@ -114,16 +114,24 @@ def test_kv_append_then_attention_roundtrip():
     assert np.array_equal(ka[3 * n_layer + 1, 5], k[2].astype(np.float16))
 
 
-def test_simd_q4_K_dot_is_bit_identical():
-    """The AVX2 restatement of vec_dot_q4_K_q8_K (the CPU baseline's compute) gives the scalar
-    oracle's bits, including ragged row counts and the shortest row."""
+@pytest.mark.parametrize("isa", ["avx2", "avx512vnni"])
+def test_simd_q4_K_dot_is_bit_identical(isa):
+    """The AVX2 and AVX-512 VNNI restatements of vec_dot_q4_K_q8_K (the CPU baseline's compute)
+    give the scalar oracle's bits, including ragged row counts and the shortest row, and extreme
+    nibbles / activation bytes."""
     import numpy as np
     from oracle import oracle as O
+    if isa == "avx512vnni" and O.simd_isa() != "avx512vnni":
+        pytest.skip("no AVX-512 VNNI on this CPU")
+    if O.simd_isa() == "scalar":
+        pytest.skip("no AVX2 on this CPU")
     rng = np.random.default_rng(11)
     for n, k, m in ((64, 4096, 1), (37, 14336, 3), (5, 256, 2)):
         w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
         x = rng.standard_normal((m, k)).astype(np.float32)
+        x[0, :16] = 100.0   # activation bytes at +-127
+        x[0, 16:32] = -100.0
         wq, xq = O.quantize(w, O.Q4_K), O.quantize(x, O.Q8_K)
         a = O.mul_mat(O.Q4_K, wq, k, xq, m, nthreads=3)
-        b = O.mul_mat(O.Q4_K, wq, k, xq, m, nthreads=3, simd=True)
+        b = O.mul_mat(O.Q4_K, wq, k, xq, m, nthreads=3, simd=isa)
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
