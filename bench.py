@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import argparse
 import datetime
+import gc
 import dataclasses
 import json
 import os
@@ -290,6 +291,12 @@ def decode_70b(args):
                           "achieved_gbs_per_gpu": round(per_gpu / (ms * 1e-3) / 1e9, 1),
                           "parallelism": f"tp{ws} (2 NCCL all-reduces / layer, logits all-gather)",
                           "data": "synthetic (random-init weights, seeded random KV history)"}), flush=True)
+    # captured graphs hold references to the NCCL communicator: destroying the process group while
+    # the step graph is alive blocks forever, so the graph (and the model) go first
+    dec.graph = None
+    del dec
+    gc.collect()
+    torch.cuda.synchronize()
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -42,6 +42,10 @@ SIGNATURES = {
     "dcg_paged_attn_scratch_size": (sz, [i32, i32, i32, i32, i32]),
     "dcg_paged_attn_decode": (i32, [vp, vp, vp, i64, i32, i32, vp, i32, vp, i32, i32, i32, i32, i32,
                                     f32, vp, vp, sz, vp]),
+    "dcg_paged_attn_prefill": (i32, [vp, vp, vp, i64, i32, i32, vp, i32, vp, vp, i32, i32, i32, i32, i32, i32,
+                                     f32, vp, vp]),
+    "dcg_qk_norm_rope_kv_append_tokens": (i32, [vp, i64, vp, i64, vp, i64, i32, i32, i32, i32, vp, vp, f32, f32,
+                                                vp, vp, vp, vp, vp, i32, i32, vp, i32, vp]),
     "dcg_kv_append": (i32, [vp, vp, vp, vp, i32, i32, vp, i32, vp, vp, i32, i32, i32, vp]),
     "dcg_add_rmsnorm_quantize": (i32, [vp, vp, vp, f32, i64, i64, i32, vp, vp]),
     "dcg_swiglu_quantize": (i32, [vp, vp, i64, i64, i64, i32, vp, vp]),

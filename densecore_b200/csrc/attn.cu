@@ -333,6 +333,215 @@ __global__ void attn_combine_kernel(const float* __restrict__ part_o, const floa
     out[((size_t)seq * hq + h) * HD + dd] = Ls > 0.0f ? O / Ls : 0.0f;
 }
 
+// ------------------------------------------------------------------------------------------
+// Multi-token (prefill / chunked prompt) causal attention over the same paged cache: the flash
+// path of inference.cpp:1519-1573 with its host-built causal mask (query i of a batch of N new
+// tokens sees keys 0 .. n_past + i, :1538-1558; the tiled path's diag_mask_inf, :1590-1711), made
+// per sequence.  Sequence s's new tokens are rows seq_starts[s] .. seq_starts[s+1]-1 of q / out;
+// token i of n_s sits at position ctx_lens[s] - n_s + i (its K/V already appended) and attends to
+// keys 0 .. that position.
+//
+// One CTA per (tile of PF_ROWS / NREP tokens of one sequence, kv head): its rows are the (token,
+// query head) pairs of that group, 16 per consumer warp (the mma's M), so each K/V byte is read
+// once per tile for all NREP heads.  A producer warp streams the tiles of KV blocks
+// 0 .. (last position) / 16 (TMA, 128-byte swizzle, as the decode kernel); every consumer warp
+// consumes every block: S = Q K^T (Q as fp16 hi + lo, K exact fp16), causal mask per row, exp2
+// online softmax, O += P V (P as hi + lo) -- fp32-accurate like the decode kernel.
+// ------------------------------------------------------------------------------------------
+constexpr int PF_CONS = 4;                  // consumer warps
+constexpr int PF_ROWS = 16 * PF_CONS;       // (token, head) rows per CTA
+constexpr int PF_STAGES = 8;
+
+template <int NREP>
+__global__ void __launch_bounds__((PF_CONS + 1) * 32, 2) paged_attn_prefill_kernel(
+    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+    const float* __restrict__ q, int n_layer, int layer, const int* __restrict__ bt, int mbs,
+    const int* __restrict__ seq_starts, const int* __restrict__ ctx, int hq, int hkv, float scale_log2,
+    float* __restrict__ out) {
+    constexpr int TQ = PF_ROWS / NREP;      // tokens per CTA
+    extern __shared__ __align__(128) uint8_t dsm[];
+    uint64_t* full = (uint64_t*)dsm;
+    uint64_t* empty = full + PF_STAGES;
+    const uint32_t dsm_s = smem_u32(dsm);
+    uint8_t* ring = dsm + ((((dsm_s + 256 + 1023) & ~1023u)) - dsm_s);
+
+    pdl_wait();
+    const int seq = blockIdx.y, kvh = blockIdx.z;
+    const int s0 = seq_starts[seq], ns = seq_starts[seq + 1] - s0;
+    const int t0 = blockIdx.x * TQ;                 // first token of the tile within the sequence
+    if (t0 >= ns) return;                           // CTA-uniform
+    const int L = ctx[seq];
+    const int pos0 = L - ns;                        // position of the sequence's first new token
+    const int tq = min(TQ, ns - t0);
+    const int last_pos = pos0 + t0 + tq - 1;
+    const int nbh = last_pos / KVB + 1;             // KV blocks this tile reads
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gid = lane >> 2, tig = lane & 3;
+
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < PF_STAGES; st++) {
+            mbar_init(&full[st], 1);
+            mbar_init(&empty[st], PF_CONS);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    bool ok = true;
+    if (warp == PF_CONS) {   // producer
+        if (lane == 0) {
+            for (int i = 0; i < nbh && ok; i++) {
+                const int st = i % PF_STAGES;
+                if (i >= PF_STAGES)
+                    ok = mbar_wait(&empty[st], (uint32_t)(((i / PF_STAGES) - 1) & 1), &g_attn_error);
+                if (!ok) break;
+                const int phys = bt[(size_t)seq * mbs + i];
+                const int slot = (phys * n_layer + layer) * KVB;
+                uint8_t* dst = ring + (size_t)st * MA_STAGE;
+                mbar_arrive_expect_tx(&full[st], MA_STAGE);
+                tma_load_4d(dst, &kmap, 0, slot, 0, kvh, &full[st]);
+                tma_load_4d(dst + 2 * MA_HALF, &vmap, 0, slot, 0, kvh, &full[st]);
+            }
+        }
+    } else {
+        // rows of this warp: r = 16 warp + gid (A rows gid) and r + 8 (A rows gid + 8);
+        // row r <-> token t0 + r / NREP, query head kvh NREP + r % NREP
+        int rpos[2];
+        const float* qrow[2];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int r = 16 * warp + gid + 8 * h;
+            const int t = t0 + r / NREP;
+            rpos[h] = t < ns ? pos0 + t : -1;      // -1: a padding row, every key masked
+            qrow[h] = q + ((size_t)(s0 + (t < ns ? t : 0)) * hq + kvh * NREP + r % NREP) * HD;
+        }
+        // Q fragments for the 8 k-steps (dims 16j ..): a0/a2 rows gid, a1/a3 rows gid + 8
+        uint32_t qh[8][4], ql[8][4];
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+#pragma unroll
+            for (int a = 0; a < 4; a++) {
+                const int h = a & 1, d = 16 * j + 8 * (a >> 1) + 2 * tig;
+                float x0 = 0.0f, x1 = 0.0f;
+                if (rpos[h] >= 0) {
+                    const float2 v = *(const float2*)(qrow[h] + d);
+                    x0 = v.x * scale_log2;
+                    x1 = v.y * scale_log2;
+                }
+                split_h2(x0, x1, qh[j][a], ql[j][a]);
+            }
+        float o[16][4];   // [dim tile n][c0, c1 (row gid), c2, c3 (row gid + 8)]
+#pragma unroll
+        for (int n = 0; n < 16; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+        float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.0f, 0.0f};
+        const uint32_t ring_s = smem_u32(ring);
+        const int mi = lane >> 3, mr = lane & 7;
+        for (int i = 0; i < nbh && ok; i++) {
+            const int st = i % PF_STAGES;
+            ok = mbar_wait(&full[st], (uint32_t)((i / PF_STAGES) & 1), &g_attn_error);
+            if (!ok) break;
+            const uint32_t kt = ring_s + (uint32_t)st * MA_STAGE, vt = kt + 2 * MA_HALF;
+            const int kb = i * KVB;   // first key of the block
+            // ---- S = Q K^T for keys kb .. kb + 15 (tiles of 8) ----
+            float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int tok = (mi >> 1) * 8 + mr, ch = 2 * j + (mi & 1);
+                uint32_t k0, k1, k2, k3;
+                ldsm_x4(swz(kt, tok, ch), k0, k1, k2, k3);
+                mma_f16(sacc[0], qh[j][0], qh[j][1], qh[j][2], qh[j][3], k0, k1);
+                mma_f16(sacc[0], ql[j][0], ql[j][1], ql[j][2], ql[j][3], k0, k1);
+                mma_f16(sacc[1], qh[j][0], qh[j][1], qh[j][2], qh[j][3], k2, k3);
+                mma_f16(sacc[1], ql[j][0], ql[j][1], ql[j][2], ql[j][3], k2, k3);
+            }
+            // lane: rows gid (c0, c1) and gid + 8 (c2, c3); keys kb + 8 tile + 2 tig + {0, 1}
+            float p[2][4];   // [tile][c]
+            float corr[2];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                float mx = -INFINITY;
+#pragma unroll
+                for (int tl = 0; tl < 2; tl++)
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+                        const int key = kb + 8 * tl + 2 * tig + e;
+                        float& v = sacc[tl][2 * h + e];
+                        if (key > rpos[h]) v = -INFINITY;
+                        mx = fmaxf(mx, v);
+                    }
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                const float mn = fmaxf(mrow[h], mx);
+                // a row that has seen no key yet (mn = -inf) keeps O = 0, l = 0
+                corr[h] = mn == -INFINITY ? 1.0f : exp2f(mrow[h] - mn);
+                float ps = 0.0f;
+#pragma unroll
+                for (int tl = 0; tl < 2; tl++)
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+                        const float v = sacc[tl][2 * h + e];
+                        const float pv = v == -INFINITY ? 0.0f : exp2f(v - mn);
+                        p[tl][2 * h + e] = pv;
+                        ps += pv;
+                    }
+                ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+                ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+                lrow[h] = lrow[h] * corr[h] + ps;
+                mrow[h] = mn;
+            }
+#pragma unroll
+            for (int n = 0; n < 16; n++) {
+                o[n][0] *= corr[0];
+                o[n][1] *= corr[0];
+                o[n][2] *= corr[1];
+                o[n][3] *= corr[1];
+            }
+            // ---- O += P V: A = P (a0: row gid keys 2tig.., a1: row gid+8, a2/a3: keys 8+2tig..) ----
+            uint32_t ph[4], pl[4];
+            split_h2(p[0][0], p[0][1], ph[0], pl[0]);
+            split_h2(p[0][2], p[0][3], ph[1], pl[1]);
+            split_h2(p[1][0], p[1][1], ph[2], pl[2]);
+            split_h2(p[1][2], p[1][3], ph[3], pl[3]);
+            // slots past the context (the last block) may hold NaN / Inf bit patterns: zero their V
+            const int nval = min(KVB, L - kb);
+            const uint32_t vm01 = (2 * tig < nval ? 0x0000FFFFu : 0u) | (2 * tig + 1 < nval ? 0xFFFF0000u : 0u);
+            const uint32_t vm23 = (8 + 2 * tig < nval ? 0x0000FFFFu : 0u) | (9 + 2 * tig < nval ? 0xFFFF0000u : 0u);
+#pragma unroll
+            for (int n2 = 0; n2 < 8; n2++) {
+                const int tok = (mi & 1) * 8 + mr, ch = 2 * n2 + (mi >> 1);
+                uint32_t v0, v1, v2, v3;
+                ldsm_x4_t(swz(vt, tok, ch), v0, v1, v2, v3);
+                if (nval < KVB) {
+                    v0 &= vm01;
+                    v2 &= vm01;
+                    v1 &= vm23;
+                    v3 &= vm23;
+                }
+                mma_f16(o[2 * n2], ph[0], ph[1], ph[2], ph[3], v0, v1);
+                mma_f16(o[2 * n2], pl[0], pl[1], pl[2], pl[3], v0, v1);
+                mma_f16(o[2 * n2 + 1], ph[0], ph[1], ph[2], ph[3], v2, v3);
+                mma_f16(o[2 * n2 + 1], pl[0], pl[1], pl[2], pl[3], v2, v3);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+        }
+        // ---- normalise and store: lane owns rows gid / gid + 8, dims 8n + 2tig, +1 ----
+        if (ok) {
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                if (rpos[h] < 0) continue;
+                const int r = 16 * warp + gid + 8 * h;
+                const float inv = lrow[h] > 0.0f ? 1.0f / lrow[h] : 0.0f;
+                float* orow = out + ((size_t)(s0 + t0 + r / NREP) * hq + kvh * NREP + r % NREP) * HD;
+#pragma unroll
+                for (int n = 0; n < 16; n++)
+                    *(float2*)(orow + 8 * n + 2 * tig) = make_float2(o[n][2 * h] * inv, o[n][2 * h + 1] * inv);
+            }
+        }
+    }
+    pdl_trigger();
+}
+
 // KV append: token i of sequence seq_ids[i] at position positions[i]; f32 -> fp16 (RNE), the
 // PagedKVCache::WriteKSlot / WriteVSlot conversion (kv_cache.cpp:566-598).
 __global__ void kv_append_kernel(const float* __restrict__ k, const float* __restrict__ v,
@@ -441,6 +650,40 @@ cudaError_t launch_kv_append(const float* k, const float* v, void* karena, void*
     if (total == 0) return cudaSuccess;
     return launch_pdl(kv_append_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, k, v,
                       (__half*)karena, (__half*)varena, n_layer, layer, bt, mbs, seq_ids, pos, n_tok, hkv, hd);
+}
+
+
+template <int NR>
+static cudaError_t launch_prefill_t(dim3 grid, cudaStream_t st, const CUtensorMap& km, const CUtensorMap& vm,
+                                    const float* q, int n_layer, int layer, const int* bt, int mbs,
+                                    const int* seq_starts, const int* ctx, int hq, int hkv, float sl2, float* out) {
+    const size_t dyn = 2048 + (size_t)PF_STAGES * MA_STAGE;
+    cudaError_t e = DCG_SMEM_ATTR((paged_attn_prefill_kernel<NR>), dyn);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(paged_attn_prefill_kernel<NR>, grid, dim3((PF_CONS + 1) * 32), dyn, st, km, vm, q, n_layer,
+                      layer, bt, mbs, seq_starts, ctx, hq, hkv, sl2, out);
+}
+
+cudaError_t launch_paged_attn_prefill(const float* q, const void* karena, const void* varena, int n_layer,
+                                      int layer, const int* bt, int mbs, const int* seq_starts, const int* ctx,
+                                      int n_seqs, int max_seq_tokens, int hq, int hkv, float scale, float* out,
+                                      cudaStream_t st, int64_t n_arena_blocks) {
+    const int nrep = hq / hkv;
+    const int tq = PF_ROWS / nrep;
+    const dim3 grid((unsigned)((max_seq_tokens + tq - 1) / tq), (unsigned)n_seqs, (unsigned)hkv);
+    const int64_t n_slots = n_arena_blocks * n_layer * KVB;
+    CUtensorMap km, vm;
+    cudaError_t e = make_kv_map(&km, karena, hkv, n_slots);
+    if (e == cudaSuccess) e = make_kv_map(&vm, varena, hkv, n_slots);
+    if (e != cudaSuccess) return e;
+    const float sl2 = scale * LOG2E;
+    switch (nrep) {
+        case 1: return launch_prefill_t<1>(grid, st, km, vm, q, n_layer, layer, bt, mbs, seq_starts, ctx, hq, hkv, sl2, out);
+        case 2: return launch_prefill_t<2>(grid, st, km, vm, q, n_layer, layer, bt, mbs, seq_starts, ctx, hq, hkv, sl2, out);
+        case 4: return launch_prefill_t<4>(grid, st, km, vm, q, n_layer, layer, bt, mbs, seq_starts, ctx, hq, hkv, sl2, out);
+        case 8: return launch_prefill_t<8>(grid, st, km, vm, q, n_layer, layer, bt, mbs, seq_starts, ctx, hq, hkv, sl2, out);
+    }
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace dcg

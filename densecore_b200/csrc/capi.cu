@@ -280,6 +280,30 @@ int dcg_paged_attn_decode(const float* q, const void* k_arena, const void* v_are
     return DCG_OK;
 }
 
+int dcg_paged_attn_prefill(const float* q, const void* k_arena, const void* v_arena, int64_t n_arena_blocks,
+                           int n_layer, int layer, const int32_t* block_tables, int max_blocks_per_seq,
+                           const int32_t* seq_starts, const int32_t* ctx_lens, int n_seqs, int max_seq_tokens,
+                           int hq, int hkv, int head_dim, int max_ctx, float scale, float* out, void* stream) {
+    if (n_seqs < 0 || max_seq_tokens < 0) return fail(DCG_EINVAL, "n_seqs and max_seq_tokens must be >= 0");
+    if (n_seqs == 0 || max_seq_tokens == 0) return DCG_OK;
+    if (!q || !k_arena || !v_arena || !block_tables || !seq_starts || !ctx_lens || !out)
+        return fail(DCG_EINVAL, "null pointer");
+    if (head_dim != 128) return fail(DCG_EINVAL, "head_dim must be 128");
+    if (hkv <= 0 || hq <= 0 || hq % hkv) return fail(DCG_EINVAL, "hq must be a multiple of hkv");
+    const int nrep = hq / hkv;
+    if (nrep != 1 && nrep != 2 && nrep != 4 && nrep != 8) return fail(DCG_EINVAL, "hq/hkv must be 1, 2, 4 or 8");
+    if (n_layer <= 0 || layer < 0 || layer >= n_layer) return fail(DCG_EINVAL, "bad layer");
+    if (n_arena_blocks <= 0) return fail(DCG_EINVAL, "n_arena_blocks must be > 0");
+    if (max_ctx < 0 || max_ctx > 16 * max_blocks_per_seq) return fail(DCG_EINVAL, "max_ctx exceeds the block table");
+    if (!aligned(k_arena, 16) || !aligned(v_arena, 16) || !aligned(q, 16) || !aligned(out, 16))
+        return fail(DCG_EINVAL, "q, out and the arenas must be 16-byte aligned");
+    DCG_CUDA(dcg::launch_paged_attn_prefill(q, k_arena, v_arena, n_layer, layer, block_tables, max_blocks_per_seq,
+                                            seq_starts, ctx_lens, n_seqs, max_seq_tokens, hq, hkv, scale, out,
+                                            (cudaStream_t)stream, n_arena_blocks),
+             "paged_attn_prefill");
+    return DCG_OK;
+}
+
 int dcg_kv_append(const float* k, const float* v, void* k_arena, void* v_arena, int n_layer,
                   int layer, const int32_t* block_tables, int max_blocks_per_seq,
                   const int32_t* seq_ids, const int32_t* positions, int n_tok, int hkv,
@@ -322,12 +346,12 @@ int dcg_swiglu_quantize(const float* gate, const float* up, int64_t ld, int64_t 
     return DCG_OK;
 }
 
-int dcg_qk_norm_rope_kv_append(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v,
+static int qk_rope_common(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v,
                                int64_t ldv, int n_seqs, int hq, int hkv, int head_dim,
                                const float* q_norm_w, const float* k_norm_w, float eps, float rope_theta,
                                const int32_t* positions, float* q_out, void* k_arena, void* v_arena,
                                int n_layer, int layer, const int32_t* block_tables,
-                               int max_blocks_per_seq, void* stream) {
+                               int max_blocks_per_seq, void* stream, const int32_t* seq_ids) {
     if (!q || !k || !v || !positions || !q_out || !k_arena || !v_arena || !block_tables)
         return fail(DCG_EINVAL, "null pointer");
     if (!q_norm_w != !k_norm_w) return fail(DCG_EINVAL, "give both QK-norm weights or neither");
@@ -337,9 +361,32 @@ int dcg_qk_norm_rope_kv_append(const float* q, int64_t ldq, const float* k, int6
     if (n_seqs == 0) return DCG_OK;
     DCG_CUDA(dcg::launch_qk_rope_append(q, ldq, k, ldk, v, ldv, n_seqs, hq, hkv, q_norm_w, k_norm_w, eps,
                                         rope_theta, positions, q_out, k_arena, v_arena, n_layer, layer,
-                                        block_tables, max_blocks_per_seq, (cudaStream_t)stream),
+                                        block_tables, max_blocks_per_seq, (cudaStream_t)stream, seq_ids),
              "qk_norm_rope_kv_append");
     return DCG_OK;
+}
+
+int dcg_qk_norm_rope_kv_append(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v,
+                               int64_t ldv, int n_seqs, int hq, int hkv, int head_dim,
+                               const float* q_norm_w, const float* k_norm_w, float eps, float rope_theta,
+                               const int32_t* positions, float* q_out, void* k_arena, void* v_arena,
+                               int n_layer, int layer, const int32_t* block_tables,
+                               int max_blocks_per_seq, void* stream) {
+    return qk_rope_common(q, ldq, k, ldk, v, ldv, n_seqs, hq, hkv, head_dim, q_norm_w, k_norm_w, eps, rope_theta,
+                          positions, q_out, k_arena, v_arena, n_layer, layer, block_tables, max_blocks_per_seq,
+                          stream, nullptr);
+}
+
+int dcg_qk_norm_rope_kv_append_tokens(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v,
+                                      int64_t ldv, int n_tok, int hq, int hkv, int head_dim,
+                                      const float* q_norm_w, const float* k_norm_w, float eps, float rope_theta,
+                                      const int32_t* seq_ids, const int32_t* positions, float* q_out,
+                                      void* k_arena, void* v_arena, int n_layer, int layer,
+                                      const int32_t* block_tables, int max_blocks_per_seq, void* stream) {
+    if (!seq_ids) return fail(DCG_EINVAL, "null pointer");
+    return qk_rope_common(q, ldq, k, ldk, v, ldv, n_tok, hq, hkv, head_dim, q_norm_w, k_norm_w, eps, rope_theta,
+                          positions, q_out, k_arena, v_arena, n_layer, layer, block_tables, max_blocks_per_seq,
+                          stream, seq_ids);
 }
 
 size_t dcg_act_size(int act_type, int64_t m, int64_t k) {

@@ -99,13 +99,14 @@ __global__ void __launch_bounds__(FUSE_THREADS) swiglu_quant_kernel(
     }
 }
 
-// one warp per (sequence, head) over hq + hkv heads; lane owns dims {2l, 2l+1, 64+2l, 65+2l}
+// one warp per (row, head) over hq + hkv heads; lane owns dims {2l, 2l+1, 64+2l, 65+2l}.  Row s is
+// one token: sequence s itself (decode), or sequence seq_ids[s] (several tokens of one sequence)
 __global__ void __launch_bounds__(FUSE_THREADS) qk_rope_append_kernel(
     const float* __restrict__ q, int64_t ldq, const float* __restrict__ k, int64_t ldk,
     const float* __restrict__ v, int64_t ldv, int n_seqs, int hq, int hkv, const float* __restrict__ qw,
     const float* __restrict__ kw, float eps, float theta, const int* __restrict__ pos,
     float* __restrict__ q_out, __half* __restrict__ karena, __half* __restrict__ varena, int n_layer,
-    int layer, const int* __restrict__ bt, int mbs) {
+    int layer, const int* __restrict__ bt, int mbs, const int* __restrict__ seq_ids) {
     constexpr int D = 128;
     pdl_wait();
     pdl_trigger();
@@ -146,7 +147,7 @@ __global__ void __launch_bounds__(FUSE_THREADS) qk_rope_append_kernel(
         return;
     }
     const int ps = pos[s];
-    const int phys = bt[(int64_t)s * mbs + ps / 16];
+    const int phys = bt[(int64_t)(seq_ids ? seq_ids[s] : s) * mbs + ps / 16];   // row s's sequence
     const size_t slot = (((size_t)phys * n_layer + layer) * 16 + (ps % 16)) * (size_t)hkv * D + (size_t)hh * D;
     *(__half2*)(karena + slot + d0) = __floats2half2_rn(r0, r1);
     *(__half2*)(karena + slot + d1) = __floats2half2_rn(r2, r3);
@@ -174,12 +175,12 @@ cudaError_t launch_qk_rope_append(const float* q, int64_t ldq, const float* k, i
                                   int64_t ldv, int n_seqs, int hq, int hkv, const float* qw, const float* kw,
                                   float eps, float theta, const int* pos, float* q_out, void* karena,
                                   void* varena, int n_layer, int layer, const int* bt, int mbs,
-                                  cudaStream_t st) {
+                                  cudaStream_t st, const int* seq_ids) {
     const int64_t warps = (int64_t)n_seqs * (hq + hkv);
     const unsigned grid = (unsigned)((warps * 32 + FUSE_THREADS - 1) / FUSE_THREADS);
     return launch_pdl(qk_rope_append_kernel, dim3(grid), dim3(FUSE_THREADS), 0, st, q, ldq, k, ldk, v, ldv,
                       n_seqs, hq, hkv, qw, kw, eps, theta, pos, q_out, (__half*)karena, (__half*)varena,
-                      n_layer, layer, bt, mbs);
+                      n_layer, layer, bt, mbs, seq_ids);
 }
 
 }  // namespace dcg

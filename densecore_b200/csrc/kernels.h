@@ -66,6 +66,11 @@ cudaError_t launch_paged_attn(const float* q, const void* karena, const void* va
                               int layer, const int* bt, int mbs, const int* ctx, int n_seqs, int hq,
                               int hkv, int max_ctx, float scale, float* out, void* scratch,
                               cudaStream_t st, int64_t n_arena_blocks);
+// multi-token causal attention (prefill / prompt chunks) over the paged cache (attn.cu)
+cudaError_t launch_paged_attn_prefill(const float* q, const void* karena, const void* varena, int n_layer,
+                                      int layer, const int* bt, int mbs, const int* seq_starts, const int* ctx,
+                                      int n_seqs, int max_seq_tokens, int hq, int hkv, float scale, float* out,
+                                      cudaStream_t st, int64_t n_arena_blocks);
 cudaError_t launch_kv_append(const float* k, const float* v, void* karena, void* varena, int n_layer,
                              int layer, const int* bt, int mbs, const int* seq_ids, const int* pos,
                              int n_tok, int hkv, int hd, cudaStream_t st);
@@ -79,7 +84,7 @@ cudaError_t launch_qk_rope_append(const float* q, int64_t ldq, const float* k, i
                                   int64_t ldv, int n_seqs, int hq, int hkv, const float* qw, const float* kw,
                                   float eps, float theta, const int* pos, float* q_out, void* karena,
                                   void* varena, int n_layer, int layer, const int* bt, int mbs,
-                                  cudaStream_t st);
+                                  cudaStream_t st, const int* seq_ids = nullptr);
 
 // error flag of the bounded waits of the GEMV kernels (0 = none); optionally cleared
 cudaError_t gemv_device_error(int* out, bool clear);

@@ -189,6 +189,34 @@ def paged_attn_decode(q: torch.Tensor, k_arena: torch.Tensor, v_arena: torch.Ten
     return out
 
 
+def paged_attn_prefill(q: torch.Tensor, k_arena: torch.Tensor, v_arena: torch.Tensor, n_layer: int,
+                       layer: int, block_tables: torch.Tensor, seq_starts: torch.Tensor, ctx_lens: torch.Tensor,
+                       hkv: int, max_seq_tokens: int, max_ctx: int, scale: float | None = None,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal attention of several new tokens per sequence over the paged fp16 KV arena.
+
+    q [n_tok, hq, 128] f32, sequence s's tokens are rows seq_starts[s] .. seq_starts[s+1]-1
+    (seq_starts [n_seqs + 1] int32); its i-th new token sits at position ctx_lens[s] - n_s + i
+    (K/V already appended) and attends to keys 0 .. that position."""
+    _check_cuda(q, "q", torch.float32)
+    for t, nm in ((k_arena, "k_arena"), (v_arena, "v_arena")):
+        _check_cuda(t, nm, torch.float16)
+    for t, nm in ((block_tables, "block_tables"), (seq_starts, "seq_starts"), (ctx_lens, "ctx_lens")):
+        _check_cuda(t, nm, torch.int32)
+    n_tok, hq, hd = q.shape
+    n_seqs = seq_starts.numel() - 1
+    if scale is None:
+        scale = 1.0 / float(hd) ** 0.5
+    if out is None:
+        out = torch.empty_like(q)
+    n_arena_blocks = k_arena.numel() // (16 * hkv * hd * n_layer)
+    _lib.check(_lib.load().dcg_paged_attn_prefill(
+        _ptr(q), _ptr(k_arena), _ptr(v_arena), n_arena_blocks, n_layer, layer, _ptr(block_tables),
+        block_tables.shape[1], _ptr(seq_starts), _ptr(ctx_lens), n_seqs, max_seq_tokens, hq, hkv, hd, max_ctx,
+        scale, _ptr(out), _stream()), "dcg_paged_attn_prefill")
+    return out
+
+
 def kv_append(k: torch.Tensor, v: torch.Tensor, k_arena: torch.Tensor, v_arena: torch.Tensor,
               n_layer: int, layer: int, block_tables: torch.Tensor, seq_ids: torch.Tensor,
               positions: torch.Tensor) -> None:
@@ -229,6 +257,17 @@ def qk_norm_rope_kv_append(q, ldq, k, ldk, v, ldv, n_seqs, hq, hkv, q_norm_w, k_
         _ptr(k_norm_w) if k_norm_w is not None else None,
         eps, theta, _ptr(positions), _ptr(q_out), _ptr(k_arena), _ptr(v_arena), n_layer, layer,
         _ptr(block_tables), block_tables.shape[1], _stream()), "dcg_qk_norm_rope_kv_append")
+
+
+def qk_norm_rope_kv_append_tokens(q, ldq, k, ldk, v, ldv, n_tok, hq, hkv, q_norm_w, k_norm_w, eps, theta,
+                                  seq_ids, positions, q_out, k_arena, v_arena, n_layer, layer, block_tables):
+    """qk_norm_rope_kv_append for token rows of any sequences (row i: sequence seq_ids[i])."""
+    _lib.check(_lib.load().dcg_qk_norm_rope_kv_append_tokens(
+        _ptr(q), ldq, _ptr(k), ldk, _ptr(v), ldv, n_tok, hq, hkv, 128,
+        _ptr(q_norm_w) if q_norm_w is not None else None,
+        _ptr(k_norm_w) if k_norm_w is not None else None,
+        eps, theta, _ptr(seq_ids), _ptr(positions), _ptr(q_out), _ptr(k_arena), _ptr(v_arena), n_layer, layer,
+        _ptr(block_tables), block_tables.shape[1], _stream()), "dcg_qk_norm_rope_kv_append_tokens")
 
 
 class HostContext:

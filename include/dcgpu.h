@@ -156,6 +156,19 @@ int dcg_paged_attn_decode(const float* q, const void* k_arena, const void* v_are
                           int max_ctx, float scale, float* out, void* scratch, size_t scratch_bytes,
                           void* stream);
 
+/* Multi-token causal attention over the same cache: the prefill / prompt-chunk branch of the
+ * attention selector (the flash path with its host-built causal mask, inference.cpp:1519-1573 and
+ * :1538-1558 -- query i of N new tokens sees keys 0 .. n_past + i -- and the tiled path's
+ * diag_mask_inf, :1590-1711), made per sequence.  Sequence s's new tokens are rows
+ * seq_starts[s] .. seq_starts[s+1]-1 of q / out ([n_tok][hq][head_dim] f32); token i of its n_s
+ * new tokens sits at position ctx_lens[s] - n_s + i, its K/V already appended, and attends to keys
+ * 0 .. that position.  max_seq_tokens >= every n_s.  seq_starts and ctx_lens are device int32
+ * arrays; the rest as dcg_paged_attn_decode.  Needs no scratch. */
+int dcg_paged_attn_prefill(const float* q, const void* k_arena, const void* v_arena, int64_t n_arena_blocks,
+                           int n_layer, int layer, const int32_t* block_tables, int max_blocks_per_seq,
+                           const int32_t* seq_starts, const int32_t* ctx_lens, int n_seqs, int max_seq_tokens,
+                           int hq, int hkv, int head_dim, int max_ctx, float scale, float* out, void* stream);
+
 /* KV append -- PagedKVCache::WriteKSlot / WriteVSlot (kv_cache.cpp:566-598) for n_tok tokens at
  * once: token i (k, v: [n_tok][hkv][head_dim] f32) goes to slot positions[i] of sequence
  * seq_ids[i] through its block table, converted to fp16 (round to nearest even). */
@@ -179,6 +192,14 @@ int dcg_kv_append(const float* k, const float* v, void* k_arena, void* v_arena, 
  *   NeoX (rotate-half) RoPE at positions[s] with base rope_theta; q goes to q_out[n_seqs][hq][128],
  *   k and v (row stride ldv) are written as fp16 to slot positions[s] of sequence s (the
  *   dcg_kv_append layout). */
+/* dcg_qk_norm_rope_kv_append for n_tok token rows of any sequences: row i is a token of sequence
+ * seq_ids[i] at positions[i] (several rows may share a sequence: a prompt chunk). */
+int dcg_qk_norm_rope_kv_append_tokens(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v,
+                                      int64_t ldv, int n_tok, int hq, int hkv, int head_dim,
+                                      const float* q_norm_w, const float* k_norm_w, float eps, float rope_theta,
+                                      const int32_t* seq_ids, const int32_t* positions, float* q_out,
+                                      void* k_arena, void* v_arena, int n_layer, int layer,
+                                      const int32_t* block_tables, int max_blocks_per_seq, void* stream);
 int dcg_add_rmsnorm_quantize(float* x, const float* delta, const float* weight, float eps, int64_t m,
                              int64_t k, int act_type, void* act, void* stream);
 int dcg_swiglu_quantize(const float* gate, const float* up, int64_t ld, int64_t m, int64_t ffn,

@@ -197,6 +197,24 @@ def kv_append(k, v, k_arena, v_arena, n_layer, layer, block_tables, seq_ids, pos
                         _p(np.ascontiguousarray(positions, dtype=np.int32)), n_tok, hkv, d)
 
 
+def paged_attn_prefill(q, k_arena, v_arena, n_layer, layer, block_tables, seq_starts, ctx_lens, hkv,
+                       scale, nthreads=1):
+    """Causal multi-token attention: sequence s's new tokens are rows seq_starts[s] ..
+    seq_starts[s+1]-1 of q; token i of its n_s sits at position ctx_lens[s] - n_s + i and attends to
+    keys 0 .. that position -- which is decode attention of that token with a context of
+    position + 1 keys (inference.cpp:1538-1558 mask semantics, per sequence)."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    bt = np.asarray(block_tables, dtype=np.int32)
+    rows_bt, ctx_tok = [], []
+    for s in range(len(seq_starts) - 1):
+        n_s = int(seq_starts[s + 1] - seq_starts[s])
+        for i in range(n_s):
+            rows_bt.append(bt[s])
+            ctx_tok.append(int(ctx_lens[s]) - n_s + i + 1)
+    return paged_attn_decode(q, k_arena, v_arena, n_layer, layer, np.stack(rows_bt),
+                             np.array(ctx_tok, np.int32), hkv, scale, nthreads)
+
+
 def ref_flash_attention_gqa(Q, K, V, scale, causal=False):
     """DenseCore FlashAttentionGQA on dense [B,H,S,D] f32 arrays (None if not built)."""
     R = ref_lib()

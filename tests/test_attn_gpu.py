@@ -129,3 +129,41 @@ def test_attention_ignores_slots_past_the_context(ops):
     assert np.isfinite(out).all()
     err = np.linalg.norm(out - ref, axis=-1) / (np.linalg.norm(ref, axis=-1) + 1e-30)
     assert err.max() < ATOL_REL
+
+
+def check_prefill(ops, ctx, ntok, hq, hkv, n_layer=2, layer=1, seed=0, nan_tail=False):
+    """New tokens per sequence (ntok[s] of them, the last at position ctx[s] - 1) against the
+    oracle's per-token causal attention."""
+    rng = np.random.default_rng(seed)
+    ka, va, bt = make_cache(rng, ctx, hkv, n_layer)
+    if nan_tail:   # slots past each context hold NaN / Inf bit patterns
+        for s, c in enumerate(ctx):
+            if c % 16:
+                blk = bt[s, c // 16]
+                ka[blk * n_layer + layer, c % 16:] = np.float16(np.nan)
+                va[blk * n_layer + layer, c % 16:] = np.float16(np.inf)
+    starts = np.concatenate([[0], np.cumsum(ntok)]).astype(np.int32)
+    q = rng.standard_normal((int(starts[-1]), hq, 128)).astype(np.float32)
+    scale = 1.0 / np.sqrt(128.0)
+    ref = O.paged_attn_prefill(q, ka, va, n_layer, layer, bt, starts, np.array(ctx), hkv, scale, nthreads=8)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    out = ops.paged_attn_prefill(dev(q), dev(ka), dev(va), n_layer, layer, dev(bt), dev(starts),
+                                 dev(np.array(ctx, np.int32)), hkv, int(max(ntok)), max(ctx)).cpu().numpy()
+    err = np.linalg.norm(out - ref, axis=-1) / (np.linalg.norm(ref, axis=-1) + 1e-30)
+    assert np.isfinite(out).all()
+    assert err.max() < ATOL_REL, f"max rel err {err.max():.2e}"
+
+
+@pytest.mark.parametrize("hq,hkv", [(8, 8), (16, 8), (32, 8), (64, 8)])
+def test_prefill_ragged_sequences(ops, hq, hkv):
+    """Whole prompts (ctx == ntok), prompt chunks after history (ctx > ntok), one-token rows."""
+    check_prefill(ops, [1, 17, 40, 100, 300], [1, 17, 9, 100, 33], hq, hkv)
+
+
+def test_prefill_ignores_slots_past_the_context(ops):
+    check_prefill(ops, [5, 21, 70], [5, 3, 70], 32, 8, nan_tail=True)
+
+
+def test_prefill_2048_tokens(ops):
+    """Config-4 prefill shape: a 2048-token prompt, 32 Q / 8 KV heads."""
+    check_prefill(ops, [2048], [2048], 32, 8, n_layer=1, layer=0)

@@ -135,3 +135,31 @@ def test_simd_q4_K_dot_is_bit_identical(isa):
         a = O.mul_mat(O.Q4_K, wq, k, xq, m, nthreads=3)
         b = O.mul_mat(O.Q4_K, wq, k, xq, m, nthreads=3, simd=isa)
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_oracle_prefill_matches_reference_causal_flash_attention():
+    """Prefill semantics pinned to DenseCore's own FlashAttentionGQA with causal = true
+    (core/include/flash_attention.h:239-272): N new tokens from position 0 over a paged arena equal
+    the reference's causal attention over the dense fp16-valued K/V (Sq = Skv = N)."""
+    rng = np.random.default_rng(31)
+    B, hq, hkv, N, d = 2, 8, 2, 37, 128
+    Q = rng.standard_normal((B, hq, N, d)).astype(np.float32)
+    K = rng.standard_normal((B, hkv, N, d)).astype(np.float16).astype(np.float32)
+    V = rng.standard_normal((B, hkv, N, d)).astype(np.float16).astype(np.float32)
+    scale = 1.0 / np.sqrt(d)
+    ref = O.ref_flash_attention_gqa(Q, K, V, scale, causal=True)
+    if ref is None:
+        pytest.skip("reference FlashAttentionGQA not built here")
+    nblk = (N + 15) // 16
+    bt = np.arange(B * nblk, dtype=np.int32)[::-1].reshape(B, nblk).copy()
+    ka = np.zeros((B * nblk, 16, hkv, d), np.float16)
+    va = np.zeros_like(ka)
+    for s in range(B):
+        for t in range(N):
+            ka[bt[s, t // 16], t % 16] = K[s, :, t].astype(np.float16)
+            va[bt[s, t // 16], t % 16] = V[s, :, t].astype(np.float16)
+    q = np.ascontiguousarray(Q.transpose(0, 2, 1, 3).reshape(B * N, hq, d))
+    got = O.paged_attn_prefill(q, ka, va, 1, 0, bt, np.array([0, N, 2 * N]), np.array([N, N]), hkv, scale)
+    want = ref.transpose(0, 2, 1, 3).reshape(B * N, hq, d)
+    err = np.linalg.norm(got - want, axis=-1) / np.linalg.norm(want, axis=-1)
+    assert err.max() < 1e-5, err.max()
