@@ -4,9 +4,11 @@ worker (core/src/worker.cpp:365-544: admit, build the batch, compute, sample, re
 per-sequence semantics the reference's batched path lacks -- every sequence reads only its own
 positions through its own block table, so its tokens do not depend on what else is in the batch.
 
-Prompts are fed one token per step through the same decode graph (a prompt token's logits are
-discarded); the first generated token comes from the last prompt token.  Sampling is greedy.
-Idle slots point at one reserved block and run a harmless one-token step.
+A newly admitted request's whole prompt is ingested by one prefill pass (Decoder.prefill: every
+matmul at M = prompt tokens, multi-token causal attention), batched over the requests admitted in
+the same step; its last token's logits give the first generated token.  With prefill=False prompts
+are instead fed one token per step through the decode graph.  Sampling is greedy.  Idle slots
+point at one reserved block and run a harmless one-token step.
 """
 from __future__ import annotations
 
@@ -64,8 +66,9 @@ class Request:
 class ContinuousBatcher:
     """Runs requests through `dec` (its batch size is the slot count)."""
 
-    def __init__(self, dec: Decoder):
+    def __init__(self, dec: Decoder, prefill: bool = True):
         self.dec = dec
+        self.use_prefill = prefill
         self.slots: list[Request | None] = [None] * dec.batch
         self.alloc = BlockAllocator(dec.n_blocks)
         self.idle_block = self.alloc.alloc(1)[0]   # where idle slots write their throw-away token
@@ -86,24 +89,44 @@ class ContinuousBatcher:
         self.queue.append(r)
         return r
 
-    def _admit(self):
+    def _admit(self) -> list[Request]:
+        new = []
         for s in range(len(self.slots)):
             if self.slots[s] is not None or not self.queue:
                 continue
             r = self.queue[0]
             blocks = self.alloc.alloc((r.capacity + KV_BLOCK - 1) // KV_BLOCK)
             if blocks is None:
-                return                      # wait for blocks to be released (FIFO admission)
+                break                       # wait for blocks to be released (FIFO admission)
             self.queue.popleft()
             r.slot, r.blocks = s, blocks
             self.slots[s] = r
             self._bt[s].fill_(self.idle_block)
             self._bt[s, :len(blocks)] = torch.tensor(blocks, dtype=torch.int32)
+            new.append(r)
+        return new
+
+    def _retire(self, s: int, r: Request):
+        self.alloc.release(r.blocks)
+        r.blocks, r.slot = [], -1
+        self.slots[s] = None
+        # the idle slot's throw-away writes must not land in blocks that now belong to others
+        self._bt[s].fill_(self.idle_block)
+        self.finished.append(r)
 
     def step(self) -> bool:
-        """Admit waiting requests, run one decode step for every slot, retire finished requests.
-        Returns False when there is nothing left to do."""
-        self._admit()
+        """Admit waiting requests (prefilling their prompts), run one decode step for every slot,
+        retire finished requests.  Returns False when there is nothing left to do."""
+        new = self._admit()
+        dec = self.dec
+        dec.block_tables.copy_(self._bt, non_blocking=False)
+        if new and self.use_prefill:
+            nxt, _ = dec.prefill([r.slot for r in new], [r.prompt for r in new])
+            for r, t in zip(new, nxt.tolist()):
+                r.pos = len(r.prompt)
+                r.out.append(int(t))
+                if r.done():
+                    self._retire(r.slot, r)
         active = [r for r in self.slots if r is not None]
         if not active:
             return bool(self.queue)
@@ -112,8 +135,6 @@ class ContinuousBatcher:
                 self._tok[s], self._ctx[s] = 0, 1
             else:
                 self._tok[s], self._ctx[s] = r.next_input(), r.pos + 1
-        dec = self.dec
-        dec.block_tables.copy_(self._bt, non_blocking=False)
         dec.tokens.copy_(self._tok)
         dec.ctx_lens.copy_(self._ctx)
         dec.replay()
@@ -125,10 +146,7 @@ class ContinuousBatcher:
             if r.pos >= len(r.prompt):      # the last prompt token and every generated one predict
                 r.out.append(int(nxt[s]))
             if r.done():
-                self.alloc.release(r.blocks)
-                r.blocks, r.slot = [], -1
-                self.slots[s] = None
-                self.finished.append(r)
+                self._retire(s, r)
         return True
 
     def run(self, max_steps: int = 1 << 30) -> list[Request]:

@@ -449,6 +449,105 @@ class Decoder:
             self.logits.copy_(self.gathered.permute(1, 0, 2).reshape(B, -1))
         self.next_tokens.copy_(torch.argmax(self.logits, dim=-1))
 
+    def prefill(self, seqs, prompts, start=None):
+        """Ingest a prompt chunk for each of the sequences `seqs` (batch slots, whose block-table
+        rows are already set) in one pass: every matmul runs with M = all chunk tokens, attention is
+        the multi-token causal kernel.  prompts[i] are the tokens of sequence seqs[i] at positions
+        start[i] .. start[i] + len - 1 (start: default 0, a whole prompt).  Their K/V are written to
+        the cache; returns (next_tokens [len(seqs)] long, logits [len(seqs), vocab]) for each chunk's
+        last token.  Runs eagerly (its shapes change from call to call); with tensor parallelism the
+        same two all-reduces per layer and the logits all-gather run in plain stream order."""
+        if self.tp_size == 1:
+            return self._prefill(seqs, prompts, start)
+        lib = ops._lib.load()
+        prev = lib.dcg_set_programmatic_launch(0)
+        try:
+            return self._prefill(seqs, prompts, start)
+        finally:
+            lib.dcg_set_programmatic_launch(prev)
+
+    def _prefill(self, seqs, prompts, start):
+        cfg, dev = self.cfg, self.device
+        D, hq, hkv, H, ffn = cfg.head_dim, self.hq, self.hkv, cfg.hidden, self.ffn
+        qd, kvd = hq * D, hkv * D
+        S = len(seqs)
+        n_s = [len(p) for p in prompts]
+        if S == 0 or min(n_s) < 1:
+            raise ValueError("every sequence needs at least one token")
+        start = list(start) if start is not None else [0] * S
+        T = sum(n_s)
+        i32 = torch.int32
+        tokens = torch.tensor([t for p in prompts for t in p], dtype=torch.long, device=dev)
+        local_seq = torch.tensor([i for i, n in enumerate(n_s) for _ in range(n)], dtype=i32, device=dev)
+        positions = torch.tensor([start[i] + j for i, n in enumerate(n_s) for j in range(n)], dtype=i32,
+                                 device=dev)
+        seq_starts = torch.tensor([0] + list(np.cumsum(n_s)), dtype=i32, device=dev)
+        ctx = torch.tensor([start[i] + n_s[i] for i in range(S)], dtype=i32, device=dev)
+        if int(ctx.max()) > self.max_ctx:
+            raise ValueError("prompt chunk runs past max_ctx")
+        bt = self.block_tables[torch.tensor(list(seqs), dtype=torch.long, device=dev)].contiguous()
+        scale = 1.0 / math.sqrt(D)
+        x = self.tok_embd[tokens].float()
+        q_rot = torch.empty((T, hq, D), device=dev)
+        attn_out = torch.empty((T, hq, D), device=dev)
+
+        def actbuf(k, wtype):
+            at = VEC_DOT_TYPE[wtype]
+            return torch.empty(int(ops._lib.load().dcg_act_size(at, T, k)), dtype=torch.uint8, device=dev)
+
+        def mm(w, act, m):
+            scr = torch.zeros(max(1, ops.mul_mat_q_scratch_size(w.qtype, w.n, w.k, m)), dtype=torch.uint8,
+                              device=dev)
+            return ops.mul_mat_q(w, act, m, scratch=scr)
+
+        delta = None
+        for li, L in enumerate(self.layers):
+            wqk = L["attn_qk"] if L["qkv_split"] else L["attn_qkv"]
+            act = actbuf(H, wqk.qtype)
+            ops.add_rmsnorm_quantize(x, L["attn_norm"], cfg.rms_eps, VEC_DOT_TYPE[wqk.qtype], act, delta)
+            yqk = mm(wqk, act, T)
+            if L["qkv_split"]:
+                wv = L["attn_v"]
+                act_v = act
+                if VEC_DOT_TYPE[wv.qtype] != VEC_DOT_TYPE[wqk.qtype]:
+                    act_v = actbuf(H, wv.qtype)
+                    ops.add_rmsnorm_quantize(x, L["attn_norm"], cfg.rms_eps, VEC_DOT_TYPE[wv.qtype], act_v)
+                yv, ldv = mm(wv, act_v, T), kvd
+            else:
+                yv, ldv = yqk[:, qd + kvd:], wqk.n
+            ops.qk_norm_rope_kv_append_tokens(yqk, wqk.n, yqk[:, qd:], wqk.n, yv, ldv, T, hq, hkv,
+                                              L["attn_q_norm"], L["attn_k_norm"], cfg.rms_eps, cfg.rope_theta,
+                                              local_seq, positions, q_rot, self.k_arena, self.v_arena,
+                                              cfg.n_layer, li, bt)
+            ops.paged_attn_prefill(q_rot, self.k_arena, self.v_arena, cfg.n_layer, li, bt, seq_starts, ctx, hkv,
+                                   max(n_s), self.max_ctx, scale, out=attn_out)
+            wo = L["attn_output"]
+            act_o = actbuf(qd, wo.qtype)
+            ops.quantize_act(attn_out.view(T, qd), VEC_DOT_TYPE[wo.qtype], out=act_o)
+            yo = self._allreduce(mm(wo, act_o, T))
+            wgu = L["ffn_gate_up"]
+            act_f = actbuf(H, wgu.qtype)
+            ops.add_rmsnorm_quantize(x, L["ffn_norm"], cfg.rms_eps, VEC_DOT_TYPE[wgu.qtype], act_f, yo)
+            ygu = mm(wgu, act_f, T)
+            wd = L["ffn_down"]
+            act_d = actbuf(ffn, wd.qtype)
+            ops.swiglu_quantize(ygu, ygu[:, ffn:], 2 * ffn, T, ffn, VEC_DOT_TYPE[wd.qtype], act_d)
+            delta = self._allreduce(mm(wd, act_d, T))
+        x += delta
+        last = x[(seq_starts[1:] - 1).long()].contiguous()
+        at = VEC_DOT_TYPE[self.output.qtype]
+        act_h = torch.empty(int(ops._lib.load().dcg_act_size(at, S, H)), dtype=torch.uint8, device=dev)
+        ops.add_rmsnorm_quantize(last, self.output_norm, cfg.rms_eps, at, act_h)
+        logits_r = mm(self.output, act_h, S)
+        if self.tp_size == 1:
+            logits = logits_r
+        else:
+            import torch.distributed as dist
+            gathered = torch.empty((self.tp_size, S, self.vocab_r), device=dev)
+            dist.all_gather_into_tensor(gathered, logits_r.contiguous(), group=self.tp_group)
+            logits = gathered.permute(1, 0, 2).reshape(S, -1)
+        return torch.argmax(logits, dim=-1), logits
+
     def _allreduce(self, y):
         """Sum the K-split partial outputs of attn_output / ffn_down over the tensor-parallel group."""
         if self.tp_size > 1:

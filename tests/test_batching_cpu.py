@@ -48,22 +48,38 @@ class FakeDecoder:
         self.cache = {}                       # (block, slot) -> token written there
         self.steps = 0
 
+    def _next(self, s, pos):
+        hist = [self.cache[(int(self.block_tables[s, p // 16]), p % 16)] for p in range(pos + 1)]
+        return (sum((i + 1) * t for i, t in enumerate(hist)) * 31 + 7) % 1000
+
     def replay(self):
         self.steps += 1
         for s in range(self.batch):
             pos = int(self.ctx_lens[s]) - 1
             blk = int(self.block_tables[s, pos // 16])
             self.cache[(blk, pos % 16)] = int(self.tokens[s])
-            hist = [self.cache[(int(self.block_tables[s, p // 16]), p % 16)] for p in range(pos + 1)]
-            self.next_tokens[s] = (sum((i + 1) * t for i, t in enumerate(hist)) * 31 + 7) % 1000
+            self.next_tokens[s] = self._next(s, pos)
+
+    def prefill(self, seqs, prompts, start=None):
+        import torch
+        self.prefills = getattr(self, "prefills", 0) + 1
+        out = []
+        for i, (s, p) in enumerate(zip(seqs, prompts)):
+            p0 = start[i] if start else 0
+            for j, t in enumerate(p):
+                pos = p0 + j
+                self.cache[(int(self.block_tables[s, pos // 16]), pos % 16)] = int(t)
+            out.append(self._next(s, p0 + len(p) - 1))
+        return torch.tensor(out), None
 
 
-def test_batched_equals_alone_with_fake_decoder():
+@pytest.mark.parametrize("prefill", [True, False])
+def test_batched_equals_alone_with_fake_decoder(prefill):
     from densecore_b200.batching import ContinuousBatcher
     reqs = [([3, 1, 4], 5), ([1], 9), ([5, 9, 2, 6, 5, 3, 5], 4), ([8, 9], 20), ([7], 1)]
 
     def run(batch, items, n_blocks=None):
-        b = ContinuousBatcher(FakeDecoder(batch, 48, n_blocks))
+        b = ContinuousBatcher(FakeDecoder(batch, 48, n_blocks), prefill=prefill)
         hs = [b.submit(p, n) for p, n in items]
         b.run()
         assert all(h.done() for h in hs) and not b.queue
@@ -71,6 +87,11 @@ def test_batched_equals_alone_with_fake_decoder():
         return [h.out for h in hs], b.dec.steps
 
     alone = [run(1, [r])[0][0] for r in reqs]
+    if prefill:   # prompt ingestion in one pass gives the tokens of token-by-token feeding
+        b = ContinuousBatcher(FakeDecoder(1, 48), prefill=False)
+        hs = [b.submit(p, n) for p, n in reqs]
+        b.run()
+        assert [h.out for h in hs] == alone
     together, steps = run(2, reqs)
     assert together == alone
     assert [len(o) for o in together] == [n for _, n in reqs]
