@@ -64,14 +64,14 @@ static int qmm_tickets(int type, int64_t n, int64_t k, int64_t m) {
     return dcg::qmm_supports(type) ? dcg::qmm_ticket_count(type, n, m) : 0;
 }
 
-// M = 1 kernel choice: the streaming mat-vec (gemv_m1.cu) unless DCG_M1_KERNEL=legacy selects the
-// earlier per-type kernels (kept for side-by-side measurement)
+// M = 1 kernel choice: the per-type kernels (qmm.cu, gemv.cu); DCG_M1_KERNEL=stream selects the
+// streaming mat-vec (gemv_m1.cu) instead, for side-by-side measurement
 static bool use_m1s(int type, int64_t n, int64_t k, int64_t m) {
-    static const bool legacy = [] {
+    static const bool stream = [] {
         const char* e = getenv("DCG_M1_KERNEL");
-        return e && strcmp(e, "legacy") == 0;
+        return e && strcmp(e, "stream") == 0;
     }();
-    return m == 1 && !legacy && dcg::m1s_supports(type, n, k);
+    return m == 1 && stream && dcg::m1s_supports(type, n, k);
 }
 
 static int enqueue_mul_mat_q(int type, const void* w, int64_t n, int64_t k, const void* act, int64_t m,

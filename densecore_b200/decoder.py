@@ -559,17 +559,27 @@ class Decoder:
         at = VEC_DOT_TYPE[wtype]
         return self._buf(("act", key, at, k), (int(ops._lib.load().dcg_act_size(at, m, k)),), torch.uint8)
 
-    def capture(self):
-        """Capture step() into a CUDA graph (buffers are static)."""
+    def capture(self, advance: bool = False):
+        """Capture step() into a CUDA graph (buffers are static).  advance: the graph also feeds
+        each sequence's next token back as its input and grows every context by one, so
+        consecutive replays decode consecutive positions (greedy generation without the host)."""
+        def body():
+            self.step()
+            if advance:
+                self.tokens.copy_(self.next_tokens)
+                self.ctx_lens.add_(1)
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream())
+        saved = (self.tokens.clone(), self.ctx_lens.clone())
         with torch.cuda.stream(s):
-            self.step()  # allocates every scratch buffer outside the capture
+            body()  # allocates every scratch buffer outside the capture
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
+        self.tokens.copy_(saved[0])
+        self.ctx_lens.copy_(saved[1])
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            self.step()
+            body()
         return self.graph
 
     def replay(self):
