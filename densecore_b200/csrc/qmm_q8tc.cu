@@ -15,6 +15,9 @@
 //   warp 0      TMA: weight tile (two 128 x 128 B swizzled boxes) + its 128 x 8 block scales
 //   warp 1      TMA: activation tile (two N x 128 B swizzled boxes) + its N x 8 block scales
 //   warp 2      MMA issue: per accumulator group of BPB blocks, one MMA per block into its region
+//   warp 3      widens each activation stage's fp16 block scales into a float table of (dx, -dx B)
+//               pairs, B = 1.5 * 2^23, so the epilogue turns a dot into dx * dot with one integer
+//               add and one fma: fma(dx, float_bits(0x4B400000 + dot), -dx B) = dx * dot, rounded once
 //   warps 4-19  epilogue: thread (row, column quarter) drains its rows of each group
 // A stage is released when its MMAs have completed and the epilogue has read its scales.
 #include <cuda.h>
@@ -49,7 +52,8 @@ template <int N>
 struct Q8tCfg {
     static constexpr int AHALF = N * 128;                                    // swizzled K half
     static constexpr int ASC = (N * 16 + 1023) / 1024 * 1024;                // N x 8 fp16 scales
-    static constexpr int ASTAGE = 2 * AHALF + ASC;
+    static constexpr int ATAB = 8 * N * 8;                                   // [8 blocks][N] (dx, -dx 1.5 2^23)
+    static constexpr int ASTAGE = 2 * AHALF + ASC + ATAB;
     static constexpr int AS = N >= 128 ? 2 : (N >= 64 ? 3 : 4);
     static constexpr int OFF_ACT = 1024;
     static constexpr int OFF_W = OFF_ACT + AS * ASTAGE;
@@ -81,7 +85,8 @@ __global__ void __launch_bounds__(Q8T_THREADS, 1)
     uint64_t* w_empty = w_full + WS;          // [WS] MMA commit + 16 epilogue warps
     uint64_t* a_full = w_empty + WS;          // [AS] tx
     uint64_t* a_empty = a_full + AS;          // [AS] MMA commit + 16 epilogue warps
-    uint64_t* acc_full = a_empty + AS;        // [2] commit
+    uint64_t* a_tab = a_empty + AS;           // [AS] scale table written (32 lanes of warp 3)
+    uint64_t* acc_full = a_tab + AS;          // [2] commit
     uint64_t* acc_empty = acc_full + 2;       // [2] 16 epilogue warps
     uint64_t* mma_done = acc_empty + 2;
     uint32_t* tmem_slot = (uint32_t*)(mma_done + 1);
@@ -102,6 +107,7 @@ __global__ void __launch_bounds__(Q8T_THREADS, 1)
         for (int s = 0; s < AS; s++) {
             mbar_init(&a_full[s], 1);
             mbar_init(&a_empty[s], 17);
+            mbar_init(&a_tab[s], 32);
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&acc_full[b], 1);
@@ -155,6 +161,23 @@ __global__ void __launch_bounds__(Q8T_THREADS, 1)
                 tma_load_2d(d + 2 * C::AHALF, &admap, s * 8, c0, &a_full[st]);
             }
         }
+    } else if (warp == 3) {
+        // ---------------- activation scale table ----------------
+        pdl_wait();
+        for (int i = 0; i < nu && ok; i++) {
+            const int st = i % AS;
+            ok = __all_sync(0xffffffffu, mbar_wait(&a_full[st], (uint32_t)((i / AS) & 1), &g_q8tc_error));
+            if (!ok) break;
+            const uint8_t* d = act + (size_t)st * C::ASTAGE;
+            const __half* dxh = (const __half*)(d + 2 * C::AHALF);       // [N][8]
+            float2* tab = (float2*)(d + 2 * C::AHALF + C::ASC);           // [8][N]
+            for (int e = lane; e < N * 8; e += 32) {
+                const int c = e >> 3, j = e & 7;
+                const float dx = __half2float(dxh[e]);
+                tab[j * N + c] = make_float2(dx, -dx * 12582912.0f);
+            }
+            mbar_arrive(&a_tab[st]);
+        }
     } else if (warp == 2) {
         // ---------------- MMA issue ----------------
         pdl_wait();
@@ -206,14 +229,14 @@ __global__ void __launch_bounds__(Q8T_THREADS, 1)
             }
             if (ok) {
                 ok = mbar_wait(&w_full[ws], (uint32_t)((i / WS) & 1), &g_q8tc_error) &&
-                     mbar_wait(&a_full[as], (uint32_t)((i / AS) & 1), &g_q8tc_error);
+                     mbar_wait(&a_tab[as], (uint32_t)((i / AS) & 1), &g_q8tc_error);
                 ok = __all_sync(0xffffffffu, ok);
             }
             if (ok) {
-                // this row's 8 weight block scales; the columns' activation block scales
+                // this row's 8 weight block scales; the columns' (dx, -dx B) table
                 const uint4 dwv = *(const uint4*)(wst + (size_t)ws * Q8T_WSTAGE + 2 * Q8T_WHALF + row * 16);
                 const __half* dws = (const __half*)&dwv;
-                const __half* dxs = (const __half*)(act + (size_t)as * C::ASTAGE + 2 * C::AHALF) + cq * NQ * 8;
+                const float2* tab = (const float2*)(act + (size_t)as * C::ASTAGE + 2 * C::AHALF + C::ASC) + cq * NQ;
                 for (int g = 0; g < GPU && ok; g++) {
                     const int q = i * GPU + g, b = q & 1;
                     ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[b], (uint32_t)((q >> 1) & 1), &g_q8tc_error));
@@ -225,6 +248,7 @@ __global__ void __launch_bounds__(Q8T_THREADS, 1)
                         const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) +
                                                (uint32_t)((b * BPB + bl) * N + cq * NQ);
                         const float dw = __half2float(dws[j]);
+                        const float4* tj = (const float4*)(tab + j * N);   // two columns per float4
                         constexpr int CH = NQ < 16 ? NQ : 16;
 #pragma unroll
                         for (int cc = 0; cc < NQ; cc += CH) {
@@ -239,9 +263,12 @@ __global__ void __launch_bounds__(Q8T_THREADS, 1)
                                 if (lane == 0) mbar_arrive(&acc_empty[b]);
                             }
 #pragma unroll
-                            for (int c = 0; c < CH; c++) {
-                                const float dx = __half2float(dxs[(cc + c) * 8 + j]);
-                                yacc[cc + c] = fmaf(dw * dx, i2f_exact22((int)v[c]), yacc[cc + c]);
+                            for (int c = 0; c < CH; c += 2) {
+                                const float4 t = tj[(cc + c) >> 1];
+                                const float p0 = fmaf(t.x, __int_as_float(0x4B400000 + (int)v[c]), t.y);
+                                const float p1 = fmaf(t.z, __int_as_float(0x4B400000 + (int)v[c + 1]), t.w);
+                                yacc[cc + c] = fmaf(dw, p0, yacc[cc + c]);
+                                yacc[cc + c + 1] = fmaf(dw, p1, yacc[cc + c + 1]);
                             }
                         }
                     }

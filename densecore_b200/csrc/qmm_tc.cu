@@ -18,12 +18,12 @@
 //               columns' scales dx (and the Q4_K min-term pair sums) in a metadata ring
 //   warp 2      one thread issues per K half 4 k-steps x 2 planes of M128 x N x K32 MMAs into
 //               C_H, C_L (double-buffered across units) and releases stages with tcgen05.commit
-//   warps 4-11  thread (row r, half h) first expands K half h of weight row r of unit i into two
-//               int8 planes H, L with q * scale = SHIFT * H + L exactly, in the core-matrix layout:
+//   warps 4-19  thread (row r, quarter p) first expands K quarter p of weight row r of unit i into
+//               two int8 planes H, L with q * scale = SHIFT * H + L exactly, in the core-matrix layout:
 //                 Q4_K  sc = 8 sh + sl (sh, sl <= 7): H = q sh, L = q sl (q <= 15), SHIFT = 8
 //                 Q6_K  p = (u - 32) sc (u the unsigned 6-bit quant, sc the signed 8-bit sub-block
 //                       scale): H = p >> 7, L = p & 127, SHIFT = 128 (the -32 offset is folded in)
-//               then, while unit i's MMAs run, drains unit i-1's accumulators for half h of the
+//               then, while unit i's MMAs run, drains unit i-1's accumulators for quarter p of the
 //               columns (tcgen05.ld), forms isum = SHIFT C_H + C_L and accumulates
 //                 Q4_K  y += dx (d isum - dmin sum_j m_j bsum32_j)      (ggml's order)
 //                 Q6_K  y += dx d isum
@@ -52,8 +52,9 @@ cudaError_t qmm_tc_device_error(int* out, bool clear) {
 }
 
 constexpr int TC_ROWS = 128;      // weight rows per tile (the MMA's M)
-constexpr int TC_THREADS = 384;   // 12 warps: 0 weight TMA, 1 activation TMA, 2 MMA, 3 spare, 4-11 prep + epilogue
+constexpr int TC_THREADS = 640;   // 20 warps: 0 weight TMA, 1 activation TMA, 2 MMA, 3 spare, 4-19 prep + epilogue
 constexpr int TC_WORK0 = 4;
+constexpr int TC_WORKERS = 16;
 constexpr int TC_HPLANE = TC_ROWS * 128;   // one int8 plane of a K half: 16 KB
 constexpr int TC_HSBO = 8 * 128;           // plane: 8-row groups 1 KB apart, 16-B K chunks 128 B apart
 constexpr int TC_MS = 4;                   // metadata slots (dx, pair sums, row scales)
@@ -92,65 +93,73 @@ struct TcCfg {
     static_assert(SMEM <= TC_SMEM_MAX, "shared memory");
 };
 
-// named barrier of the 8 prep / epilogue warps
-__device__ __forceinline__ void work_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// named barrier of the 16 prep / epilogue warps
+__device__ __forceinline__ void work_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
 
-// ---- prep: one weight row of one super-block (in shared memory) -> the two planes of K half h ----
-// Q4_K K half h (sub-blocks 4h .. 4h+3): chunk kc (16 elements) of sub-block kc/2
+// ---- prep: one weight row of one super-block (in shared memory) -> the two planes' 4 K chunks
+// (16 elements each) of quarter p: K half h = p / 2, chunks j = 4 (p % 2) .. +3 of that half ----
+// Q4_K quarter p = sub-blocks 2p (low nibbles of byte group p) and 2p + 1 (its high nibbles)
 template <int TYPE, typename std::enable_if<TYPE == DCG_TYPE_Q4_K, int>::type = 0>
-__device__ __forceinline__ void prep_half(const uint8_t* row, int h, uint8_t* pH, uint8_t* pL) {
-    const Q4kScales sc = q4k_unpack(*(const uint4*)row);
-    uint32_t qs[16];   // nibble bytes 64h .. 64h+63
+__device__ __forceinline__ void prep_quarter(const uint8_t* row, int p, uint8_t* pH, uint8_t* pL) {
+    const uint4 hdr = *(const uint4*)row;
+    const uint4 g0 = *(const uint4*)(row + 16 + 32 * p), g1 = *(const uint4*)(row + 32 + 32 * p);
+    const Q4kScales sc = q4k_unpack(hdr);
+    const uint32_t w[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    const int j0 = 4 * (p & 1);
 #pragma unroll
-    for (int q = 0; q < 4; q++) *(uint4*)&qs[4 * q] = ((const uint4*)(row + 16 + 64 * h))[q];
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const int sbk = 4 * h + (j >> 1);                       // sub-block
+    for (int c = 0; c < 4; c++) {
+        const int sbk = 2 * p + (c >> 1);   // chunks 0, 1: sub-block 2p; 2, 3: sub-block 2p + 1
         const uint32_t scs = ((sbk < 4 ? sc.sc03 : sc.sc47) >> (8 * (sbk & 3))) & 0x3Fu;
         const uint32_t sh = scs >> 3, sl = scs & 7u;
-        const int g = (j >> 2);                                 // 32-byte group within the half
         uint4 vh, vl;
         uint32_t* ph = (uint32_t*)&vh;
         uint32_t* pl = (uint32_t*)&vl;
 #pragma unroll
-        for (int w = 0; w < 4; w++) {
-            const uint32_t word = qs[g * 8 + (j & 1) * 4 + w];
-            const uint32_t nib = (sbk & 1) ? (word >> 4) & 0x0F0F0F0Fu : word & 0x0F0F0F0Fu;
-            ph[w] = nib * sh;
-            pl[w] = nib * sl;
+        for (int t = 0; t < 4; t++) {
+            const uint32_t word = w[(c & 1) * 4 + t];
+            const uint32_t nib = (c >> 1) ? (word >> 4) & 0x0F0F0F0Fu : word & 0x0F0F0F0Fu;
+            ph[t] = nib * sh;
+            pl[t] = nib * sl;
         }
-        *(uint4*)(pH + j * 128) = vh;
-        *(uint4*)(pL + j * 128) = vl;
+        *(uint4*)(pH + (j0 + c) * 128) = vh;
+        *(uint4*)(pL + (j0 + c) * 128) = vl;
     }
 }
 
-// Q6_K K half h: chunk j (elements 128h + 16j .. +15) = sub-block 8h + j, group grp = j/2,
+// Q6_K chunk j of K half h (elements 128h + 16j .. +15) = sub-block 8h + j, group grp = j/2,
 // l-range 16 (j & 1) .. +15; u = low nibble of ql[64h + 32 (grp & 1) + l] (shifted by 4 (grp >> 1))
 // | 2 bits of qh[32h + l] (shifted by 2 grp) << 4.  p = (u - 32) sc is formed two elements per
 // 32-bit word (16-bit lanes, biased by 32768 so no lane borrows): V = (u0 | u1 << 16) sc + K with
 // K = (32768 - 32 sc) in both lanes; then L = V & 127 and H = (V >> 7) & 255 per lane.
 template <int TYPE, typename std::enable_if<TYPE == DCG_TYPE_Q6_K, int>::type = 0>
-__device__ __forceinline__ void prep_half(const uint8_t* row, int h, uint8_t* pH, uint8_t* pL) {
-    const uint32_t* w32 = (const uint32_t*)row;
-    const uint2 scv = *(const uint2*)(row + 192 + 8 * h);
-    const uint32_t scw[2] = {scv.x, scv.y};   // scales 8h .. 8h+7
+__device__ __forceinline__ void prep_quarter(const uint8_t* row, int p, uint8_t* pH, uint8_t* pL) {
+    const int h = p >> 1, j0 = 4 * (p & 1);
+    const uint32_t scw = *(const uint32_t*)(row + 192 + 8 * h + j0);   // scales of chunks j0 .. j0+3
+    uint4 ql[4], qh[2];
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const int grp = j >> 1, l0 = 16 * (j & 1);
-        const int sc = (int)(int8_t)((scw[j >> 2] >> (8 * (j & 3))) & 0xFF);
+    for (int c = 0; c < 4; c++) {   // chunk j0 + c: group (j0 + c) / 2, l0 = 16 (c & 1)
+        const int grp = (j0 + c) >> 1;
+        ql[c] = *(const uint4*)(row + 64 * h + 32 * (grp & 1) + 16 * (c & 1));
+    }
+    qh[0] = *(const uint4*)(row + 128 + 32 * h);
+    qh[1] = *(const uint4*)(row + 128 + 32 * h + 16);
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        const int j = j0 + c, grp = j >> 1;
+        const int sc = (int)(int8_t)((scw >> (8 * c)) & 0xFF);
         const uint32_t kk = (uint32_t)(32768 - 32 * sc) * 0x10001u;
+        const uint32_t* qlw = (const uint32_t*)&ql[c];
+        const uint32_t* qhw = (const uint32_t*)&qh[c & 1];
         uint4 vh, vl;
         uint32_t* ph = (uint32_t*)&vh;
         uint32_t* pl = (uint32_t*)&vl;
 #pragma unroll
-        for (int w = 0; w < 4; w++) {
-            const uint32_t ql = w32[(64 * h + 32 * (grp & 1) + l0) / 4 + w];
-            const uint32_t qh = w32[(128 + 32 * h + l0) / 4 + w];
-            const uint32_t u = ((ql >> (4 * (grp >> 1))) & 0x0F0F0F0Fu) | (((qh >> (2 * grp)) & 0x03030303u) << 4);
+        for (int t = 0; t < 4; t++) {
+            const uint32_t u = ((qlw[t] >> (4 * (grp >> 1))) & 0x0F0F0F0Fu) | (((qhw[t] >> (2 * grp)) & 0x03030303u) << 4);
             const uint32_t v01 = __byte_perm(u, 0u, 0x4140u) * (uint32_t)sc + kk;
             const uint32_t v23 = __byte_perm(u, 0u, 0x4342u) * (uint32_t)sc + kk;
-            pl[w] = __byte_perm(v01 & 0x007F007Fu, v23 & 0x007F007Fu, 0x6420u);
-            ph[w] = __byte_perm((v01 >> 7) & 0x00FF00FFu, (v23 >> 7) & 0x00FF00FFu, 0x6420u);
+            pl[t] = __byte_perm(v01 & 0x007F007Fu, v23 & 0x007F007Fu, 0x6420u);
+            ph[t] = __byte_perm((v01 >> 7) & 0x00FF00FFu, (v23 >> 7) & 0x00FF00FFu, 0x6420u);
         }
         *(uint4*)(pH + j * 128) = vh;
         *(uint4*)(pL + j * 128) = vl;
@@ -168,16 +177,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     constexpr bool Q4 = TYPE == DCG_TYPE_Q4_K;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* w_full = (uint64_t*)smem;        // [WS] weight tile landed (tx)
-    uint64_t* w_empty = w_full + WS;           // [WS] 8 prep warps read it
+    uint64_t* w_empty = w_full + WS;           // [WS] 16 prep warps read it
     uint64_t* a_full = w_empty + WS;           // [AS] activation tile landed (tx)
     uint64_t* a_empty = a_full + AS;           // [AS] MMAs that read it done
-    uint64_t* pl_full = a_empty + AS;          // [2] K-half planes written (128 prep threads)
+    uint64_t* pl_full = a_empty + AS;          // [2] K-half planes written (256 prep threads)
     uint64_t* pl_empty = pl_full + 2;          // [2] MMAs that read them done
     uint64_t* acc_full = pl_empty + 2;         // [2] accumulators complete
-    uint64_t* acc_empty = acc_full + 2;        // [2] 8 epilogue warps read them
+    uint64_t* acc_empty = acc_full + 2;        // [2] 16 epilogue warps read them
     uint64_t* meta_full = acc_empty + 2;       // [MS] column metadata staged (32 producer lanes)
     uint64_t* row_full = meta_full + MS;       // [MS] row scales staged (128 prep threads)
-    uint64_t* meta_empty = row_full + MS;      // [MS] 8 epilogue warps done with the slot
+    uint64_t* meta_empty = row_full + MS;      // [MS] 16 epilogue warps done with the slot
     uint64_t* mma_done = meta_empty + MS;      // [1] every MMA retired
     uint32_t* tmem_slot = (uint32_t*)(mma_done + 1);
     int* last_flag = (int*)(tmem_slot + 1);
@@ -195,22 +204,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < WS; s++) {
             mbar_init(&w_full[s], 1);
-            mbar_init(&w_empty[s], 8);
+            mbar_init(&w_empty[s], TC_WORKERS);
         }
         for (int s = 0; s < AS; s++) {
             mbar_init(&a_full[s], 1);
             mbar_init(&a_empty[s], 1);
         }
         for (int b = 0; b < 2; b++) {
-            mbar_init(&pl_full[b], 128);
+            mbar_init(&pl_full[b], 256);
             mbar_init(&pl_empty[b], 1);
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 8);
+            mbar_init(&acc_empty[b], TC_WORKERS);
         }
         for (int s = 0; s < MS; s++) {
             mbar_init(&meta_full[s], 32);
             mbar_init(&row_full[s], 128);
-            mbar_init(&meta_empty[s], 8);
+            mbar_init(&meta_empty[s], TC_WORKERS);
         }
         mbar_init(mma_done, 1);
         fence_mbar_init();
@@ -243,33 +252,61 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         pdl_wait();
     } else if (warp == 1) {
         // ---------------- activation producer + column metadata ----------------
+        // lane c stages columns c, c + 32, ...: their dx (and Q4_K pair sums) for unit i + 1 are
+        // loaded while unit i is handled, so the global-memory latency stays off the issue path
         pdl_wait();
+        constexpr int CPL = (N + 31) / 32;   // columns per lane
+        float ndx[CPL];
+        uint4 nbs[CPL];
+        auto load_meta = [&](int i) {
+            const int64_t u = u0 + i, tile = u / nb;
+            const int s = (int)(u % nb);
+            const int c0 = (int)(tile % ct_tiles) * N;
+#pragma unroll
+            for (int j = 0; j < CPL; j++) {
+                const int c = lane + 32 * j, col = c0 + c;
+                ndx[j] = 0.0f;
+                nbs[j] = make_uint4(0, 0, 0, 0);
+                if (i < nu && c < N && col < m) {
+                    ndx[j] = __ldg(&((const float*)a.d)[(size_t)col * nb + s]);
+                    if (Q4) nbs[j] = __ldg((const uint4*)(a.bs32 + ((size_t)col * nb + s) * 8));
+                }
+            }
+        };
+        load_meta(0);
         for (int i = 0; i < nu && ok; i++) {
             const int64_t u = u0 + i, tile = u / nb;
             const int s = (int)(u % nb), st = i % AS, ms = i % MS;
             const int c0 = (int)(tile % ct_tiles) * N;
             if (i >= AS) ok = mbar_wait(&a_empty[st], (uint32_t)(((i / AS) - 1) & 1), &g_tc_error);
-            if (ok && i >= MS) ok = mbar_wait(&meta_empty[ms], (uint32_t)(((i / MS) - 1) & 1), &g_tc_error);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
-            float* mdx = (float*)(meta + (size_t)ms * C::META);
-            uint4* mbs = (uint4*)(mdx + N);
-            for (int c = lane; c < N; c += 32) {
-                const int col = c0 + c;
-                float dx = 0.0f;
-                uint4 bs = make_uint4(0, 0, 0, 0);
-                if (col < m) {
-                    dx = __ldg(&((const float*)a.d)[(size_t)col * nb + s]);
-                    if (Q4) bs = __ldg((const uint4*)(a.bs32 + ((size_t)col * nb + s) * 8));
-                }
-                mdx[c] = dx;
-                if (Q4) mbs[c] = bs;
-            }
-            mbar_arrive(&meta_full[ms]);
             if (lane == 0) {
                 mbar_arrive_expect_tx(&a_full[st], (uint32_t)C::AT);
                 tma_load_3d(act + (size_t)st * C::AT, &amap, 0, c0, s * 16, &a_full[st]);
             }
+            float cdx[CPL];
+            uint4 cbs[CPL];
+#pragma unroll
+            for (int j = 0; j < CPL; j++) {
+                cdx[j] = ndx[j];
+                cbs[j] = nbs[j];
+            }
+            load_meta(i + 1);
+            if (i >= MS) ok = mbar_wait(&meta_empty[ms], (uint32_t)(((i / MS) - 1) & 1), &g_tc_error);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            float* mdx = (float*)(meta + (size_t)ms * C::META);
+            uint4* mbs = (uint4*)(mdx + N);
+#pragma unroll
+            for (int j = 0; j < CPL; j++) {
+                const int c = lane + 32 * j;
+                if (c < N) {
+                    mdx[c] = cdx[j];
+                    if (Q4) mbs[c] = cbs[j];
+                }
+            }
+            mbar_arrive(&meta_full[ms]);
         }
     } else if (warp == 2) {
         // ---------------- MMA issue ----------------
@@ -305,14 +342,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_wait(mma_done, 0, &g_tc_error);
         }
     } else if (warp >= TC_WORK0) {
-        // ---------------- prep + epilogue: thread <-> (weight row, half) ----------------
-        // Iteration i expands unit i's weights (this thread's K half of its row) and then drains
-        // unit i-1's accumulators (this thread's half of the columns): unit i's MMAs run while
-        // unit i-1 is drained.
-        constexpr int NH = N / 2;
-        const int quarter = warp & 3, half = (warp - TC_WORK0) >> 2;
+        // ---------------- prep + epilogue: thread <-> (weight row, quarter) ----------------
+        // Iteration i expands unit i's weights (quarter qp of its row's K) and then drains unit
+        // i-1's accumulators (quarter qp of the columns): unit i's MMAs run while unit i-1 is
+        // drained.
+        constexpr int NH = N / 4;                       // columns per thread
+        const int quarter = warp & 3, qp = (warp - TC_WORK0) >> 2;   // TMEM lane group, K / column quarter
+        const int half = qp >> 1;                     // the K half this thread's prep writes
         const int row = quarter * 32 + lane;
-        const int et = threadIdx.x - TC_WORK0 * 32;   // 0..255
+        const int et = threadIdx.x - TC_WORK0 * 32;   // 0..511
         pdl_wait();   // y, the partials and the tickets may be in use by the previous kernel
         float dnext = 0.0f;
         auto load_d = [&](int i) -> float {   // Q6_K: the row's fp16 d of unit i (0 past the rows)
@@ -321,7 +359,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const int64_t r = (tile / ct_tiles) * TC_ROWS + row;
             return r < n ? __half2float(wd[r * nb + (u % nb)]) : 0.0f;
         };
-        if (!Q4 && half == 0) dnext = load_d(0);
+        if (!Q4 && qp == 0) dnext = load_d(0);
         float yacc[NH];
         int seg_s0 = 0;
         for (int i = 0; i <= nu; i++) {
@@ -329,13 +367,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if (i < nu && ok) {
                 const int st = i % WS, ms = i % MS;
                 ok = mbar_wait(&w_full[st], (uint32_t)((i / WS) & 1), &g_tc_error);
-                if (ok && half == 0 && i >= MS)
+                if (ok && qp == 0 && i >= MS)
                     ok = mbar_wait(&meta_empty[ms], (uint32_t)(((i / MS) - 1) & 1), &g_tc_error);
                 if (ok && i >= 1) ok = mbar_wait(&pl_empty[half], (uint32_t)((i - 1) & 1), &g_tc_error);
                 ok = __all_sync(0xffffffffu, ok);
                 if (ok) {
                     const uint8_t* src = raw + (size_t)st * C::WT + (size_t)row * TcW<TYPE>::ROWB;
-                    if (half == 0) {   // the row's scales of this unit, for the epilogue
+                    if (qp == 0) {   // the row's scales of this unit, for the epilogue
                         if (Q4) {
                             const uint4 hdr = *(const uint4*)src;
                             const Q4kScales sc = q4k_unpack(hdr);
@@ -347,7 +385,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         mbar_arrive(&row_full[ms]);
                     }
                     uint8_t* pH = planes + (size_t)(2 * half) * TC_HPLANE + (size_t)(row >> 3) * TC_HSBO + (row & 7) * 16;
-                    prep_half<TYPE>(src, half, pH, pH + TC_HPLANE);
+                    prep_quarter<TYPE>(src, qp, pH, pH + TC_HPLANE);
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&w_empty[st]);
                     fence_proxy_async_smem();
@@ -372,10 +410,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
             if (ok) {
                 tc_fence_after();
-                const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 2 * N + half * NH);
+                const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 2 * N + qp * NH);
                 const uint4 rp = rowp[ms * TC_ROWS + row];
-                const float* mdx = (const float*)(meta + (size_t)ms * C::META) + half * NH;
-                const uint4* mbs = (const uint4*)((const float*)(meta + (size_t)ms * C::META) + N) + half * NH;
+                const float* mdx = (const float*)(meta + (size_t)ms * C::META) + qp * NH;
+                const uint4* mbs = (const uint4*)((const float*)(meta + (size_t)ms * C::META) + N) + qp * NH;
                 float2 dd = make_float2(__uint_as_float(rp.x), 0.0f);
                 int mp0 = 0, mp1 = 0, mp2 = 0, mp3 = 0;
                 if (Q4) {
@@ -393,9 +431,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     if (CH == 16) {
                         tmem_ld16(lane_addr + cc, hv);
                         tmem_ld16(lane_addr + N + cc, lv);
-                    } else {
+                    } else if (CH == 8) {
                         tmem_ld8(lane_addr + cc, hv);
                         tmem_ld8(lane_addr + N + cc, lv);
+                    } else {
+                        tmem_ld4(lane_addr + cc, hv);
+                        tmem_ld4(lane_addr + N + cc, lv);
                     }
                     tmem_wait_ld();
                     if (cc + CH == NH) {   // every read of this buffer issued and complete
@@ -430,7 +471,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const int64_t rt = tile / ct_tiles;
                 const int ct = (int)(tile % ct_tiles);
                 const int64_t r = rt * TC_ROWS + row;
-                const int cbase = ct * N + half * NH;
+                const int cbase = ct * N + qp * NH;
                 if (seg_s0 == 0 && s == nb - 1) {
                     if (ok && r < n)
 #pragma unroll
@@ -441,7 +482,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     const int slot = sk_begin(bid, T, G) > t0 ? 0 : 1;
                     float* P = part + (size_t)(bid * 2 + slot) * N * TC_ROWS;
 #pragma unroll
-                    for (int c = 0; c < NH; c++) P[(half * NH + c) * TC_ROWS + row] = yacc[c];
+                    for (int c = 0; c < NH; c++) P[(qp * NH + c) * TC_ROWS + row] = yacc[c];
                     __threadfence();
                     work_bar();
                     const int64_t cf = sk_owner(t0, T, G), cl = sk_owner(t0 + nb - 1, T, G);
@@ -462,7 +503,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                             const int sq = sk_begin(q, T, G) > t0 ? 0 : 1;
                             const float* Q = part + (size_t)(q * 2 + sq) * N * TC_ROWS;
 #pragma unroll
-                            for (int c = 0; c < NH; c++) yacc[c] += __ldcg(&Q[(half * NH + c) * TC_ROWS + row]);
+                            for (int c = 0; c < NH; c++) yacc[c] += __ldcg(&Q[(qp * NH + c) * TC_ROWS + row]);
                         }
                         if (ok && r < n)
 #pragma unroll
