@@ -20,42 +20,50 @@ namespace dcg {
 
 constexpr int FUSE_THREADS = 256;
 
-__device__ __forceinline__ float block_sum(float v, float* red) {
+__device__ __forceinline__ double block_sum(double v, double* red) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (lane == 0) red[warp] = v;
     __syncthreads();
-    float t = 0.0f;
+    double t = 0.0;
     for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += red[w];
     __syncthreads();
     return t;
+}
+
+// ggml's rms_norm scale: the fp32 squares summed in double, mean rounded to fp32, then
+// 1.0f / sqrtf(mean + eps) with IEEE-rounded fp32 operations (the sum's order differs from the
+// CPU's sequential one only far below fp32 resolution)
+__device__ __forceinline__ float rms_scale(double sumsq, int64_t k, float eps) {
+    const float mean = (float)(sumsq / (double)k);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
 }
 
 // one CTA per activation row
 __global__ void __launch_bounds__(FUSE_THREADS) add_rmsnorm_quant_kernel(
     float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w, float eps,
     int64_t k, int act_type, ActQ a) {
-    __shared__ float red[FUSE_THREADS / 32];
+    __shared__ double red[FUSE_THREADS / 32];
     pdl_wait();
     pdl_trigger();
     const int64_t row = blockIdx.x;
     float* xr = x + row * k;
-    float ss = 0.0f;
+    double ss = 0.0;
     for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
         float v = xr[i];
         if (delta) {
-            v += delta[row * k + i];
+            v = __fadd_rn(v, delta[row * k + i]);
             xr[i] = v;
         }
-        ss += v * v;
+        ss += (double)__fmul_rn(v, v);
     }
-    const float rs = rsqrtf(block_sum(ss, red) / (float)k + eps);  // also orders the x writes above
+    const float rs = rms_scale(block_sum(ss, red), k, eps);  // block_sum also orders the x writes above
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     if (act_type == DCG_TYPE_Q8_0) {
         for (int64_t b = warp; b < k / QK8_0; b += nw) {
             const int64_t i = b * QK8_0 + lane;
-            warp_q8_0_store(xr[i] * rs * w[i], lane, a, row * (k / QK8_0) + b);
+            warp_q8_0_store(__fmul_rn(__fmul_rn(xr[i], rs), w[i]), lane, a, row * (k / QK8_0) + b);
         }
     } else {
         for (int64_t b = warp; b < k / QK_K; b += nw) {
@@ -63,7 +71,7 @@ __global__ void __launch_bounds__(FUSE_THREADS) add_rmsnorm_quant_kernel(
 #pragma unroll
             for (int j = 0; j < 8; j++) {
                 const int64_t i = b * QK_K + lane * 8 + j;
-                v[j] = xr[i] * rs * w[i];
+                v[j] = __fmul_rn(__fmul_rn(xr[i], rs), w[i]);
             }
             warp_q8_K_store(v, lane, a, row * (k / QK_K) + b);
         }
@@ -86,14 +94,14 @@ __global__ void __launch_bounds__(FUSE_THREADS) swiglu_quant_kernel(
     if (act_type == DCG_TYPE_Q8_0) {
         const int64_t i = b * QK8_0 + lane;
         const float gv = gr[i];
-        warp_q8_0_store(gv / (1.0f + expf(-gv)) * ur[i], lane, a, row * per_row + b);
+        warp_q8_0_store(__fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), ur[i]), lane, a, row * per_row + b);
     } else {
         float v[8];
 #pragma unroll
         for (int j = 0; j < 8; j++) {
             const int64_t i = b * QK_K + lane * 8 + j;
             const float gv = gr[i];
-            v[j] = gv / (1.0f + expf(-gv)) * ur[i];
+            v[j] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), ur[i]);
         }
         warp_q8_K_store(v, lane, a, row * per_row + b);
     }
@@ -104,7 +112,7 @@ __global__ void __launch_bounds__(FUSE_THREADS) swiglu_quant_kernel(
 __global__ void __launch_bounds__(FUSE_THREADS) qk_rope_append_kernel(
     const float* __restrict__ q, int64_t ldq, const float* __restrict__ k, int64_t ldk,
     const float* __restrict__ v, int64_t ldv, int n_seqs, int hq, int hkv, const float* __restrict__ qw,
-    const float* __restrict__ kw, float eps, float theta, const int* __restrict__ pos,
+    const float* __restrict__ kw, float eps, float theta_scale, const int* __restrict__ pos,
     float* __restrict__ q_out, __half* __restrict__ karena, __half* __restrict__ varena, int n_layer,
     int layer, const int* __restrict__ bt, int mbs, const int* __restrict__ seq_ids) {
     constexpr int D = 128;
@@ -121,25 +129,26 @@ __global__ void __launch_bounds__(FUSE_THREADS) qk_rope_append_kernel(
     const float* nw = is_q ? qw : kw;
     const int d0 = 2 * lane, d1 = 64 + 2 * lane;
     float x0 = src[d0], x1 = src[d0 + 1], y0 = src[d1], y1 = src[d1 + 1];
-    if (nw) {  // QK-norm (Qwen3); skipped when no norm weight is given (Llama)
-        float ss = x0 * x0 + x1 * x1 + y0 * y0 + y1 * y1;
+    if (nw) {  // QK-norm (Qwen3), the rms_norm of the head as above; skipped without weights (Llama)
+        double ss = (double)__fmul_rn(x0, x0) + (double)__fmul_rn(x1, x1) + (double)__fmul_rn(y0, y0) +
+                    (double)__fmul_rn(y1, y1);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float rs = rsqrtf(ss / (float)D + eps);
-        x0 *= rs * nw[d0];
-        x1 *= rs * nw[d0 + 1];
-        y0 *= rs * nw[d1];
-        y1 *= rs * nw[d1 + 1];
+        const float rs = rms_scale(ss, D, eps);
+        x0 = __fmul_rn(__fmul_rn(x0, rs), nw[d0]);
+        x1 = __fmul_rn(__fmul_rn(x1, rs), nw[d0 + 1]);
+        y0 = __fmul_rn(__fmul_rn(y0, rs), nw[d1]);
+        y1 = __fmul_rn(__fmul_rn(y1, rs), nw[d1 + 1]);
     }
-    // NeoX rotate-half: (x_i, x_{i+64}) at angle p * theta^(-2i/D)
-    const float p = (float)pos[s];
-    const float f0 = (float)exp2(-(double)(2 * d0) / D * log2((double)theta));
-    const float f1 = (float)exp2(-(double)(2 * (d0 + 1)) / D * log2((double)theta));
-    float s0, c0, s1, c1;
-    sincosf(p * f0, &s0, &c0);
-    sincosf(p * f1, &s1, &c1);
-    const float r0 = x0 * c0 - y0 * s0, r1 = x1 * c1 - y1 * s1;
-    const float r2 = y0 * c0 + x0 * s0, r3 = y1 * c1 + x1 * s1;
+    // NeoX rotate-half: (x_i, x_{i+64}) at angle theta_i, with ggml's fp32 recurrence
+    // theta_0 = p, theta_{i+1} = theta_i * theta_scale (theta_scale = powf(base, -2/D), from the host)
+    float t0 = (float)pos[s];
+    for (int i = 0; i < d0; i++) t0 = __fmul_rn(t0, theta_scale);
+    const float t1 = __fmul_rn(t0, theta_scale);
+    const float c0 = cosf(t0), s0 = sinf(t0), c1 = cosf(t1), s1 = sinf(t1);
+    // ggml's rotation: x0 cos - x1 sin, x0 sin + x1 cos, each product rounded
+    const float r0 = __fsub_rn(__fmul_rn(x0, c0), __fmul_rn(y0, s0)), r1 = __fsub_rn(__fmul_rn(x1, c1), __fmul_rn(y1, s1));
+    const float r2 = __fadd_rn(__fmul_rn(x0, s0), __fmul_rn(y0, c0)), r3 = __fadd_rn(__fmul_rn(x1, s1), __fmul_rn(y1, c1));
     if (is_q) {
         float* dst = q_out + ((int64_t)s * hq + hh) * D;
         *(float2*)(dst + d0) = make_float2(r0, r1);
@@ -178,8 +187,10 @@ cudaError_t launch_qk_rope_append(const float* q, int64_t ldq, const float* k, i
                                   cudaStream_t st, const int* seq_ids) {
     const int64_t warps = (int64_t)n_seqs * (hq + hkv);
     const unsigned grid = (unsigned)((warps * 32 + FUSE_THREADS - 1) / FUSE_THREADS);
+    // ggml's per-dimension angle ratio powf(freq_base, -2 / n_dims), computed once on the host (libm)
+    const float theta_scale = powf(theta, -2.0f / 128.0f);
     return launch_pdl(qk_rope_append_kernel, dim3(grid), dim3(FUSE_THREADS), 0, st, q, ldq, k, ldk, v, ldv,
-                      n_seqs, hq, hkv, qw, kw, eps, theta, pos, q_out, (__half*)karena, (__half*)varena,
+                      n_seqs, hq, hkv, qw, kw, eps, theta_scale, pos, q_out, (__half*)karena, (__half*)varena,
                       n_layer, layer, bt, mbs, seq_ids);
 }
 
