@@ -17,6 +17,7 @@ import pytest
 import torch
 
 from chained_ref import reference_step
+from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
 
