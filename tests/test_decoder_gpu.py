@@ -71,13 +71,19 @@ def _act_rows(buf, at, m, k):
 
 
 def _check_quantized(name, got_rows, ref_values, at):
-    """Activation bytes: equal to quantize(ref) but for rare boundary flips (< 0.1 % of quants)."""
+    """Activation bytes: quants equal to quantize(ref) but for rare boundary flips (< 0.1 %); block
+    scales equal, or (where the block's largest input differs in its last bits: SiLU's expf, RoPE's
+    cosf / sinf are not the host's) within 1e-6 relative (Q8_K f32) / one fp16 step (Q8_0)."""
     want = O.quantize(np.asarray(ref_values, np.float32), at)
     bb, dn, nq = (34, 2, 32) if at == O.Q8_0 else (292, 4, 256)
     g, w = got_rows.reshape(-1, bb), want.reshape(-1, bb)
     frac = float((g[:, dn:dn + nq] != w[:, dn:dn + nq]).mean())
     assert frac < 1e-3, (name, "quants differing", frac)
-    assert float((g[:, :dn] != w[:, :dn]).any(-1).mean()) < 1e-2, (name, "block scales differing")
+    sd = np.float16 if at == O.Q8_0 else np.float32
+    dg = g[:, :dn].copy().view(sd).astype(np.float64).ravel()
+    dw = w[:, :dn].copy().view(sd).astype(np.float64).ravel()
+    rel = np.abs(dg - dw) / np.maximum(np.abs(dw), 1e-30)
+    assert rel.max() <= (2.0 ** -10 if at == O.Q8_0 else 1e-6), (name, "block scales", float(rel.max()))
 
 
 def _check_mm(name, y, wrows, wt, k, act_rows, m):
