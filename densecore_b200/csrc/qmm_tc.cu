@@ -42,6 +42,23 @@ namespace dcg {
 
 __device__ int g_tc_error = 0;
 
+// Pipeline timeline for tuning, compiled in only with -DDCG_TC_TRACE (never in the library build):
+// clock64 stamps of 8 events for the first 64 units of CTAs 0-3 (g_tc_trace[cta][unit][event]).
+#ifdef DCG_TC_TRACE
+__device__ long long g_tc_trace[4][64][8];
+#define TC_TRACE(i, ev)                                                                            \
+    do {                                                                                           \
+        if (blockIdx.x < 4 && (i) < 64) g_tc_trace[blockIdx.x][(i)][(ev)] = clock64();             \
+    } while (0)
+extern "C" int dcg_debug_tc_trace(void* out) {
+    return (int)cudaMemcpyFromSymbol(out, g_tc_trace, sizeof(g_tc_trace));
+}
+#else
+#define TC_TRACE(i, ev) \
+    do {                \
+    } while (0)
+#endif
+
 cudaError_t qmm_tc_device_error(int* out, bool clear) {
     cudaError_t e = cudaMemcpyFromSymbol(out, g_tc_error, sizeof(int));
     if (e == cudaSuccess && clear && *out) {
@@ -245,6 +262,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const int rt = (int)(tile / ct_tiles);
                 if (i >= WS) ok = mbar_wait(&w_empty[st], (uint32_t)(((i / WS) - 1) & 1), &g_tc_error);
                 if (!ok) break;
+                TC_TRACE(i, 0);
                 mbar_arrive_expect_tx(&w_full[st], (uint32_t)C::WT);
                 tma_load_2d(raw + (size_t)st * C::WT, &wmap, s * (TcW<TYPE>::ROWB / 4), rt * TC_ROWS, &w_full[st]);
             }
@@ -282,6 +300,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             if (lane == 0) {
+                TC_TRACE(i, 1);
                 mbar_arrive_expect_tx(&a_full[st], (uint32_t)C::AT);
                 tma_load_3d(act + (size_t)st * C::AT, &amap, 0, c0, s * 16, &a_full[st]);
             }
@@ -317,6 +336,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const int st = i % AS, b = i & 1;
                 ok = mbar_wait(&a_full[st], (uint32_t)((i / AS) & 1), &g_tc_error) &&
                      (i < 2 || mbar_wait(&acc_empty[b], (uint32_t)(((i >> 1) - 1) & 1), &g_tc_error));
+                TC_TRACE(i, 4);
                 const uint32_t pa = smem_u32(act + (size_t)st * C::AT);
                 const uint32_t dH = tmem + (uint32_t)(b * 2 * N), dL = dH + N;
 #pragma unroll
@@ -337,6 +357,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if (!ok) break;
                 tc_commit(&a_empty[st]);
                 tc_commit(&acc_full[b]);
+                TC_TRACE(i, 5);
             }
             tc_commit(mma_done);
             mbar_wait(mma_done, 0, &g_tc_error);
@@ -367,6 +388,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if (i < nu && ok) {
                 const int st = i % WS, ms = i % MS;
                 ok = mbar_wait(&w_full[st], (uint32_t)((i / WS) & 1), &g_tc_error);
+                if (warp == TC_WORK0 && lane == 0) TC_TRACE(i, 2);
                 if (ok && qp == 0 && i >= MS)
                     ok = mbar_wait(&meta_empty[ms], (uint32_t)(((i / MS) - 1) & 1), &g_tc_error);
                 if (ok && i >= 1) ok = mbar_wait(&pl_empty[half], (uint32_t)((i - 1) & 1), &g_tc_error);
@@ -390,6 +412,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     if (lane == 0) mbar_arrive(&w_empty[st]);
                     fence_proxy_async_smem();
                     mbar_arrive(&pl_full[half]);
+                    if (warp == TC_WORK0 && lane == 0) TC_TRACE(i, 3);
                 }
             }
             if (i == 0) continue;
@@ -403,6 +426,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 for (int c = 0; c < NH; c++) yacc[c] = 0.0f;
             }
             if (ok) {
+                if (warp == TC_WORK0 && lane == 0) TC_TRACE(e, 6);
                 ok = mbar_wait(&acc_full[b], (uint32_t)((e >> 1) & 1), &g_tc_error) &&
                      mbar_wait(&meta_full[ms], (uint32_t)((e / MS) & 1), &g_tc_error) &&
                      mbar_wait(&row_full[ms], (uint32_t)((e / MS) & 1), &g_tc_error);
@@ -465,6 +489,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&meta_empty[ms]);
+                if (warp == TC_WORK0 && lane == 0) TC_TRACE(e, 7);
             }
             // ---- end of a tile segment: direct store, or partial + ticket (last arriver sums) ----
             if (e == nu - 1 || s == nb - 1) {
