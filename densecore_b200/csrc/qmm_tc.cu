@@ -97,8 +97,11 @@ struct TcCfg {
     static constexpr int AS = N >= 128 ? 2 : (N >= 64 ? 3 : 4);    // activation ring
     static constexpr int META = N * 4 + N * 16;                    // per column: dx, 8 pair sums
     static constexpr int OFF_BAR = 0;                              // barriers, flag, TMEM slot
-    static constexpr int OFF_PL = 1024;                            // planes [K half][H, L]
-    static constexpr int OFF_ACT = OFF_PL + 4 * TC_HPLANE;
+    // plane buffers: two (units alternate, so the prep of unit i+1 need not wait for unit i's
+    // MMAs) where shared memory allows, else one
+    static constexpr int PB = N <= 32 ? 2 : 1;
+    static constexpr int OFF_PL = 1024;                            // planes [buffer][K half][H, L]
+    static constexpr int OFF_ACT = OFF_PL + PB * 4 * TC_HPLANE;
     static constexpr int OFF_META = OFF_ACT + AS * AT;
     static constexpr int OFF_ROWP = OFF_META + TC_MS * META;       // [slot][128 rows] 16 B
     static constexpr int OFF_RAW = OFF_ROWP + TC_MS * TC_ROWS * 16;
@@ -197,9 +200,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint64_t* w_empty = w_full + WS;           // [WS] 16 prep warps read it
     uint64_t* a_full = w_empty + WS;           // [AS] activation tile landed (tx)
     uint64_t* a_empty = a_full + AS;           // [AS] MMAs that read it done
-    uint64_t* pl_full = a_empty + AS;          // [2] K-half planes written (256 prep threads)
-    uint64_t* pl_empty = pl_full + 2;          // [2] MMAs that read them done
-    uint64_t* acc_full = pl_empty + 2;         // [2] accumulators complete
+    uint64_t* pl_full = a_empty + AS;          // [PB][2] K-half planes written (256 prep threads)
+    uint64_t* pl_empty = pl_full + 2 * C::PB;  // [PB][2] MMAs that read them done
+    uint64_t* acc_full = pl_empty + 2 * C::PB; // [2] accumulators complete
     uint64_t* acc_empty = acc_full + 2;        // [2] 16 epilogue warps read them
     uint64_t* meta_full = acc_empty + 2;       // [MS] column metadata staged (32 producer lanes)
     uint64_t* row_full = meta_full + MS;       // [MS] row scales staged (128 prep threads)
@@ -227,9 +230,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_init(&a_full[s], 1);
             mbar_init(&a_empty[s], 1);
         }
-        for (int b = 0; b < 2; b++) {
+        for (int b = 0; b < 2 * C::PB; b++) {
             mbar_init(&pl_full[b], 256);
             mbar_init(&pl_empty[b], 1);
+        }
+        for (int b = 0; b < 2; b++) {
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], TC_WORKERS);
         }
@@ -341,10 +346,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const uint32_t dH = tmem + (uint32_t)(b * 2 * N), dL = dH + N;
 #pragma unroll
                 for (int h = 0; h < 2; h++) {
-                    ok = ok && mbar_wait(&pl_full[h], (uint32_t)(i & 1), &g_tc_error);
+                    const int pb = i % C::PB;
+                    ok = ok && mbar_wait(&pl_full[pb * 2 + h], (uint32_t)((i / C::PB) & 1), &g_tc_error);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t pH = smem_u32(planes + (size_t)(2 * h) * TC_HPLANE), pL = pH + TC_HPLANE;
+                    const uint32_t pH = smem_u32(planes + (size_t)(pb * 4 + 2 * h) * TC_HPLANE), pL = pH + TC_HPLANE;
 #pragma unroll
                     for (int j = 0; j < 4; j++) {   // k-step: K chunks 8h + 2j, 8h + 2j + 1
                         const uint64_t bd = umma_desc(pa + (h * 4 + j) * 2 * N * 16, N * 16, 128);
@@ -352,7 +358,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         mma_i8(dH, umma_desc(pH + j * 256, 128, TC_HSBO), bd, idesc, accum);
                         mma_i8(dL, umma_desc(pL + j * 256, 128, TC_HSBO), bd, idesc, accum);
                     }
-                    tc_commit(&pl_empty[h]);
+                    tc_commit(&pl_empty[pb * 2 + h]);
                 }
                 if (!ok) break;
                 tc_commit(&a_empty[st]);
@@ -391,7 +397,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if (warp == TC_WORK0 && lane == 0) TC_TRACE(i, 2);
                 if (ok && qp == 0 && i >= MS)
                     ok = mbar_wait(&meta_empty[ms], (uint32_t)(((i / MS) - 1) & 1), &g_tc_error);
-                if (ok && i >= 1) ok = mbar_wait(&pl_empty[half], (uint32_t)((i - 1) & 1), &g_tc_error);
+                const int pb = i % C::PB;
+                if (ok && i >= C::PB)
+                    ok = mbar_wait(&pl_empty[pb * 2 + half], (uint32_t)(((i / C::PB) - 1) & 1), &g_tc_error);
                 ok = __all_sync(0xffffffffu, ok);
                 if (ok) {
                     const uint8_t* src = raw + (size_t)st * C::WT + (size_t)row * TcW<TYPE>::ROWB;
@@ -406,12 +414,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         }
                         mbar_arrive(&row_full[ms]);
                     }
-                    uint8_t* pH = planes + (size_t)(2 * half) * TC_HPLANE + (size_t)(row >> 3) * TC_HSBO + (row & 7) * 16;
+                    uint8_t* pH = planes + (size_t)(pb * 4 + 2 * half) * TC_HPLANE + (size_t)(row >> 3) * TC_HSBO + (row & 7) * 16;
                     prep_quarter<TYPE>(src, qp, pH, pH + TC_HPLANE);
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&w_empty[st]);
                     fence_proxy_async_smem();
-                    mbar_arrive(&pl_full[half]);
+                    mbar_arrive(&pl_full[pb * 2 + half]);
                     if (warp == TC_WORK0 && lane == 0) TC_TRACE(i, 3);
                 }
             }
