@@ -113,6 +113,20 @@ struct TcCfg {
     static_assert(SMEM <= TC_SMEM_MAX, "shared memory");
 };
 
+// cp.async of 4 / 16 bytes global -> shared (src_bytes = 0: zero fill), and an arrive on an
+// mbarrier once this thread's earlier cp.asyncs have landed (counted as one expected arrival)
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // named barrier of the 16 prep / epilogue warps
 __device__ __forceinline__ void work_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
 
@@ -275,28 +289,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         pdl_wait();
     } else if (warp == 1) {
         // ---------------- activation producer + column metadata ----------------
-        // lane c stages columns c, c + 32, ...: their dx (and Q4_K pair sums) for unit i + 1 are
-        // loaded while unit i is handled, so the global-memory latency stays off the issue path
+        // lane c stages columns c, c + 32, ...: their dx (and Q4_K pair sums) arrive by cp.async
+        // straight into the metadata slot, which this lane's completion arrival marks full
         pdl_wait();
         constexpr int CPL = (N + 31) / 32;   // columns per lane
-        float ndx[CPL];
-        uint4 nbs[CPL];
-        auto load_meta = [&](int i) {
-            const int64_t u = u0 + i, tile = u / nb;
-            const int s = (int)(u % nb);
-            const int c0 = (int)(tile % ct_tiles) * N;
-#pragma unroll
-            for (int j = 0; j < CPL; j++) {
-                const int c = lane + 32 * j, col = c0 + c;
-                ndx[j] = 0.0f;
-                nbs[j] = make_uint4(0, 0, 0, 0);
-                if (i < nu && c < N && col < m) {
-                    ndx[j] = __ldg(&((const float*)a.d)[(size_t)col * nb + s]);
-                    if (Q4) nbs[j] = __ldg((const uint4*)(a.bs32 + ((size_t)col * nb + s) * 8));
-                }
-            }
-        };
-        load_meta(0);
         for (int i = 0; i < nu && ok; i++) {
             const int64_t u = u0 + i, tile = u / nb;
             const int s = (int)(u % nb), st = i % AS, ms = i % MS;
@@ -309,14 +305,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 mbar_arrive_expect_tx(&a_full[st], (uint32_t)C::AT);
                 tma_load_3d(act + (size_t)st * C::AT, &amap, 0, c0, s * 16, &a_full[st]);
             }
-            float cdx[CPL];
-            uint4 cbs[CPL];
-#pragma unroll
-            for (int j = 0; j < CPL; j++) {
-                cdx[j] = ndx[j];
-                cbs[j] = nbs[j];
-            }
-            load_meta(i + 1);
             if (i >= MS) ok = mbar_wait(&meta_empty[ms], (uint32_t)(((i / MS) - 1) & 1), &g_tc_error);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
@@ -324,13 +312,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             uint4* mbs = (uint4*)(mdx + N);
 #pragma unroll
             for (int j = 0; j < CPL; j++) {
-                const int c = lane + 32 * j;
+                const int c = lane + 32 * j, col = c0 + c;
                 if (c < N) {
-                    mdx[c] = cdx[j];
-                    if (Q4) mbs[c] = cbs[j];
+                    const bool live = col < m;
+                    const size_t e = live ? (size_t)col * nb + s : 0;
+                    cp_async4(&mdx[c], (const float*)a.d + e, live ? 4u : 0u);
+                    if (Q4) cp_async16(&mbs[c], a.bs32 + e * 8, live ? 16u : 0u);
                 }
             }
-            mbar_arrive(&meta_full[ms]);
+            cp_async_arrive(&meta_full[ms]);
         }
     } else if (warp == 2) {
         // ---------------- MMA issue ----------------
@@ -379,14 +369,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int row = quarter * 32 + lane;
         const int et = threadIdx.x - TC_WORK0 * 32;   // 0..511
         pdl_wait();   // y, the partials and the tickets may be in use by the previous kernel
-        float dnext = 0.0f;
-        auto load_d = [&](int i) -> float {   // Q6_K: the row's fp16 d of unit i (0 past the rows)
-            if (Q4 || i >= nu) return 0.0f;
+        // Q6_K: the row's fp16 d of unit i, fetched two units ahead by cp.async as the aligned pair of
+        // halves holding it (the epilogue picks the half) into the unit's row slot, whose row_full
+        // arrival is that copy's completion
+        auto fetch_d = [&](int i) {
+            if (Q4 || i >= nu) return;
             const int64_t u = u0 + i, tile = u / nb;
             const int64_t r = (tile / ct_tiles) * TC_ROWS + row;
-            return r < n ? __half2float(wd[r * nb + (u % nb)]) : 0.0f;
+            const size_t e = r < n ? (size_t)(r * nb + (u % nb)) & ~(size_t)1 : 0;
+            cp_async4(&rowp[(i % MS) * TC_ROWS + row], wd + e, r < n ? 4u : 0u);
+            cp_async_arrive(&row_full[i % MS]);
         };
-        if (!Q4 && qp == 0) dnext = load_d(0);
+        if (!Q4 && qp == 0) {
+            fetch_d(0);
+            fetch_d(1);
+        }
         float yacc[NH];
         int seg_s0 = 0;
         for (int i = 0; i <= nu; i++) {
@@ -408,11 +405,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                             const uint4 hdr = *(const uint4*)src;
                             const Q4kScales sc = q4k_unpack(hdr);
                             rowp[ms * TC_ROWS + row] = make_uint4(hdr.x, sc.mn03, sc.mn47, 0u);
-                        } else {
-                            rowp[ms * TC_ROWS + row] = make_uint4(__float_as_uint(dnext), 0u, 0u, 0u);
-                            dnext = load_d(i + 1);
+                            mbar_arrive(&row_full[ms]);
+                        } else if (i + 2 < nu) {   // the slot of unit i + 2 held unit i - 2
+                            const int m2 = (i + 2) % MS;
+                            if (i + 2 >= MS)
+                                ok = mbar_wait(&meta_empty[m2], (uint32_t)((((i + 2) / MS) - 1) & 1), &g_tc_error);
+                            fetch_d(i + 2);
                         }
-                        mbar_arrive(&row_full[ms]);
                     }
                     uint8_t* pH = planes + (size_t)(pb * 4 + 2 * half) * TC_HPLANE + (size_t)(row >> 3) * TC_HSBO + (row & 7) * 16;
                     prep_quarter<TYPE>(src, qp, pH, pH + TC_HPLANE);
@@ -446,7 +445,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const uint4 rp = rowp[ms * TC_ROWS + row];
                 const float* mdx = (const float*)(meta + (size_t)ms * C::META) + qp * NH;
                 const uint4* mbs = (const uint4*)((const float*)(meta + (size_t)ms * C::META) + N) + qp * NH;
-                float2 dd = make_float2(__uint_as_float(rp.x), 0.0f);
+                float2 dd = make_float2(0.0f, 0.0f);
+                if (!Q4) {   // the fetched pair of halves; this unit's d is the one at an odd index or not
+                    const int64_t r = (tile / ct_tiles) * TC_ROWS + row;
+                    const __half2 pr = *reinterpret_cast<const __half2*>(&rp.x);
+                    dd.x = ((r * nb + s) & 1) ? __high2float(pr) : __low2float(pr);
+                }
                 int mp0 = 0, mp1 = 0, mp2 = 0, mp3 = 0;
                 if (Q4) {
                     dd = __half22float2(*reinterpret_cast<const __half2*>(&rp.x));
