@@ -43,9 +43,9 @@ namespace dcg {
 __device__ int g_tc_error = 0;
 
 // Pipeline timeline for tuning, compiled in only with -DDCG_TC_TRACE (never in the library build):
-// clock64 stamps of 8 events for the first 64 units of CTAs 0-3 (g_tc_trace[cta][unit][event]).
+// clock64 stamps of 12 events for the first 64 units of CTAs 0-3 (g_tc_trace[cta][unit][event]).
 #ifdef DCG_TC_TRACE
-__device__ long long g_tc_trace[4][64][8];
+__device__ long long g_tc_trace[4][64][12];
 #define TC_TRACE(i, ev)                                                                            \
     do {                                                                                           \
         if (blockIdx.x < 4 && (i) < 64) g_tc_trace[blockIdx.x][(i)][(ev)] = clock64();             \
@@ -398,6 +398,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if (ok && i >= C::PB)
                     ok = mbar_wait(&pl_empty[pb * 2 + half], (uint32_t)(((i / C::PB) - 1) & 1), &g_tc_error);
                 ok = __all_sync(0xffffffffu, ok);
+                if (warp == TC_WORK0 && lane == 0) TC_TRACE(i, 8);
                 if (ok) {
                     const uint8_t* src = raw + (size_t)st * C::WT + (size_t)row * TcW<TYPE>::ROWB;
                     if (qp == 0) {   // the row's scales of this unit, for the epilogue
@@ -415,6 +416,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     }
                     uint8_t* pH = planes + (size_t)(pb * 4 + 2 * half) * TC_HPLANE + (size_t)(row >> 3) * TC_HSBO + (row & 7) * 16;
                     prep_quarter<TYPE>(src, qp, pH, pH + TC_HPLANE);
+                    if (warp == TC_WORK0 && lane == 0) TC_TRACE(i, 9);
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&w_empty[st]);
                     fence_proxy_async_smem();
@@ -439,6 +441,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                      mbar_wait(&row_full[ms], (uint32_t)((e / MS) & 1), &g_tc_error);
                 ok = __all_sync(0xffffffffu, ok);   // warp-uniform: the TMEM loads are .sync.aligned
             }
+            if (warp == TC_WORK0 && lane == 0) TC_TRACE(e, 10);
             if (ok) {
                 tc_fence_after();
                 const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 2 * N + qp * NH);
@@ -475,6 +478,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         tmem_ld4(lane_addr + N + cc, lv);
                     }
                     tmem_wait_ld();
+                    if (cc == 0 && warp == TC_WORK0 && lane == 0) TC_TRACE(e, 11);
                     if (cc + CH == NH) {   // every read of this buffer issued and complete
                         tc_fence_before();
                         __syncwarp();
