@@ -29,7 +29,7 @@
 
 namespace dcg {
 
-constexpr int HD = 128;        // head_dim (all BASELINE configs)
+constexpr int HD = 128;        // head_dim (Qwen3 and Llama-3 layouts; the entry points reject others)
 constexpr int KVB = 16;        // tokens per KV block
 constexpr float LOG2E = 1.4426950408889634f;
 
