@@ -614,7 +614,10 @@ static TcPlan tc_plan(int64_t n, int64_t k, int64_t m) {
     p.rt = (n + TC_ROWS - 1) / TC_ROWS;
     p.T = p.rt * p.ct * (k / QK_K);
     const int64_t sms = num_sms();
-    p.G = p.T < sms ? p.T : sms;
+    // at least sk_min_units() units per CTA (tuning knob DCG_SK_MIN_UNITS), at most one CTA per SM
+    const int64_t mu = sk_min_units();
+    const int64_t want = (p.T + mu - 1) / mu;
+    p.G = want < sms ? want : sms;
     return p;
 }
 

@@ -3,6 +3,7 @@
 // and the stream-K work split.
 #pragma once
 #include <stdint.h>
+#include <stdlib.h>
 
 #include "tma.cuh"
 
@@ -79,5 +80,16 @@ __device__ __forceinline__ float i2f_exact22(int v) { return __int_as_float(0x4B
 // stream-K ranges: CTA c owns units [begin(c), begin(c+1)); owner(u) is the CTA whose range holds u
 __host__ __device__ __forceinline__ int64_t sk_begin(int64_t c, int64_t T, int64_t G) { return c * T / G; }
 __device__ __forceinline__ int64_t sk_owner(int64_t u, int64_t T, int64_t G) { return ((u + 1) * G - 1) / T; }
+
+// minimum stream-K units per CTA when the matrix has fewer units than SMs (DCG_SK_MIN_UNITS
+// overrides it for tuning)
+inline int64_t sk_min_units() {
+    static const int64_t v = [] {
+        const char* e = getenv("DCG_SK_MIN_UNITS");
+        const long x = e ? atol(e) : 1;
+        return (int64_t)(x > 0 ? x : 1);
+    }();
+    return v;
+}
 
 }  // namespace dcg
