@@ -653,6 +653,46 @@ def profile_case(args):
     print("profile case done", qtype, n, k, m)
 
 
+def copy_ceiling():
+    """What one launch can stream at the mat-vec's sizes: torch device-to-device copies of 17.8 MB
+    (the Q8_0 4096x4096 weight) and 33 MB (one Q4_K FFN matrix), back to back in a CUDA graph over
+    a ring of buffers larger than L2; GB/s counts the bytes read (the mat-vec's traffic is reads)."""
+    import torch
+    torch.cuda.set_device(0)
+    out = []
+    for nbytes in (17_825_792, 33_030_144):
+        ring = max(4, -(-512 * 2**20 // nbytes))
+        src = [torch.empty(nbytes, dtype=torch.uint8, device="cuda").fill_(1) for _ in range(ring)]
+        dst = [torch.empty(nbytes // 16, dtype=torch.uint8, device="cuda") for _ in range(ring)]
+        # read nbytes, write 1/16 of it: a read-dominated stream like the mat-vec's
+        views = [s.view(16, -1) for s in src]
+
+        def once():
+            for v, d in zip(views, dst):
+                torch.sum(v, dim=0, dtype=torch.uint8, out=d)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            once()
+        torch.cuda.current_stream().wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            once()
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 20
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * ring)
+        out.append({"bytes_read": nbytes, "us_per_launch": round(us, 2), "read_gbs": round(nbytes / us / 1e3, 1)})
+    print(json.dumps({"copy_ceiling": out}))
+
+
 def attn_case(which: str, iters: int):
     """One layer of config-3/4 paged decode attention (n_layer = 1 arena), eager, for ncu."""
     import numpy as np
@@ -712,6 +752,8 @@ def main():
     ap.add_argument("--profile-shape", default="up", choices=["up", "down", "sq"])
     ap.add_argument("--profile-m", type=int, default=1)
     ap.add_argument("--profile-iters", type=int, default=6)
+    ap.add_argument("--copy-ceiling", action="store_true",
+                    help="only time a read-dominated torch stream at the mat-vec sizes and exit")
     ap.add_argument("--profile-attn", default=None, choices=["3", "4"],
                     help="run only one layer's paged decode attention of config 3/4 (for ncu)")
     ap.add_argument("--profile-decode", default=None, choices=["3", "4"],
@@ -719,6 +761,9 @@ def main():
     args = ap.parse_args()
     if args.profile_type:
         profile_case(args)
+        return
+    if args.copy_ceiling:
+        copy_ceiling()
         return
     if args.decode_70b:
         decode_70b(args)
