@@ -318,8 +318,16 @@ constexpr int M1_STAGE = QMM_ROWS * M1_SROW;       // one super-block of 64 rows
 constexpr int M1_HDR = 512;                        // barriers | zero pad | 64 row partials
 constexpr int M1_XQ = QK_K + 16 + 4;               // per super-block: quants, pair sums, d
 constexpr int M1_MAX_SPS = 32;                     // activation slice: at most 32 super-blocks
-constexpr int M1_CTAS = 4;     // resident CTAs per SM (swept 2..6 x 2..7 stages on config 2)
-constexpr int M1_STAGES = 4;   // weight ring depth
+// resident CTAs per SM and weight ring depth (swept 2..6 x 2..7 on config 2; the macros exist only
+// for such sweeps)
+#ifndef DCG_M1_CTAS
+#define DCG_M1_CTAS 4
+#endif
+#ifndef DCG_M1_STAGES
+#define DCG_M1_STAGES 4
+#endif
+constexpr int M1_CTAS = DCG_M1_CTAS;
+constexpr int M1_STAGES = DCG_M1_STAGES;
 constexpr int M1_MAX_CLUSTER = 8;                  // portable cluster size bounds the splits
 
 template <bool QX>
