@@ -52,15 +52,35 @@ void set_error(const std::string& m) { g_last_error = m; }
 // ------------------------------------------------------------------------------------------
 // scratch of dcg_mul_mat: [quantized activation | matmul tickets + split-K partials]
 // (the matmul part: the tcgen05 kernel for m >= 2 Q4_K / Q6_K, the Q4_K M = 1 kernel's fallback)
-static bool use_tc(int type, int64_t n, int64_t k, int64_t m) { return dcg::qmm_tc_supports(type, n, k, m); }
+// Batches up to DCG_MMA_MAX_M (default 0: none) take the register-fed mma.sync kernels instead of the
+// tcgen05 ones, for side-by-side measurement
+static int64_t mma_max_m() {
+    static const int64_t v = [] {
+        const char* e = getenv("DCG_MMA_MAX_M");
+        return e ? (int64_t)atoll(e) : (int64_t)0;
+    }();
+    return v;
+}
+static bool use_tc(int type, int64_t n, int64_t k, int64_t m) {
+    return m > mma_max_m() && dcg::qmm_tc_supports(type, n, k, m);
+}
+// Q8_0 weights of up to 16M elements at m <= 64 (the projections of a small model's decode step)
+// run faster on the register-fed mma.sync kernel (qmm_rd.cu): measured on B200 at m = 64, 4096x1024
+// 8.1 vs 11.7 us, 6144x1024 11.7 vs 19.7 us, 1024x3072 12.9 vs 14.9 us; the tcgen05 kernel keeps
+// the large ones (151936x1024: 106 vs 176 us)
+static bool use_q8tc(int type, int64_t n, int64_t k, int64_t m) {
+    if (type == DCG_TYPE_Q8_0 && m <= 64 && n * k <= (int64_t)16 << 20 && dcg::qmm_rd_supports(type, k, m))
+        return false;
+    return m > mma_max_m() && dcg::qmm_q8tc_supports(type, n, k, m);
+}
 static size_t qmm_part(int type, int64_t n, int64_t k, int64_t m) {
     if (use_tc(type, n, k, m)) return dcg::qmm_tc_scratch_bytes(type, n, k, m);
-    if (dcg::qmm_q8tc_supports(type, n, k, m)) return dcg::qmm_q8tc_scratch_bytes(n, k, m);
+    if (use_q8tc(type, n, k, m)) return dcg::qmm_q8tc_scratch_bytes(n, k, m);
     return dcg::qmm_supports(type) ? dcg::qmm_scratch_bytes(type, n, k, m) : 0;
 }
 static int qmm_tickets(int type, int64_t n, int64_t k, int64_t m) {
     if (use_tc(type, n, k, m)) return dcg::qmm_tc_ticket_count(type, n, k, m);
-    if (dcg::qmm_q8tc_supports(type, n, k, m)) return dcg::qmm_q8tc_ticket_count(n, k, m);
+    if (use_q8tc(type, n, k, m)) return dcg::qmm_q8tc_ticket_count(n, k, m);
     return dcg::qmm_supports(type) ? dcg::qmm_ticket_count(type, n, m) : 0;
 }
 
@@ -84,7 +104,7 @@ static int enqueue_mul_mat_q(int type, const void* w, int64_t n, int64_t k, cons
         DCG_CUDA(dcg::launch_qmm_tc(type, w, n, k, act, m, y, qscratch, st), "qmm_tc");
         return DCG_OK;
     }
-    if (dcg::qmm_q8tc_supports(type, n, k, m)) {
+    if (use_q8tc(type, n, k, m)) {
         DCG_CUDA(dcg::launch_qmm_q8tc(w, n, k, act, m, y, qscratch, st), "qmm_q8tc");
         return DCG_OK;
     }

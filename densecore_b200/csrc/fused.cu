@@ -40,7 +40,78 @@ __device__ __forceinline__ float rms_scale(double sumsq, int64_t k, float eps) {
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
 }
 
-// one CTA per activation row
+// one CTA per activation row, the row staged in shared memory: every thread issues all of its
+// 16-byte loads of x (and delta) before it uses one, so a row costs one memory latency instead of one
+// per element; the norm weight (constant) is staged before the wait on the producing kernel.
+// x, delta and weight 16-byte aligned, k <= RMS_MAX_K.
+constexpr int RMS_MAX_K = 8192;
+__global__ void __launch_bounds__(FUSE_THREADS) add_rmsnorm_quant_v4_kernel(
+    float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w, float eps,
+    int64_t k, int act_type, ActQ a) {
+    __shared__ double red[FUSE_THREADS / 32];
+    extern __shared__ float4 rms_sm[];   // [k/4] x, then [k/4] weight
+    const int k4 = (int)(k / 4);
+    float4* xs = rms_sm;
+    float4* ws = rms_sm + k4;
+    for (int i = threadIdx.x; i < k4; i += FUSE_THREADS) ws[i] = __ldg((const float4*)w + i);
+    pdl_wait();
+    pdl_trigger();
+    const int64_t row = blockIdx.x;
+    float4* xr = (float4*)(x + row * k);
+    const float4* dr = delta ? (const float4*)(delta + row * k) : nullptr;
+    double ss = 0.0;
+    constexpr int U = RMS_MAX_K / 4 / FUSE_THREADS;   // 16-byte vectors per thread at most
+    float4 v[U], d[U];
+#pragma unroll
+    for (int j = 0; j < U; j++) {
+        const int i = threadIdx.x + j * FUSE_THREADS;
+        if (i < k4) {
+            v[j] = xr[i];
+            if (dr) d[j] = dr[i];
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < U; j++) {
+        const int i = threadIdx.x + j * FUSE_THREADS;
+        if (i < k4) {
+            float4 t = v[j];
+            if (dr) {
+                t.x = __fadd_rn(t.x, d[j].x);
+                t.y = __fadd_rn(t.y, d[j].y);
+                t.z = __fadd_rn(t.z, d[j].z);
+                t.w = __fadd_rn(t.w, d[j].w);
+                xr[i] = t;
+            }
+            xs[i] = t;
+            ss += (double)__fmul_rn(t.x, t.x);
+            ss += (double)__fmul_rn(t.y, t.y);
+            ss += (double)__fmul_rn(t.z, t.z);
+            ss += (double)__fmul_rn(t.w, t.w);
+        }
+    }
+    const float rs = rms_scale(block_sum(ss, red), k, eps);  // block_sum's barrier publishes xs
+    const float* xf = (const float*)xs;
+    const float* wf = (const float*)ws;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (act_type == DCG_TYPE_Q8_0) {
+        for (int64_t b = warp; b < k / QK8_0; b += nw) {
+            const int64_t i = b * QK8_0 + lane;
+            warp_q8_0_store(__fmul_rn(__fmul_rn(xf[i], rs), wf[i]), lane, a, row * (k / QK8_0) + b);
+        }
+    } else {
+        for (int64_t b = warp; b < k / QK_K; b += nw) {
+            float vv[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int64_t i = b * QK_K + lane * 8 + j;
+                vv[j] = __fmul_rn(__fmul_rn(xf[i], rs), wf[i]);
+            }
+            warp_q8_K_store(vv, lane, a, row * (k / QK_K) + b);
+        }
+    }
+}
+
+// general form (any alignment, any k): one CTA per activation row
 __global__ void __launch_bounds__(FUSE_THREADS) add_rmsnorm_quant_kernel(
     float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w, float eps,
     int64_t k, int act_type, ActQ a) {
@@ -168,6 +239,14 @@ __global__ void __launch_bounds__(FUSE_THREADS) qk_rope_append_kernel(
 cudaError_t launch_add_rmsnorm_quant(float* x, const float* delta, const float* w, float eps, int64_t m,
                                      int64_t k, int act_type, void* act, cudaStream_t st) {
     const ActQ a = act_view(act_type, act, m, k);
+    const bool a16 = ((uintptr_t)x | (uintptr_t)delta | (uintptr_t)w) % 16 == 0;
+    if (a16 && k <= RMS_MAX_K && k % 4 == 0) {
+        const size_t smem = (size_t)k * 8;
+        cudaError_t e = DCG_SMEM_ATTR(add_rmsnorm_quant_v4_kernel, RMS_MAX_K * 8);
+        if (e != cudaSuccess) return e;
+        return launch_pdl(add_rmsnorm_quant_v4_kernel, dim3((unsigned)m), dim3(FUSE_THREADS), smem, st, x, delta, w,
+                          eps, k, act_type, a);
+    }
     return launch_pdl(add_rmsnorm_quant_kernel, dim3((unsigned)m), dim3(FUSE_THREADS), 0, st, x, delta, w, eps,
                       k, act_type, a);
 }
