@@ -99,16 +99,21 @@ struct TcCfg {
     static constexpr int OFF_BAR = 0;                              // barriers, flag, TMEM slot
     // plane buffers: two (units alternate, so the prep of unit i+1 need not wait for unit i's
     // MMAs) where shared memory allows, else one
-    static constexpr int PB = N <= 32 ? 2 : 1;
+    // TA: the planes live in tensor memory (A operand read from TMEM), for N <= 64, where they fit
+    // beside the accumulators: columns [0, 4N) accumulators, [256 + 128 pb + 64 h, +32) H and
+    // [+32, +64) L of plane buffer pb, K half h.  Otherwise in shared memory.
+    static constexpr bool TA = N <= 64;
+    static constexpr int PB = (TA || N <= 32) ? 2 : 1;
     static constexpr int OFF_PL = 1024;                            // planes [buffer][K half][H, L]
-    static constexpr int OFF_ACT = OFF_PL + PB * 4 * TC_HPLANE;
+    static constexpr int OFF_ACT = OFF_PL + (TA ? 0 : PB * 4 * TC_HPLANE);
     static constexpr int OFF_META = OFF_ACT + AS * AT;
     static constexpr int OFF_ROWP = OFF_META + TC_MS * META;       // [slot][128 rows] 16 B
     static constexpr int OFF_RAW = OFF_ROWP + TC_MS * TC_ROWS * 16;
     static constexpr int WS_FIT = (TC_SMEM_MAX - OFF_RAW) / WT;
     static constexpr int WS = WS_FIT > 8 ? 8 : WS_FIT;             // weight ring
     static constexpr int SMEM = OFF_RAW + WS * WT;
-    static constexpr int TMEM_COLS = 4 * N;                        // [2 buffers][C_H, C_L] x N
+    static constexpr int TMEM_COLS = TA ? 512 : 4 * N;             // [2 buffers][C_H, C_L] x N (+ planes)
+    static constexpr int TMEM_PL = 256;
     static_assert(WS >= 2, "weight ring too shallow");
     static_assert(SMEM <= TC_SMEM_MAX, "shared memory");
 };
@@ -134,29 +139,23 @@ __device__ __forceinline__ void work_bar() { asm volatile("bar.sync 1, 512;" :::
 // (16 elements each) of quarter p: K half h = p / 2, chunks j = 4 (p % 2) .. +3 of that half ----
 // Q4_K quarter p = sub-blocks 2p (low nibbles of byte group p) and 2p + 1 (its high nibbles)
 template <int TYPE, typename std::enable_if<TYPE == DCG_TYPE_Q4_K, int>::type = 0>
-__device__ __forceinline__ void prep_quarter(const uint8_t* row, int p, uint8_t* pH, uint8_t* pL) {
+__device__ __forceinline__ void prep_quarter(const uint8_t* row, int p, uint32_t (&H)[16], uint32_t (&L)[16]) {
     const uint4 hdr = *(const uint4*)row;
     const uint4 g0 = *(const uint4*)(row + 16 + 32 * p), g1 = *(const uint4*)(row + 32 + 32 * p);
     const Q4kScales sc = q4k_unpack(hdr);
     const uint32_t w[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-    const int j0 = 4 * (p & 1);
 #pragma unroll
     for (int c = 0; c < 4; c++) {
         const int sbk = 2 * p + (c >> 1);   // chunks 0, 1: sub-block 2p; 2, 3: sub-block 2p + 1
         const uint32_t scs = ((sbk < 4 ? sc.sc03 : sc.sc47) >> (8 * (sbk & 3))) & 0x3Fu;
         const uint32_t sh = scs >> 3, sl = scs & 7u;
-        uint4 vh, vl;
-        uint32_t* ph = (uint32_t*)&vh;
-        uint32_t* pl = (uint32_t*)&vl;
 #pragma unroll
         for (int t = 0; t < 4; t++) {
             const uint32_t word = w[(c & 1) * 4 + t];
             const uint32_t nib = (c >> 1) ? (word >> 4) & 0x0F0F0F0Fu : word & 0x0F0F0F0Fu;
-            ph[t] = nib * sh;
-            pl[t] = nib * sl;
+            H[4 * c + t] = nib * sh;
+            L[4 * c + t] = nib * sl;
         }
-        *(uint4*)(pH + (j0 + c) * 128) = vh;
-        *(uint4*)(pL + (j0 + c) * 128) = vl;
     }
 }
 
@@ -166,7 +165,7 @@ __device__ __forceinline__ void prep_quarter(const uint8_t* row, int p, uint8_t*
 // 32-bit word (16-bit lanes, biased by 32768 so no lane borrows): V = (u0 | u1 << 16) sc + K with
 // K = (32768 - 32 sc) in both lanes; then L = V & 127 and H = (V >> 7) & 255 per lane.
 template <int TYPE, typename std::enable_if<TYPE == DCG_TYPE_Q6_K, int>::type = 0>
-__device__ __forceinline__ void prep_quarter(const uint8_t* row, int p, uint8_t* pH, uint8_t* pL) {
+__device__ __forceinline__ void prep_quarter(const uint8_t* row, int p, uint32_t (&H)[16], uint32_t (&L)[16]) {
     const int h = p >> 1, j0 = 4 * (p & 1);
     const uint32_t scw = *(const uint32_t*)(row + 192 + 8 * h + j0);   // scales of chunks j0 .. j0+3
     uint4 ql[4], qh[2];
@@ -184,19 +183,26 @@ __device__ __forceinline__ void prep_quarter(const uint8_t* row, int p, uint8_t*
         const uint32_t kk = (uint32_t)(32768 - 32 * sc) * 0x10001u;
         const uint32_t* qlw = (const uint32_t*)&ql[c];
         const uint32_t* qhw = (const uint32_t*)&qh[c & 1];
-        uint4 vh, vl;
-        uint32_t* ph = (uint32_t*)&vh;
-        uint32_t* pl = (uint32_t*)&vl;
 #pragma unroll
         for (int t = 0; t < 4; t++) {
             const uint32_t u = ((qlw[t] >> (4 * (grp >> 1))) & 0x0F0F0F0Fu) | (((qhw[t] >> (2 * grp)) & 0x03030303u) << 4);
             const uint32_t v01 = __byte_perm(u, 0u, 0x4140u) * (uint32_t)sc + kk;
             const uint32_t v23 = __byte_perm(u, 0u, 0x4342u) * (uint32_t)sc + kk;
-            pl[t] = __byte_perm(v01 & 0x007F007Fu, v23 & 0x007F007Fu, 0x6420u);
-            ph[t] = __byte_perm((v01 >> 7) & 0x00FF00FFu, (v23 >> 7) & 0x00FF00FFu, 0x6420u);
+            L[4 * c + t] = __byte_perm(v01 & 0x007F007Fu, v23 & 0x007F007Fu, 0x6420u);
+            H[4 * c + t] = __byte_perm((v01 >> 7) & 0x00FF00FFu, (v23 >> 7) & 0x00FF00FFu, 0x6420u);
         }
-        *(uint4*)(pH + j * 128) = vh;
-        *(uint4*)(pL + j * 128) = vl;
+    }
+}
+
+// the 4 chunks of quarter p (chunks 4 (p % 2) .. +3 of its K half) into shared-memory planes laid out
+// as core matrices: 16-B K chunks 128 B apart
+__device__ __forceinline__ void planes_store(const uint32_t (&H)[16], const uint32_t (&L)[16], int p, uint8_t* pH,
+                                             uint8_t* pL) {
+    const int j0 = 4 * (p & 1);
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        *(uint4*)(pH + (j0 + c) * 128) = make_uint4(H[4 * c], H[4 * c + 1], H[4 * c + 2], H[4 * c + 3]);
+        *(uint4*)(pL + (j0 + c) * 128) = make_uint4(L[4 * c], L[4 * c + 1], L[4 * c + 2], L[4 * c + 3]);
     }
 }
 
@@ -340,13 +346,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     ok = ok && mbar_wait(&pl_full[pb * 2 + h], (uint32_t)((i / C::PB) & 1), &g_tc_error);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t pH = smem_u32(planes + (size_t)(pb * 4 + 2 * h) * TC_HPLANE), pL = pH + TC_HPLANE;
+                    if (C::TA) {
+                        const uint32_t tH = tmem + (uint32_t)(C::TMEM_PL + pb * 128 + h * 64), tL = tH + 32;
 #pragma unroll
-                    for (int j = 0; j < 4; j++) {   // k-step: K chunks 8h + 2j, 8h + 2j + 1
-                        const uint64_t bd = umma_desc(pa + (h * 4 + j) * 2 * N * 16, N * 16, 128);
-                        const uint32_t accum = (h | j) ? 1u : 0u;
-                        mma_i8(dH, umma_desc(pH + j * 256, 128, TC_HSBO), bd, idesc, accum);
-                        mma_i8(dL, umma_desc(pL + j * 256, 128, TC_HSBO), bd, idesc, accum);
+                        for (int j = 0; j < 4; j++) {   // k-step: K elements 32j .. +31 of the half
+                            const uint64_t bd = umma_desc(pa + (h * 4 + j) * 2 * N * 16, N * 16, 128);
+                            const uint32_t accum = (h | j) ? 1u : 0u;
+                            mma_i8_ta(dH, tH + 8 * j, bd, idesc, accum);
+                            mma_i8_ta(dL, tL + 8 * j, bd, idesc, accum);
+                        }
+                    } else {
+                        const uint32_t pH = smem_u32(planes + (size_t)(pb * 4 + 2 * h) * TC_HPLANE), pL = pH + TC_HPLANE;
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {   // k-step: K chunks 8h + 2j, 8h + 2j + 1
+                            const uint64_t bd = umma_desc(pa + (h * 4 + j) * 2 * N * 16, N * 16, 128);
+                            const uint32_t accum = (h | j) ? 1u : 0u;
+                            mma_i8(dH, umma_desc(pH + j * 256, 128, TC_HSBO), bd, idesc, accum);
+                            mma_i8(dL, umma_desc(pL + j * 256, 128, TC_HSBO), bd, idesc, accum);
+                        }
                     }
                     tc_commit(&pl_empty[pb * 2 + h]);
                 }
@@ -414,12 +431,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                             fetch_d(i + 2);
                         }
                     }
-                    uint8_t* pH = planes + (size_t)(pb * 4 + 2 * half) * TC_HPLANE + (size_t)(row >> 3) * TC_HSBO + (row & 7) * 16;
-                    prep_quarter<TYPE>(src, qp, pH, pH + TC_HPLANE);
+                    uint32_t hv[16], lv[16];
+                    prep_quarter<TYPE>(src, qp, hv, lv);
+                    if (C::TA) {
+                        // the MMAs that read this plane buffer have retired (pl_empty); order the
+                        // stores after them, and the next MMAs after the stores
+                        tc_fence_after();
+                        const uint32_t tH = tmem + ((uint32_t)(quarter * 32) << 16) +
+                                            (uint32_t)(C::TMEM_PL + pb * 128 + half * 64 + 16 * (qp & 1));
+                        tmem_st16(tH, hv);
+                        tmem_st16(tH + 32, lv);
+                        tmem_wait_st();
+                        tc_fence_before();
+                    } else {
+                        uint8_t* pH = planes + (size_t)(pb * 4 + 2 * half) * TC_HPLANE + (size_t)(row >> 3) * TC_HSBO + (row & 7) * 16;
+                        planes_store(hv, lv, qp, pH, pH + TC_HPLANE);
+                    }
                     if (warp == TC_WORK0 && lane == 0) TC_TRACE(i, 9);
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&w_empty[st]);
-                    fence_proxy_async_smem();
+                    if (!C::TA) fence_proxy_async_smem();
                     mbar_arrive(&pl_full[pb * 2 + half]);
                     if (warp == TC_WORK0 && lane == 0) TC_TRACE(i, 3);
                 }
