@@ -132,8 +132,12 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// named barrier of the 16 prep / epilogue warps
-__device__ __forceinline__ void work_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+// named barrier of the draining warps: all 16 workers, or the 8 epilogue-only warps (SPLIT)
+template <bool SPLIT>
+__device__ __forceinline__ void work_bar() {
+    if (SPLIT) asm volatile("bar.sync 1, 256;" ::: "memory");
+    else asm volatile("bar.sync 1, 512;" ::: "memory");
+}
 
 // ---- prep: one weight row of one super-block (in shared memory) -> the two planes' 4 K chunks
 // (16 elements each) of quarter p: K half h = p / 2, chunks j = 4 (p % 2) .. +3 of that half ----
@@ -244,24 +248,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < WS; s++) {
             mbar_init(&w_full[s], 1);
-            mbar_init(&w_empty[s], TC_WORKERS);
+            mbar_init(&w_empty[s], C::TA ? TC_WORKERS / 2 : TC_WORKERS);
         }
         for (int s = 0; s < AS; s++) {
             mbar_init(&a_full[s], 1);
             mbar_init(&a_empty[s], 1);
         }
         for (int b = 0; b < 2 * C::PB; b++) {
-            mbar_init(&pl_full[b], 256);
+            mbar_init(&pl_full[b], C::TA ? 128 : 256);
             mbar_init(&pl_empty[b], 1);
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], TC_WORKERS);
+            mbar_init(&acc_empty[b], C::TA ? TC_WORKERS / 2 : TC_WORKERS);
         }
         for (int s = 0; s < MS; s++) {
             mbar_init(&meta_full[s], 32);
             mbar_init(&row_full[s], 128);
-            mbar_init(&meta_empty[s], TC_WORKERS);
+            mbar_init(&meta_empty[s], C::TA ? TC_WORKERS / 2 : TC_WORKERS);
         }
         mbar_init(mma_done, 1);
         fence_mbar_init();
@@ -380,11 +384,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // Iteration i expands unit i's weights (quarter qp of its row's K) and then drains unit
         // i-1's accumulators (quarter qp of the columns): unit i's MMAs run while unit i-1 is
         // drained.
-        constexpr int NH = N / 4;                       // columns per thread
-        const int quarter = warp & 3, qp = (warp - TC_WORK0) >> 2;   // TMEM lane group, K / column quarter
+        // SPLIT (planes in tensor memory): warps 4-11 only expand (thread = row x K half, two K
+        // quarters) and warps 12-19 only drain (thread = row x half of the columns), so the prep of
+        // unit i+1 overlaps the drain of unit i instead of following it.  Otherwise each of the 16
+        // warps does both, for a K quarter and a quarter of the columns.
+        constexpr bool SPLIT = C::TA;
+        constexpr int NH = SPLIT ? N / 2 : N / 4;      // columns per thread
+        const int quarter = warp & 3, grp = (warp - TC_WORK0) >> 2;   // TMEM lane group, warp group
+        const bool do_prep = !SPLIT || grp < 2, do_epi = !SPLIT || grp >= 2;
+        const int qp = SPLIT ? (do_prep ? 2 * grp : 0) : grp;   // (first) K quarter this thread expands
         const int half = qp >> 1;                     // the K half this thread's prep writes
+        const int cq = SPLIT ? grp - 2 : grp;         // column part this thread drains
         const int row = quarter * 32 + lane;
-        const int et = threadIdx.x - TC_WORK0 * 32;   // 0..511
+        const int et = threadIdx.x - (SPLIT ? TC_WORK0 + 8 : TC_WORK0) * 32;   // among the draining threads
         pdl_wait();   // y, the partials and the tickets may be in use by the previous kernel
         // Q6_K: the row's fp16 d of unit i, fetched two units ahead by cp.async as the aligned pair of
         // halves holding it (the epilogue picks the half) into the unit's row slot, whose row_full
@@ -397,7 +409,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             cp_async4(&rowp[(i % MS) * TC_ROWS + row], wd + e, r < n ? 4u : 0u);
             cp_async_arrive(&row_full[i % MS]);
         };
-        if (!Q4 && qp == 0) {
+        if (!Q4 && do_prep && qp == 0) {
             fetch_d(0);
             fetch_d(1);
         }
@@ -405,7 +417,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         int seg_s0 = 0;
         for (int i = 0; i <= nu; i++) {
             // ---- prep of unit i ----
-            if (i < nu && ok) {
+            if (do_prep && i < nu && ok) {
                 const int st = i % WS, ms = i % MS;
                 ok = mbar_wait(&w_full[st], (uint32_t)((i / WS) & 1), &g_tc_error);
                 if (warp == TC_WORK0 && lane == 0) TC_TRACE(i, 2);
@@ -432,18 +444,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         }
                     }
                     uint32_t hv[16], lv[16];
-                    prep_quarter<TYPE>(src, qp, hv, lv);
                     if (C::TA) {
                         // the MMAs that read this plane buffer have retired (pl_empty); order the
                         // stores after them, and the next MMAs after the stores
                         tc_fence_after();
-                        const uint32_t tH = tmem + ((uint32_t)(quarter * 32) << 16) +
-                                            (uint32_t)(C::TMEM_PL + pb * 128 + half * 64 + 16 * (qp & 1));
-                        tmem_st16(tH, hv);
-                        tmem_st16(tH + 32, lv);
+#pragma unroll
+                        for (int q2 = 0; q2 < (SPLIT ? 2 : 1); q2++) {
+                            prep_quarter<TYPE>(src, qp + q2, hv, lv);
+                            const uint32_t tH = tmem + ((uint32_t)(quarter * 32) << 16) +
+                                                (uint32_t)(C::TMEM_PL + pb * 128 + half * 64 + 16 * ((qp + q2) & 1));
+                            tmem_st16(tH, hv);
+                            tmem_st16(tH + 32, lv);
+                        }
                         tmem_wait_st();
                         tc_fence_before();
                     } else {
+                        prep_quarter<TYPE>(src, qp, hv, lv);
                         uint8_t* pH = planes + (size_t)(pb * 4 + 2 * half) * TC_HPLANE + (size_t)(row >> 3) * TC_HSBO + (row & 7) * 16;
                         planes_store(hv, lv, qp, pH, pH + TC_HPLANE);
                     }
@@ -455,7 +471,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     if (warp == TC_WORK0 && lane == 0) TC_TRACE(i, 3);
                 }
             }
-            if (i == 0) continue;
+            if (i == 0 || !do_epi) continue;
             // ---- epilogue of unit e = i - 1 ----
             const int e = i - 1;
             const int64_t u = u0 + e, tile = u / nb;
@@ -466,19 +482,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 for (int c = 0; c < NH; c++) yacc[c] = 0.0f;
             }
             if (ok) {
-                if (warp == TC_WORK0 && lane == 0) TC_TRACE(e, 6);
+                if (warp == TC_WORK0 + (SPLIT ? 8 : 0) && lane == 0) TC_TRACE(e, 6);
                 ok = mbar_wait(&acc_full[b], (uint32_t)((e >> 1) & 1), &g_tc_error) &&
                      mbar_wait(&meta_full[ms], (uint32_t)((e / MS) & 1), &g_tc_error) &&
                      mbar_wait(&row_full[ms], (uint32_t)((e / MS) & 1), &g_tc_error);
                 ok = __all_sync(0xffffffffu, ok);   // warp-uniform: the TMEM loads are .sync.aligned
             }
-            if (warp == TC_WORK0 && lane == 0) TC_TRACE(e, 10);
+            if (warp == TC_WORK0 + (SPLIT ? 8 : 0) && lane == 0) TC_TRACE(e, 10);
             if (ok) {
                 tc_fence_after();
-                const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 2 * N + qp * NH);
+                const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 2 * N + cq * NH);
                 const uint4 rp = rowp[ms * TC_ROWS + row];
-                const float* mdx = (const float*)(meta + (size_t)ms * C::META) + qp * NH;
-                const uint4* mbs = (const uint4*)((const float*)(meta + (size_t)ms * C::META) + N) + qp * NH;
+                const float* mdx = (const float*)(meta + (size_t)ms * C::META) + cq * NH;
+                const uint4* mbs = (const uint4*)((const float*)(meta + (size_t)ms * C::META) + N) + cq * NH;
                 float2 dd = make_float2(0.0f, 0.0f);
                 if (!Q4) {   // the fetched pair of halves; this unit's d is the one at an odd index or not
                     const int64_t r = (tile / ct_tiles) * TC_ROWS + row;
@@ -509,7 +525,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         tmem_ld4(lane_addr + N + cc, lv);
                     }
                     tmem_wait_ld();
-                    if (cc == 0 && warp == TC_WORK0 && lane == 0) TC_TRACE(e, 11);
+                    if (cc == 0 && warp == TC_WORK0 + (SPLIT ? 8 : 0) && lane == 0) TC_TRACE(e, 11);
                     if (cc + CH == NH) {   // every read of this buffer issued and complete
                         tc_fence_before();
                         __syncwarp();
@@ -536,14 +552,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&meta_empty[ms]);
-                if (warp == TC_WORK0 && lane == 0) TC_TRACE(e, 7);
+                if (warp == TC_WORK0 + (SPLIT ? 8 : 0) && lane == 0) TC_TRACE(e, 7);
             }
             // ---- end of a tile segment: direct store, or partial + ticket (last arriver sums) ----
             if (e == nu - 1 || s == nb - 1) {
                 const int64_t rt = tile / ct_tiles;
                 const int ct = (int)(tile % ct_tiles);
                 const int64_t r = rt * TC_ROWS + row;
-                const int cbase = ct * N + qp * NH;
+                const int cbase = ct * N + cq * NH;
                 if (seg_s0 == 0 && s == nb - 1) {
                     if (ok && r < n)
 #pragma unroll
@@ -554,9 +570,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     const int slot = sk_begin(bid, T, G) > t0 ? 0 : 1;
                     float* P = part + (size_t)(bid * 2 + slot) * N * TC_ROWS;
 #pragma unroll
-                    for (int c = 0; c < NH; c++) P[(qp * NH + c) * TC_ROWS + row] = yacc[c];
+                    for (int c = 0; c < NH; c++) P[(cq * NH + c) * TC_ROWS + row] = yacc[c];
                     __threadfence();
-                    work_bar();
+                    work_bar<SPLIT>();
                     const int64_t cf = sk_owner(t0, T, G), cl = sk_owner(t0 + nb - 1, T, G);
                     if (et == 0) {
                         const int old = atomicAdd(&tickets[tile], 1);
@@ -564,7 +580,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         if (last) tickets[tile] = 0;   // every contributor has arrived: ready for the next call
                         *last_flag = last;
                     }
-                    work_bar();
+                    work_bar<SPLIT>();
                     const int last = *last_flag;
                     if (last) {
                         __threadfence();
@@ -575,14 +591,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                             const int sq = sk_begin(q, T, G) > t0 ? 0 : 1;
                             const float* Q = part + (size_t)(q * 2 + sq) * N * TC_ROWS;
 #pragma unroll
-                            for (int c = 0; c < NH; c++) yacc[c] += __ldcg(&Q[(qp * NH + c) * TC_ROWS + row]);
+                            for (int c = 0; c < NH; c++) yacc[c] += __ldcg(&Q[(cq * NH + c) * TC_ROWS + row]);
                         }
                         if (ok && r < n)
 #pragma unroll
                             for (int c = 0; c < NH; c++)
                                 if (cbase + c < m) y[(size_t)(cbase + c) * n + r] = yacc[c];
                     }
-                    work_bar();   // last_flag is reused by the next segment
+                    work_bar<SPLIT>();   // last_flag is reused by the next segment
                 }
             }
         }
