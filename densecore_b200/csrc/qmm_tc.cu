@@ -100,10 +100,11 @@ struct TcCfg {
     // plane buffers: two (units alternate, so the prep of unit i+1 need not wait for unit i's
     // MMAs) where shared memory allows, else one
     // TA: the planes live in tensor memory (A operand read from TMEM), for N <= 64, where they fit
-    // beside the accumulators: columns [0, 4N) accumulators, [256 + 128 pb + 64 h, +32) H and
-    // [+32, +64) L of plane buffer pb, K half h.  Otherwise in shared memory.
+    // beside the accumulators: columns [0, 4N) accumulators, [TMEM_PL + 128 pb + 64 h, +32) H and
+    // [+32, +64) L of plane buffer pb, K half h (three buffers for N <= 32, two for N = 64).
+    // Otherwise in shared memory.
     static constexpr bool TA = N <= 64;
-    static constexpr int PB = (TA || N <= 32) ? 2 : 1;
+    static constexpr int PB = TA ? (N <= 32 ? 3 : 2) : (N <= 32 ? 2 : 1);
     static constexpr int OFF_PL = 1024;                            // planes [buffer][K half][H, L]
     static constexpr int OFF_ACT = OFF_PL + (TA ? 0 : PB * 4 * TC_HPLANE);
     static constexpr int OFF_META = OFF_ACT + AS * AT;
@@ -113,7 +114,7 @@ struct TcCfg {
     static constexpr int WS = WS_FIT > 8 ? 8 : WS_FIT;             // weight ring
     static constexpr int SMEM = OFF_RAW + WS * WT;
     static constexpr int TMEM_COLS = TA ? 512 : 4 * N;             // [2 buffers][C_H, C_L] x N (+ planes)
-    static constexpr int TMEM_PL = 256;
+    static constexpr int TMEM_PL = 512 - PB * 128;                // first plane column (TA)
     static_assert(WS >= 2, "weight ring too shallow");
     static_assert(SMEM <= TC_SMEM_MAX, "shared memory");
 };
