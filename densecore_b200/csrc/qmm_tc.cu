@@ -103,17 +103,22 @@ struct TcCfg {
     // beside the accumulators: columns [0, 4N) accumulators, [TMEM_PL + 128 pb + 64 h, +32) H and
     // [+32, +64) L of plane buffer pb, K half h (three buffers for N <= 32, two for N = 64).
     // Otherwise in shared memory.
-    static constexpr bool TA = N <= 64;
-    static constexpr int PB = TA ? (N <= 32 ? 3 : 2) : (N <= 32 ? 2 : 1);
+    // SB8 (Q4_K, N <= 32): one unscaled plane (the 4-bit quants as int8) in shared memory and one
+    // MMA per sub-block into its own accumulator region, [2 buffers][8 sub-blocks] x N columns; the
+    // drain applies the 6-bit scales as integers.  Half the MMAs of the two-plane form.
+    static constexpr bool SB8 = TYPE == DCG_TYPE_Q4_K && N <= 32;
+    static constexpr bool TA = !SB8 && N <= 64;
+    static constexpr int PB = SB8 ? 2 : (TA ? (N <= 32 ? 3 : 2) : (N <= 32 ? 2 : 1));
     static constexpr int OFF_PL = 1024;                            // planes [buffer][K half][H, L]
-    static constexpr int OFF_ACT = OFF_PL + (TA ? 0 : PB * 4 * TC_HPLANE);
+    static constexpr int PL_BYTES = SB8 ? PB * 2 * TC_HPLANE : (TA ? 0 : PB * 4 * TC_HPLANE);
+    static constexpr int OFF_ACT = OFF_PL + PL_BYTES;
     static constexpr int OFF_META = OFF_ACT + AS * AT;
     static constexpr int OFF_ROWP = OFF_META + TC_MS * META;       // [slot][128 rows] 16 B
     static constexpr int OFF_RAW = OFF_ROWP + TC_MS * TC_ROWS * 16;
     static constexpr int WS_FIT = (TC_SMEM_MAX - OFF_RAW) / WT;
     static constexpr int WS = WS_FIT > 8 ? 8 : WS_FIT;             // weight ring
     static constexpr int SMEM = OFF_RAW + WS * WT;
-    static constexpr int TMEM_COLS = TA ? 512 : 4 * N;             // [2 buffers][C_H, C_L] x N (+ planes)
+    static constexpr int TMEM_COLS = SB8 ? 16 * N : (TA ? 512 : 4 * N);   // accumulators (+ planes)
     static constexpr int TMEM_PL = 512 - PB * 128;                // first plane column (TA)
     static_assert(WS >= 2, "weight ring too shallow");
     static_assert(SMEM <= TC_SMEM_MAX, "shared memory");
@@ -249,24 +254,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < WS; s++) {
             mbar_init(&w_full[s], 1);
-            mbar_init(&w_empty[s], C::TA ? TC_WORKERS / 2 : TC_WORKERS);
+            mbar_init(&w_empty[s], (C::TA || C::SB8) ? TC_WORKERS / 2 : TC_WORKERS);
         }
         for (int s = 0; s < AS; s++) {
             mbar_init(&a_full[s], 1);
             mbar_init(&a_empty[s], 1);
         }
         for (int b = 0; b < 2 * C::PB; b++) {
-            mbar_init(&pl_full[b], C::TA ? 128 : 256);
+            mbar_init(&pl_full[b], (C::TA || C::SB8) ? 128 : 256);
             mbar_init(&pl_empty[b], 1);
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], C::TA ? TC_WORKERS / 2 : TC_WORKERS);
+            mbar_init(&acc_empty[b], (C::TA || C::SB8) ? TC_WORKERS / 2 : TC_WORKERS);
         }
         for (int s = 0; s < MS; s++) {
             mbar_init(&meta_full[s], 32);
             mbar_init(&row_full[s], 128);
-            mbar_init(&meta_empty[s], C::TA ? TC_WORKERS / 2 : TC_WORKERS);
+            mbar_init(&meta_empty[s], (C::TA || C::SB8) ? TC_WORKERS / 2 : TC_WORKERS);
         }
         mbar_init(mma_done, 1);
         fence_mbar_init();
@@ -345,13 +350,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 TC_TRACE(i, 4);
                 const uint32_t pa = smem_u32(act + (size_t)st * C::AT);
                 const uint32_t dH = tmem + (uint32_t)(b * 2 * N), dL = dH + N;
+                const uint32_t dS = tmem + (uint32_t)(b * 8 * N);   // SB8: sub-block regions
 #pragma unroll
                 for (int h = 0; h < 2; h++) {
                     const int pb = i % C::PB;
                     ok = ok && mbar_wait(&pl_full[pb * 2 + h], (uint32_t)((i / C::PB) & 1), &g_tc_error);
                     if (!ok) break;
+                    TC_TRACE(i, 8 + h);
                     tc_fence_after();
-                    if (C::TA) {
+                    if (C::SB8) {
+                        const uint32_t pQ = smem_u32(planes + (size_t)(pb * 2 + h) * TC_HPLANE);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {   // sub-block 4h + j: K chunks 8h + 2j, 8h + 2j + 1
+                            const uint64_t bd = umma_desc(pa + (h * 4 + j) * 2 * N * 16, N * 16, 128);
+                            mma_i8(dS + (uint32_t)((h * 4 + j) * N), umma_desc(pQ + j * 256, 128, TC_HSBO), bd, idesc, 0u);
+                        }
+                    } else if (C::TA) {
                         const uint32_t tH = tmem + (uint32_t)(C::TMEM_PL + pb * 128 + h * 64), tL = tH + 32;
 #pragma unroll
                         for (int j = 0; j < 4; j++) {   // k-step: K elements 32j .. +31 of the half
@@ -389,8 +403,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // quarters) and warps 12-19 only drain (thread = row x half of the columns), so the prep of
         // unit i+1 overlaps the drain of unit i instead of following it.  Otherwise each of the 16
         // warps does both, for a K quarter and a quarter of the columns.
-        constexpr bool SPLIT = C::TA;
+        constexpr bool SPLIT = C::TA || C::SB8;
         constexpr int NH = SPLIT ? N / 2 : N / 4;      // columns per thread
+        constexpr int SH = C::SB8 ? 0 : 1;             // SB8 prep stores the quants unscaled
         const int quarter = warp & 3, grp = (warp - TC_WORK0) >> 2;   // TMEM lane group, warp group
         const bool do_prep = !SPLIT || grp < 2, do_epi = !SPLIT || grp >= 2;
         const int qp = SPLIT ? (do_prep ? 2 * grp : 0) : grp;   // (first) K quarter this thread expands
@@ -428,14 +443,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if (ok && i >= C::PB)
                     ok = mbar_wait(&pl_empty[pb * 2 + half], (uint32_t)(((i / C::PB) - 1) & 1), &g_tc_error);
                 ok = __all_sync(0xffffffffu, ok);
-                if (warp == TC_WORK0 && lane == 0) TC_TRACE(i, 8);
+                
                 if (ok) {
                     const uint8_t* src = raw + (size_t)st * C::WT + (size_t)row * TcW<TYPE>::ROWB;
                     if (qp == 0) {   // the row's scales of this unit, for the epilogue
                         if (Q4) {
                             const uint4 hdr = *(const uint4*)src;
                             const Q4kScales sc = q4k_unpack(hdr);
-                            rowp[ms * TC_ROWS + row] = make_uint4(hdr.x, sc.mn03, sc.mn47, 0u);
+                            rowp[ms * TC_ROWS + row] = C::SB8 ? hdr : make_uint4(hdr.x, sc.mn03, sc.mn47, 0u);
                             mbar_arrive(&row_full[ms]);
                         } else if (i + 2 < nu) {   // the slot of unit i + 2 held unit i - 2
                             const int m2 = (i + 2) % MS;
@@ -459,15 +474,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         }
                         tmem_wait_st();
                         tc_fence_before();
+                    } else if (C::SB8) {
+                        // quants as int8 (no scale), K half `half` of plane buffer pb
+                        uint8_t* pQ = planes + (size_t)(pb * 2 + half) * TC_HPLANE + (size_t)(row >> 3) * TC_HSBO + (row & 7) * 16;
+#pragma unroll
+                        for (int q2 = 0; q2 < 2; q2++) {
+                            const int p4 = qp + q2;   // quarter: sub-blocks 2 p4 (low nibbles), 2 p4 + 1 (high)
+                            const uint4 g0 = *(const uint4*)(src + 16 + 32 * p4), g1 = *(const uint4*)(src + 32 + 32 * p4);
+                            const int j0 = 4 * (p4 & 1);
+                            const uint32_t m4 = 0x0F0F0F0Fu;
+                            *(uint4*)(pQ + (j0 + 0) * 128) = make_uint4(g0.x & m4, g0.y & m4, g0.z & m4, g0.w & m4);
+                            *(uint4*)(pQ + (j0 + 1) * 128) = make_uint4(g1.x & m4, g1.y & m4, g1.z & m4, g1.w & m4);
+                            *(uint4*)(pQ + (j0 + 2) * 128) = make_uint4((g0.x >> 4) & m4, (g0.y >> 4) & m4, (g0.z >> 4) & m4, (g0.w >> 4) & m4);
+                            *(uint4*)(pQ + (j0 + 3) * 128) = make_uint4((g1.x >> 4) & m4, (g1.y >> 4) & m4, (g1.z >> 4) & m4, (g1.w >> 4) & m4);
+                        }
                     } else {
                         prep_quarter<TYPE>(src, qp, hv, lv);
                         uint8_t* pH = planes + (size_t)(pb * 4 + 2 * half) * TC_HPLANE + (size_t)(row >> 3) * TC_HSBO + (row & 7) * 16;
                         planes_store(hv, lv, qp, pH, pH + TC_HPLANE);
                     }
-                    if (warp == TC_WORK0 && lane == 0) TC_TRACE(i, 9);
+                    
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&w_empty[st]);
-                    if (!C::TA) fence_proxy_async_smem();
+                    if (!C::TA) fence_proxy_async_smem();   // generic-proxy plane stores -> the MMA's reads
                     mbar_arrive(&pl_full[pb * 2 + half]);
                     if (warp == TC_WORK0 && lane == 0) TC_TRACE(i, 3);
                 }
@@ -492,62 +521,101 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if (warp == TC_WORK0 + (SPLIT ? 8 : 0) && lane == 0) TC_TRACE(e, 10);
             if (ok) {
                 tc_fence_after();
-                const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 2 * N + cq * NH);
-                const uint4 rp = rowp[ms * TC_ROWS + row];
-                const float* mdx = (const float*)(meta + (size_t)ms * C::META) + cq * NH;
-                const uint4* mbs = (const uint4*)((const float*)(meta + (size_t)ms * C::META) + N) + cq * NH;
-                float2 dd = make_float2(0.0f, 0.0f);
-                if (!Q4) {   // the fetched pair of halves; this unit's d is the one at an odd index or not
-                    const int64_t r = (tile / ct_tiles) * TC_ROWS + row;
-                    const __half2 pr = *reinterpret_cast<const __half2*>(&rp.x);
-                    dd.x = ((r * nb + s) & 1) ? __high2float(pr) : __low2float(pr);
-                }
-                int mp0 = 0, mp1 = 0, mp2 = 0, mp3 = 0;
-                if (Q4) {
-                    dd = __half22float2(*reinterpret_cast<const __half2*>(&rp.x));
-                    // mins as (m0, m1), (m2, m3), ... pairs in the low bytes for dp2a
-                    mp0 = (int)(rp.y & 0xFFu) | (int)((rp.y >> 8) & 0xFFu) << 8;
-                    mp1 = (int)((rp.y >> 16) & 0xFFu) | (int)(rp.y >> 24) << 8;
-                    mp2 = (int)(rp.z & 0xFFu) | (int)((rp.z >> 8) & 0xFFu) << 8;
-                    mp3 = (int)((rp.z >> 16) & 0xFFu) | (int)(rp.z >> 24) << 8;
-                }
-                constexpr int CH = NH < 16 ? NH : 16;
+                if constexpr (C::SB8) {
+                    // sub-block j's int32 dots C_j: isum = sum_j sc_j C_j exactly (ggml's integer sum)
+                    const uint4 hdr = rowp[ms * TC_ROWS + row];
+                    const Q4kScales sc = q4k_unpack(hdr);
+                    const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&hdr.x));
+                    const int mp0 = (int)(sc.mn03 & 0xFFu) | (int)((sc.mn03 >> 8) & 0xFFu) << 8;
+                    const int mp1 = (int)((sc.mn03 >> 16) & 0xFFu) | (int)(sc.mn03 >> 24) << 8;
+                    const int mp2 = (int)(sc.mn47 & 0xFFu) | (int)((sc.mn47 >> 8) & 0xFFu) << 8;
+                    const int mp3 = (int)((sc.mn47 >> 16) & 0xFFu) | (int)(sc.mn47 >> 24) << 8;
+                    const float* mdx = (const float*)(meta + (size_t)ms * C::META) + cq * NH;
+                    const uint4* mbs = (const uint4*)((const float*)(meta + (size_t)ms * C::META) + N) + cq * NH;
+                    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 8 * N + cq * NH);
+                    int isum[NH];
 #pragma unroll
-                for (int cc = 0; cc < NH; cc += CH) {
-                    uint32_t hv[16], lv[16];
-                    if (CH == 16) {
-                        tmem_ld16(lane_addr + cc, hv);
-                        tmem_ld16(lane_addr + N + cc, lv);
-                    } else if (CH == 8) {
-                        tmem_ld8(lane_addr + cc, hv);
-                        tmem_ld8(lane_addr + N + cc, lv);
-                    } else {
-                        tmem_ld4(lane_addr + cc, hv);
-                        tmem_ld4(lane_addr + N + cc, lv);
-                    }
-                    tmem_wait_ld();
-                    if (cc == 0 && warp == TC_WORK0 + (SPLIT ? 8 : 0) && lane == 0) TC_TRACE(e, 11);
-                    if (cc + CH == NH) {   // every read of this buffer issued and complete
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&acc_empty[b]);
-                    }
+                    for (int c = 0; c < NH; c++) isum[c] = 0;
 #pragma unroll
-                    for (int j = 0; j < CH; j++) {
-                        const float dx = mdx[cc + j];   // 0 for columns past m
-                        // isum = SHIFT C_H + C_L as one correctly rounded fp32 value (what
-                        // (float)isum gives), from exact conversions of |C_H|, |C_L| < 2^22
-                        const float fsum = fmaf(i2f_exact22((int)hv[j]), (float)TcW<TYPE>::SHIFT,
-                                                i2f_exact22((int)lv[j]));
-                        if (Q4) {
-                            const uint4 bs = mbs[cc + j];
-                            int msum = __dp2a_lo((int)bs.x, mp0, 0);
-                            msum = __dp2a_lo((int)bs.y, mp1, msum);
-                            msum = __dp2a_lo((int)bs.z, mp2, msum);
-                            msum = __dp2a_lo((int)bs.w, mp3, msum);
-                            yacc[cc + j] += dx * (dd.x * fsum - dd.y * i2f_exact22(msum));
+                    for (int j = 0; j < 8; j++) {
+                        const int scj = (int)(((j < 4 ? sc.sc03 : sc.sc47) >> (8 * (j & 3))) & 0xFFu);
+                        uint32_t v[16];
+                        if (NH == 16) tmem_ld16(lane_addr + (uint32_t)(j * N), v);
+                        else tmem_ld8(lane_addr + (uint32_t)(j * N), v);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int c = 0; c < NH; c++) isum[c] += scj * (int)v[c];
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[b]);
+#pragma unroll
+                    for (int c = 0; c < NH; c++) {
+                        const uint4 bs = mbs[c];
+                        int msum = __dp2a_lo((int)bs.x, mp0, 0);
+                        msum = __dp2a_lo((int)bs.y, mp1, msum);
+                        msum = __dp2a_lo((int)bs.z, mp2, msum);
+                        msum = __dp2a_lo((int)bs.w, mp3, msum);
+                        yacc[c] += mdx[c] * (dd.x * __int2float_rn(isum[c]) - dd.y * i2f_exact22(msum));
+                    }
+                } else {
+                    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 2 * N + cq * NH);
+                    const uint4 rp = rowp[ms * TC_ROWS + row];
+                    const float* mdx = (const float*)(meta + (size_t)ms * C::META) + cq * NH;
+                    const uint4* mbs = (const uint4*)((const float*)(meta + (size_t)ms * C::META) + N) + cq * NH;
+                    float2 dd = make_float2(0.0f, 0.0f);
+                    if (!Q4) {   // the fetched pair of halves; this unit's d is the one at an odd index or not
+                        const int64_t r = (tile / ct_tiles) * TC_ROWS + row;
+                        const __half2 pr = *reinterpret_cast<const __half2*>(&rp.x);
+                        dd.x = ((r * nb + s) & 1) ? __high2float(pr) : __low2float(pr);
+                    }
+                    int mp0 = 0, mp1 = 0, mp2 = 0, mp3 = 0;
+                    if (Q4) {
+                        dd = __half22float2(*reinterpret_cast<const __half2*>(&rp.x));
+                        // mins as (m0, m1), (m2, m3), ... pairs in the low bytes for dp2a
+                        mp0 = (int)(rp.y & 0xFFu) | (int)((rp.y >> 8) & 0xFFu) << 8;
+                        mp1 = (int)((rp.y >> 16) & 0xFFu) | (int)(rp.y >> 24) << 8;
+                        mp2 = (int)(rp.z & 0xFFu) | (int)((rp.z >> 8) & 0xFFu) << 8;
+                        mp3 = (int)((rp.z >> 16) & 0xFFu) | (int)(rp.z >> 24) << 8;
+                    }
+                    constexpr int CH = NH < 16 ? NH : 16;
+    #pragma unroll
+                    for (int cc = 0; cc < NH; cc += CH) {
+                        uint32_t hv[16], lv[16];
+                        if (CH == 16) {
+                            tmem_ld16(lane_addr + cc, hv);
+                            tmem_ld16(lane_addr + N + cc, lv);
+                        } else if (CH == 8) {
+                            tmem_ld8(lane_addr + cc, hv);
+                            tmem_ld8(lane_addr + N + cc, lv);
                         } else {
-                            yacc[cc + j] += dx * (dd.x * fsum);
+                            tmem_ld4(lane_addr + cc, hv);
+                            tmem_ld4(lane_addr + N + cc, lv);
+                        }
+                        tmem_wait_ld();
+                        if (cc == 0 && warp == TC_WORK0 + (SPLIT ? 8 : 0) && lane == 0) TC_TRACE(e, 11);
+                        if (cc + CH == NH) {   // every read of this buffer issued and complete
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&acc_empty[b]);
+                        }
+    #pragma unroll
+                        for (int j = 0; j < CH; j++) {
+                            const float dx = mdx[cc + j];   // 0 for columns past m
+                            // isum = SHIFT C_H + C_L as one correctly rounded fp32 value (what
+                            // (float)isum gives), from exact conversions of |C_H|, |C_L| < 2^22
+                            const float fsum = fmaf(i2f_exact22((int)hv[j]), (float)TcW<TYPE>::SHIFT,
+                                                    i2f_exact22((int)lv[j]));
+                            if (Q4) {
+                                const uint4 bs = mbs[cc + j];
+                                int msum = __dp2a_lo((int)bs.x, mp0, 0);
+                                msum = __dp2a_lo((int)bs.y, mp1, msum);
+                                msum = __dp2a_lo((int)bs.z, mp2, msum);
+                                msum = __dp2a_lo((int)bs.w, mp3, msum);
+                                yacc[cc + j] += dx * (dd.x * fsum - dd.y * i2f_exact22(msum));
+                            } else {
+                                yacc[cc + j] += dx * (dd.x * fsum);
+                            }
                         }
                     }
                 }
