@@ -313,8 +313,14 @@ __global__ void __launch_bounds__(QMM_THREADS, NT >= 4 ? 1 : (NT >= 2 ? 2 : 3))
 // ------------------------------------------------------------------------------------------
 constexpr int M1_WARPS = 4;        // consumer warps; warp 4 only issues the copies
 constexpr int M1_THREADS = 160;
-constexpr int M1_SROW = Q4_K_BYTES;                // 144 B: rows gid, gid+1 hit disjoint banks
-constexpr int M1_STAGE = QMM_ROWS * M1_SROW;       // one super-block of 64 rows
+// super-blocks per ring stage: one 2-D box of 64 rows x M1_SBS super-blocks (wider boxes move more
+// bytes per row segment; 144-B rows, M1_SBS = 1, keep the consumer's loads free of bank conflicts)
+#ifndef DCG_M1_SBS
+#define DCG_M1_SBS 1
+#endif
+constexpr int M1_SBS = DCG_M1_SBS;
+constexpr int M1_SROW = Q4_K_BYTES * M1_SBS;       // smem row stride of a stage
+constexpr int M1_STAGE = QMM_ROWS * M1_SROW;       // M1_SBS super-blocks of 64 rows
 constexpr int M1_HDR = 512;                        // barriers | zero pad | 64 row partials
 constexpr int M1_XQ = QK_K + 16 + 4;               // per super-block: quants, pair sums, d
 constexpr int M1_MAX_SPS = 32;                     // activation slice: at most 32 super-blocks
@@ -348,7 +354,8 @@ __global__ void __launch_bounds__(M1_THREADS, M1_CTAS)
     const int gid = lane >> 2, tig = lane & 3;
     const int64_t r0 = (int64_t)blockIdx.x * QMM_ROWS;
     const int sb0 = blockIdx.z * sps, sb1 = min(nb, sb0 + sps);
-    const int nchunks = sb1 - sb0;
+    const int nchunks = sb1 - sb0;                 // super-blocks of this split
+    const int nst = (nchunks + M1_SBS - 1) / M1_SBS;   // ring stages
 
     if (threadIdx.x < 16) ((uint32_t*)zpad)[threadIdx.x] = 0u;
     if (threadIdx.x < QMM_ROWS) ypart[threadIdx.x] = 0.0f;
@@ -362,12 +369,12 @@ __global__ void __launch_bounds__(M1_THREADS, M1_CTAS)
     __syncthreads();
 
     // producer lane: the first ring fill, then all warps stage the activation slice
-    const int pre = min(M1_STAGES, nchunks);
+    const int pre = min(M1_STAGES, nst);
     auto issue = [&](int c) {
         const int st = c % M1_STAGES;
         mbar_arrive_expect_tx(&full[st], (uint32_t)M1_STAGE);
         fence_proxy_async_smem();
-        tma_load_2d(ring + (size_t)st * M1_STAGE, &wmap, (sb0 + c) * (Q4_K_BYTES / 4), (int)r0, &full[st]);
+        tma_load_2d(ring + (size_t)st * M1_STAGE, &wmap, (sb0 + c * M1_SBS) * (Q4_K_BYTES / 4), (int)r0, &full[st]);
     };
     if (warp == M1_WARPS && lane == 0)
         for (int c = 0; c < pre; c++) issue(c);
@@ -405,7 +412,7 @@ __global__ void __launch_bounds__(M1_THREADS, M1_CTAS)
     bool ok = true;
     if (warp == M1_WARPS) {  // producer: keep the ring full
         if (lane == 0) {
-            for (int c = pre; c < nchunks && ok; c++) {
+            for (int c = pre; c < nst && ok; c++) {
                 ok = mbar_wait(&empty[c % M1_STAGES], (uint32_t)(((c / M1_STAGES) - 1) & 1), &g_qmm_error);
                 if (ok) issue(c);
             }
@@ -414,12 +421,16 @@ __global__ void __launch_bounds__(M1_THREADS, M1_CTAS)
         const bool active = (gid >> 1) == tig;  // feeds column gid (sub-block gid) of every mma
         const bool odd = gid & 1;                // ... through b1 (odd sub-block) or b0 (even)
         float yA = 0.0f, yB = 0.0f;
-        for (int c = 0; c < nchunks; c++) {
-            const float dx = xd[c];
+        for (int c = 0; c < nst; c++) {
             ok = mbar_wait(&full[c % M1_STAGES], (uint32_t)((c / M1_STAGES) & 1), &g_qmm_error);
             if (!ok) break;
             const uint8_t* stage = ring + (size_t)(c % M1_STAGES) * M1_STAGE;
-            const uint8_t* rowA = stage + (warp * 16 + gid) * M1_SROW;
+#pragma unroll
+          for (int jj = 0; jj < M1_SBS; jj++) {
+            const int cs = c * M1_SBS + jj;        // super-block within the split
+            if (cs >= nchunks) break;
+            const float dx = xd[cs];
+            const uint8_t* rowA = stage + (warp * 16 + gid) * M1_SROW + jj * Q4_K_BYTES;
             const uint8_t* rowB = rowA + 8 * M1_SROW;
             const uint4 hA = *(const uint4*)rowA, hB = *(const uint4*)rowB;
             // weight words: pair group tig, elements 4i..4i+3 (i = 0..7) of rows gid / gid+8
@@ -428,7 +439,7 @@ __global__ void __launch_bounds__(M1_THREADS, M1_CTAS)
             const uint32_t wa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
             const uint32_t wb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
             // activation words of sub-block gid (active lanes) or zeros
-            const uint8_t* xsrc = active ? (const uint8_t*)xqs + c * QK_K + 32 * gid : zpad;
+            const uint8_t* xsrc = active ? (const uint8_t*)xqs + cs * QK_K + 32 * gid : zpad;
             const uint4 x0 = *(const uint4*)xsrc, x1 = *(const uint4*)(xsrc + 16);
             const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
             int acc[4] = {0, 0, 0, 0};
@@ -447,12 +458,13 @@ __global__ void __launch_bounds__(M1_THREADS, M1_CTAS)
             const uint32_t mnB = ((tig < 2 ? sB.mn03 : sB.mn47) >> sh) & 0xFFFFu;
             const int isA = (int)(scA & 0xFF) * acc[0] + (int)(scA >> 8) * acc[1];
             const int isB = (int)(scB & 0xFF) * acc[2] + (int)(scB >> 8) * acc[3];
-            const int bsp = *(const int*)(xbs + c * 8 + 2 * tig);  // pair sums of sub-blocks 2tig, 2tig+1
+            const int bsp = *(const int*)(xbs + cs * 8 + 2 * tig);  // pair sums of sub-blocks 2tig, 2tig+1
             const int msA = __dp2a_lo(bsp, (int)mnA, 0), msB = __dp2a_lo(bsp, (int)mnB, 0);
             const float2 dA = __half22float2(*reinterpret_cast<const __half2*>(&hA.x));
             const float2 dB = __half22float2(*reinterpret_cast<const __half2*>(&hB.x));
             yA += dx * (dA.x * (float)isA - dA.y * (float)msA);
             yB += dx * (dB.x * (float)isB - dB.y * (float)msB);
+          }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[c % M1_STAGES]);
         }
@@ -566,6 +578,8 @@ static bool m1_plan(int64_t n, int64_t k, int* rb, int* S, int* sps) {
     s = std::max(s, (nb + M1_MAX_SPS - 1) / M1_MAX_SPS);
     if (s > M1_MAX_CLUSTER) return false;
     *sps = (nb + s - 1) / s;
+    *sps = (*sps + M1_SBS - 1) / M1_SBS * M1_SBS;   // splits start on a stage boundary
+    if (*sps > M1_MAX_SPS) return false;
     *S = (nb + *sps - 1) / *sps;
     return true;
 }
@@ -580,7 +594,7 @@ static cudaError_t launch_q4k_m1(const uint8_t* W, int64_t n, int64_t k, const A
     if (e != cudaSuccess) return e;
     const int nb = (int)(k / QK_K);
     CUtensorMap wmap;
-    e = make_wmap(&wmap, W, n, (size_t)nb * Q4_K_BYTES, 1);
+    e = make_wmap(&wmap, W, n, (size_t)nb * Q4_K_BYTES, M1_SBS);
     if (e != cudaSuccess) return e;
     // A programmatic dependent whose own dependents are released only at its exit (after the
     // cluster reduction).  Released earlier, the next grid's clusters landed in a GPU still
