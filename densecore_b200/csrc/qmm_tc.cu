@@ -405,7 +405,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // warps does both, for a K quarter and a quarter of the columns.
         constexpr bool SPLIT = C::TA || C::SB8;
         constexpr int NH = SPLIT ? N / 2 : N / 4;      // columns per thread
-        constexpr int SH = C::SB8 ? 0 : 1;             // SB8 prep stores the quants unscaled
         const int quarter = warp & 3, grp = (warp - TC_WORK0) >> 2;   // TMEM lane group, warp group
         const bool do_prep = !SPLIT || grp < 2, do_epi = !SPLIT || grp >= 2;
         const int qp = SPLIT ? (do_prep ? 2 * grp : 0) : grp;   // (first) K quarter this thread expands
