@@ -643,12 +643,16 @@ def profile_case(args):
     torch.cuda.set_device(0)
     qtype = {"q4k": Q4_K, "q8_0": 8, "q6k": 14}[args.profile_type]
     n, k = {"up": SHAPES[0], "down": SHAPES[1], "sq": (4096, 4096)}[args.profile_shape]
+    if args.profile_nk:
+        n, k = (int(v) for v in args.profile_nk.split(","))
     m = args.profile_m
-    w = ops.QuantWeight.from_float(torch.randn((n, k), device="cuda") * 0.02, qtype)
+    w0 = ops.QuantWeight.from_float(torch.randn((n, k), device="cuda") * 0.02, qtype)
+    # a ring of copies, so a launch late in the run reads its weight from DRAM, not L2
+    ws = [w0] + [ops.QuantWeight(qtype, n, k, w0.packed.clone()) for _ in range(args.profile_ring - 1)]
     x = torch.randn((m, k), device="cuda")
     y = torch.empty((m, n), device="cuda")
-    for _ in range(args.profile_iters):
-        ops.mul_mat(w, x, out=y)
+    for i in range(args.profile_iters):
+        ops.mul_mat(ws[i % len(ws)], x, out=y)
     torch.cuda.synchronize()
     print("profile case done", qtype, n, k, m)
 
@@ -752,6 +756,8 @@ def main():
                     help="run only a small eager GEMV case (for ncu) and exit")
     ap.add_argument("--profile-shape", default="up", choices=["up", "down", "sq"])
     ap.add_argument("--profile-m", type=int, default=1)
+    ap.add_argument("--profile-nk", default=None, help="profiling: weight shape n,k instead of --profile-shape")
+    ap.add_argument("--profile-ring", type=int, default=1, help="profiling: distinct copies of the weight")
     ap.add_argument("--profile-iters", type=int, default=6)
     ap.add_argument("--copy-ceiling", action="store_true",
                     help="only time plain device copies at the mat-vec sizes and exit")
