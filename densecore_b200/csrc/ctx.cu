@@ -25,7 +25,8 @@ struct dcg_ctx {
     std::unordered_map<const void*, dcg_weight*> by_host;
     void* scratch = nullptr;  // device: [activation f32 | quantized activation | output f32]
     size_t scratch_cap = 0;
-    void* pinned = nullptr;  // host staging, same layout as the f32 parts
+    void* pinned = nullptr;  // host staging, same layout as the f32 parts (mapped into the device)
+    void* pinned_dev = nullptr;  // its device address
     size_t pinned_cap = 0;
 };
 
@@ -72,7 +73,13 @@ int grow(dcg_ctx* c, size_t dev_bytes, size_t host_bytes) {
         if (c->pinned) cudaFreeHost(c->pinned);
         c->pinned = nullptr;
         c->pinned_cap = 0;
-        CTX_CUDA(cudaMallocHost(&c->pinned, host_bytes), "cudaMallocHost(staging)");
+        CTX_CUDA(cudaHostAlloc(&c->pinned, host_bytes, cudaHostAllocMapped), "cudaHostAlloc(staging)");
+        const cudaError_t e = cudaHostGetDevicePointer(&c->pinned_dev, c->pinned, 0);
+        if (e != cudaSuccess) {
+            cudaFreeHost(c->pinned);
+            c->pinned = nullptr;
+            return cerr(e, "cudaHostGetDevicePointer(staging)");
+        }
         c->pinned_cap = host_bytes;
     }
     return DCG_OK;
@@ -189,9 +196,13 @@ int dcg_ctx_mul_mat(dcg_ctx* c, dcg_weight* w, const float* x_host, int64_t m, f
     uint8_t* hy = hx + xb;
     memcpy(hx, x_host, (size_t)m * w->k * 4);
     CTX_CUDA(cudaMemcpyAsync(dx, hx, (size_t)m * w->k * 4, cudaMemcpyHostToDevice, c->stream), "H2D");
-    rc = dcg_mul_mat(w->type, w->dev, w->n, w->k, (const float*)dx, m, (float*)dy, dq, qb, c->stream);
+    // m = 1: the kernel writes y straight into the mapped staging buffer (one row of posted PCIe
+    // writes), so no device-to-host copy follows; larger m go through device memory and a copy
+    float* ydst = m == 1 ? (float*)((uint8_t*)c->pinned_dev + xb) : (float*)dy;
+    rc = dcg_mul_mat(w->type, w->dev, w->n, w->k, (const float*)dx, m, ydst, dq, qb, c->stream);
     if (rc) return rc;
-    CTX_CUDA(cudaMemcpyAsync(hy, dy, (size_t)m * w->n * 4, cudaMemcpyDeviceToHost, c->stream), "D2H");
+    if (m != 1)
+        CTX_CUDA(cudaMemcpyAsync(hy, dy, (size_t)m * w->n * 4, cudaMemcpyDeviceToHost, c->stream), "D2H");
     CTX_CUDA(cudaStreamSynchronize(c->stream), "sync");
     memcpy(y_host, hy, (size_t)m * w->n * 4);
     return DCG_OK;

@@ -280,6 +280,7 @@ class HostContext:
         _lib.check(self._L.dcg_ctx_create(device, ctypes.byref(h)), "dcg_ctx_create")
         self.h = h
         self._keep = {}
+        self._mm = self._L.dcg_ctx_mul_mat
 
     def register(self, rows: np.ndarray, qtype: int, k: int):
         rows = np.ascontiguousarray(rows, dtype=np.uint8)
@@ -293,10 +294,15 @@ class HostContext:
 
     def mul_mat(self, w, x: np.ndarray) -> np.ndarray:
         rows, n, k = self._keep[w.value]
-        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, k)
-        y = np.empty((x.shape[0], n), dtype=np.float32)
-        _lib.check(self._L.dcg_ctx_mul_mat(self.h, w, x.ctypes.data, x.shape[0], y.ctypes.data),
-                   "dcg_ctx_mul_mat")
+        if not (x.dtype == np.float32 and x.flags.c_contiguous):
+            x = np.ascontiguousarray(x, dtype=np.float32)
+        m = x.size // k
+        if m * k != x.size:
+            raise ValueError(f"x has {x.size} elements, not a multiple of k={k}")
+        y = np.empty((m, n), dtype=np.float32)
+        rc = self._mm(self.h, w, x.ctypes.data, m, y.ctypes.data)
+        if rc:
+            _lib.check(rc, "dcg_ctx_mul_mat")
         return y
 
     def close(self):
