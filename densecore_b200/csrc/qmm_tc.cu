@@ -18,15 +18,20 @@
 //               columns' scales dx (and the Q4_K min-term pair sums) in a metadata ring
 //   warp 2      one thread issues per K half 4 k-steps x 2 planes of M128 x N x K32 MMAs into
 //               C_H, C_L (double-buffered across units) and releases stages with tcgen05.commit
-//   warps 4-19  thread (row r, quarter p) first expands K quarter p of weight row r of unit i into
-//               two int8 planes H, L with q * scale = SHIFT * H + L exactly, in the core-matrix layout:
+//   warps 4-19  expand unit i's weights and drain unit i-1's accumulators (tcgen05.ld), in one of
+//               three forms (TcCfg):
+//     SB8 (Q4_K, N <= 32)  one plane of the unscaled 4-bit quants as int8 in shared memory, one
+//               MMA per 32-element sub-block into its own accumulator region; the drain forms
+//               isum = sum_j sc_j C_j in integers, y += dx (d isum - dmin sum_j m_j bsum32_j)
+//     TA (Q4_K N = 64, Q6_K N <= 64)  two int8 planes with q * scale = SHIFT * H + L exactly,
+//               stored into tensor memory (tcgen05.st) and read there by the MMAs:
 //                 Q4_K  sc = 8 sh + sl (sh, sl <= 7): H = q sh, L = q sl (q <= 15), SHIFT = 8
 //                 Q6_K  p = (u - 32) sc (u the unsigned 6-bit quant, sc the signed 8-bit sub-block
 //                       scale): H = p >> 7, L = p & 127, SHIFT = 128 (the -32 offset is folded in)
-//               then, while unit i's MMAs run, drains unit i-1's accumulators for quarter p of the
-//               columns (tcgen05.ld), forms isum = SHIFT C_H + C_L and accumulates
-//                 Q4_K  y += dx (d isum - dmin sum_j m_j bsum32_j)      (ggml's order)
-//                 Q6_K  y += dx d isum
+//               the drain forms isum = SHIFT C_H + C_L, y += dx (d isum [- dmin msum])
+//     N = 128 (prefill)  the same two planes in shared memory
+//               In SB8 and TA warps 4-11 only expand and warps 12-19 only drain, so the expansion
+//               of unit i+1 overlaps the drain of unit i; for N = 128 all 16 do both.
 // Every wait is bounded (device error flag); tensor memory is always freed before exit.
 #include <cuda.h>
 #include <cudaTypedefs.h>
