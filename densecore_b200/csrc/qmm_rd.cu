@@ -14,6 +14,8 @@
 // Device weight layout (common.cuh): payload rows + separate fp16 scale array.
 // Split-K: when the row x column blocks cannot fill the GPU, grid.z splits K and the splits of a
 // tile form one thread-block cluster that reduces through distributed shared memory.
+#include <stdlib.h>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "tma.cuh"
@@ -321,7 +323,10 @@ static cudaError_t launch_rd_t(const PackedW& w, int64_t n, int64_t k, const Act
     const int resident = per_sm[dev] * num_sms();
     int S = (resident + rb * cb - 1) / (rb * cb);
     S = S < 1 ? 1 : (S > 8 ? 8 : S);
-    const int min_sps = TYPE == DCG_TYPE_Q8_0 ? 4 : 2;   // below this a split costs more than it gains
+    // below min_sps super-blocks per split a split costs more than it gains (DCG_RD_MIN_SPS
+    // overrides it, for tuning)
+    static const int min_sps_env = getenv("DCG_RD_MIN_SPS") ? atoi(getenv("DCG_RD_MIN_SPS")) : 0;
+    const int min_sps = min_sps_env > 0 ? min_sps_env : (TYPE == DCG_TYPE_Q8_0 ? 4 : 2);
     S = S > nsb / min_sps ? (nsb / min_sps > 0 ? nsb / min_sps : 1) : S;
     const int sps = (nsb + S - 1) / S;
     S = (nsb + sps - 1) / sps;
