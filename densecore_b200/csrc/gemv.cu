@@ -414,8 +414,6 @@ constexpr int XR_CTAS = 3;
 template <int TYPE, int M, int UW>
 __global__ void __launch_bounds__(256, (UW <= 4 ? XR_CTAS : 2)) gemv_tma_xr_kernel(PackedW w, int64_t n, int64_t k, ActQ a,
                                                              int m0, float* __restrict__ y, int TR) {
-    pdl_wait();
-    pdl_trigger();
     constexpr int PER = UnitInfo<TYPE>::BLOCKS;
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = (uint64_t*)smem;
@@ -446,6 +444,9 @@ __global__ void __launch_bounds__(256, (UW <= 4 ? XR_CTAS : 2)) gemv_tma_xr_kern
     };
     if (threadIdx.x == 0)
         for (int i = 0; i < XR_STAGES - 1 && i < my_tiles; i++) issue(i);
+    // the weight tiles are constant: requested before the wait on the kernel producing the activation
+    pdl_wait();
+    pdl_trigger();
 
     // this lane's activation slice, once (overlaps the first bulk copies)
     XReg xr[UW][M];
