@@ -128,7 +128,6 @@ template <int NT>
 __global__ void __launch_bounds__(RD_WARPS * 32) qmm_q8_0_rd_kernel(PackedW w, int64_t n, int64_t k,
                                                                    ActQ a, int m, float* __restrict__ y,
                                                                    int sps) {
-    pdl_wait();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int gid = lane >> 2, tig = lane & 3;
     const int64_t rowA = ((int64_t)blockIdx.x * RD_WARPS + warp) * 16 + gid, rowB = rowA + 8;
@@ -152,12 +151,14 @@ __global__ void __launch_bounds__(RD_WARPS * 32) qmm_q8_0_rd_kernel(PackedW w, i
     const bool live = rowA - gid < n;
 
     if (!live) {   // rows past n: no loads, but the warp still takes part in the split reduction
+        pdl_wait();
         rd_store<NT>(acc, red, y, n, m, (int64_t)blockIdx.x * RD_WARPS * 16, c0, warp, gid, tig, false);
         pdl_trigger();
         return;
     }
     Q80Frag cur, nxt;
     q80_load(cur, w, rowA, rowB, n, 0, tig);
+    pdl_wait();   // the first weight fragments (constant) are already in flight
     for (int sb = 0; sb < nsb; sb++) {
         if (sb + 1 < nsb) q80_load(nxt, w, rowA, rowB, n, sb + 1, tig);
 #pragma unroll
@@ -239,7 +240,6 @@ template <int NT>
 __global__ void __launch_bounds__(RD_WARPS * 32) qmm_q6k_rd_kernel(PackedW w, int64_t n, int64_t k,
                                                                   ActQ a, int m, float* __restrict__ y,
                                                                    int sps) {
-    pdl_wait();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int gid = lane >> 2, tig = lane & 3;
     const int64_t rowA = ((int64_t)blockIdx.x * RD_WARPS + warp) * 16 + gid, rowB = rowA + 8;
@@ -261,12 +261,14 @@ __global__ void __launch_bounds__(RD_WARPS * 32) qmm_q6k_rd_kernel(PackedW w, in
     const bool live = rowA - gid < n;
 
     if (!live) {   // rows past n: no loads, but the warp still takes part in the split reduction
+        pdl_wait();
         rd_store<NT>(acc, red, y, n, m, (int64_t)blockIdx.x * RD_WARPS * 16, c0, warp, gid, tig, false);
         pdl_trigger();
         return;
     }
     Q6Frag cur, nxt;
     q6_load(cur, w, rowA, rowB, n, 0, tig);
+    pdl_wait();   // the first weight fragments (constant) are already in flight
     for (int sb = 0; sb < nsb; sb++) {
         if (sb + 1 < nsb) q6_load(nxt, w, rowA, rowB, n, sb + 1, tig);
 #pragma unroll
